@@ -1,0 +1,288 @@
+"""CPU oracle for the NSN packed-KV hot path.
+
+TEST INFRASTRUCTURE ONLY.  This module is a NumPy restatement of the
+reference's arithmetic, used as the checker by ``tests/``, by
+``__graft_entry__.smoke()`` and by the ``cpu_baseline`` leg of ``bench.py``.
+The product (``nsn_b200``) never imports it and never falls back to it.
+
+Parity pin: every function here is checked against golden vectors produced by
+running the reference's own code (``tests/golden/make_golden.py`` imports the
+reference's ``loop_kv_nb06_primitives`` / ``loop_kv_nb06_codec`` and records
+their outputs in ``tests/golden/*.npz``), see ``tests/test_oracle_golden.py``.
+
+Reference files (paths inside the reference project):
+  experiments/nb06/source/loop_kv_nb06_primitives.py  pack_codes :15-24,
+      unpack_codes_reference :26-35, nsn_encode :37-55, nsn_decode :57-66,
+      nsn_qdq :68-70, planned_bytes :72-81
+  experiments/nb06/source/loop_kv_nb06_codec.py  pack3 :6-15, unpack3 :17-26,
+      encode_group :28-34, restore_group :36-38
+  papers/nsn-integrated/code/nsn_int3_core.py  nsn_int3_qdq :11-21
+  experiments/nb06/source/loop_kv_nb06_kernel.py  repeat_kv :156-165, sdpa :169-174
+  experiments/ac08/source/loop_kv_ac08_attention.py  finish :38-44
+
+Rounding facts this restatement depends on (all IEEE binary32 unless noted):
+  * The reference computes ``torch.linalg.vector_norm(a, dim=-1)`` on the CPU.
+    For a row whose 128 elements are contiguous in memory, PyTorch reduces in
+    8 interleaved lanes: lane j accumulates x[j], x[j+8], ..., x[j+120] as
+    ``acc = acc + x*x`` (a rounded multiply, then a rounded add, no fused
+    multiply-add), then the lanes are added in order 0..7 and the square root
+    is taken.  For a row whose elements are strided (e.g. a transposed input)
+    the sum is a plain sequential ``acc = acc + x*x`` over c = 0..127.  Both
+    orders were measured against torch 2.11 (20000 random rows, zero
+    mismatching bits) and are pinned by the golden vectors.
+  * ``torch.round`` rounds half to even (``np.rint``); casts to fp16/bf16
+    round to nearest even.
+"""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+
+BLOCK = 64
+DIM = 128
+EPS = np.float32(1e-12)
+SCALE = 0.08838834764831845  # 1/sqrt(128), loop_kv_vf01_kernel.py:90
+
+# Status bits shared with the CUDA kernels (nsn_b200/csrc/nsnkv_common.cuh).
+ST_INPUT_NONFINITE = 1
+ST_META_OVERFLOW = 2
+ST_META_UNDERFLOW = 4
+ST_OUTPUT_NONFINITE = 8
+
+
+class NumericalFailure(RuntimeError):
+    pass
+
+
+# ---------------------------------------------------------------- norms
+def row_sumsq_lanes8(a: np.ndarray) -> np.ndarray:
+    """Sum of squares over the last axis (128) in PyTorch's contiguous-row order."""
+    a = np.asarray(a, np.float32)
+    assert a.shape[-1] == DIM
+    acc = a[..., 0:8] * a[..., 0:8]
+    for i in range(8, DIM, 8):
+        blk = a[..., i:i + 8]
+        acc = acc + blk * blk
+    s = acc[..., 0].copy()
+    for j in range(1, 8):
+        s = s + acc[..., j]
+    return s
+
+
+def row_sumsq_seq(a: np.ndarray) -> np.ndarray:
+    """Sum of squares over the last axis in plain sequential order."""
+    a = np.asarray(a, np.float32)
+    s = a[..., 0] * a[..., 0]
+    for c in range(1, a.shape[-1]):
+        s = s + a[..., c] * a[..., c]
+    return s
+
+
+def row_norm(a: np.ndarray, strided: bool = False) -> np.ndarray:
+    s = row_sumsq_seq(a) if strided else row_sumsq_lanes8(a)
+    return np.sqrt(s).astype(np.float32)
+
+
+# ---------------------------------------------------------------- encode / decode
+def nsn_encode(x, bits: int, strided: bool = False):
+    """Restates ``nsn_encode`` (loop_kv_nb06_primitives.py:37-55).
+
+    x: float array [..., 64, 128] (fp16/bf16 values already widened exactly to
+    float32, or float32).  ``strided`` selects the sequential norm order that
+    the reference uses when the channel axis of ``x.float()`` is not
+    contiguous.  Returns (q uint8 [...,64,128], n f16 [...,64,1],
+    m f16 [...,1,128], s f16 [...,1,128], status bits).
+    """
+    a = np.asarray(x, np.float32)
+    assert a.shape[-2:] == (BLOCK, DIM)
+    status = 0
+    if not np.isfinite(a).all():
+        status |= ST_INPUT_NONFINITE
+    levels = np.float32((1 << bits) - 1)
+    n = row_norm(a, strided)[..., None]
+    d = a / np.maximum(n, EPS)
+    m = d.min(axis=-2, keepdims=True)
+    mx = d.max(axis=-2, keepdims=True)
+    s = (mx - m) / levels
+    denom = np.where(s == 0, np.float32(1), s)
+    q = np.clip(np.rint((d - m) / denom), 0, levels).astype(np.uint8)
+    q = np.where(s == 0, np.uint8(0), q)
+    with np.errstate(over="ignore", invalid="ignore"):
+        n16, m16, s16 = (t.astype(np.float16) for t in (n, m, s))
+    if not (np.isfinite(n16).all() and np.isfinite(m16).all() and np.isfinite(s16).all()):
+        status |= ST_META_OVERFLOW
+    if ((n != 0) & (n16 == 0)).any() or ((s != 0) & (s16 == 0)).any():
+        status |= ST_META_UNDERFLOW
+    return q, n16, m16, s16, status
+
+
+def nsn_decode(q, n16, m16, s16, out_dtype=np.float32, strided: bool = False):
+    """Restates ``nsn_decode`` (loop_kv_nb06_primitives.py:57-66) in float32.
+
+    Returns the float32 reconstruction before the final cast; ``cast`` below
+    performs the reference's ``.to(dtype)``.
+    """
+    n = np.asarray(n16, np.float32)
+    m = np.asarray(m16, np.float32)
+    s = np.asarray(s16, np.float32)
+    d = m + s * np.asarray(q, np.float32)
+    den = np.maximum(row_norm(d, strided)[..., None], EPS)
+    y = n * (d / den)
+    y = np.where(n == 0, np.float32(0), y)
+    return cast(y, out_dtype)
+
+
+def nsn_qdq(x, bits: int, out_dtype=np.float32, strided: bool = False):
+    q, n, m, s, _ = nsn_encode(x, bits, strided)
+    return nsn_decode(q, n, m, s, out_dtype)
+
+
+def nsn_int3_qdq(x, out_dtype=np.float32, strided: bool = False):
+    """nsn_int3_core.py:11-21 is nsn_qdq(x, 3) (the reference's own equality)."""
+    return nsn_qdq(x, 3, out_dtype, strided)
+
+
+# ---------------------------------------------------------------- dtype helpers
+def bf16_bits(a) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns, round to nearest even (NaN kept NaN)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32)
+    rounded = ((u + np.uint32(0x7FFF) + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(np.isnan(a), ((u >> 16) | 0x40).astype(np.uint16), rounded).astype(np.uint16)
+
+
+def from_bf16_bits(b) -> np.ndarray:
+    return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def cast(y, out_dtype):
+    """Cast float32 values as torch's ``.to(dtype)`` does; bf16 returned as float32 values."""
+    if out_dtype in (np.float32, "float32"):
+        return np.asarray(y, np.float32)
+    if out_dtype in (np.float16, "float16"):
+        with np.errstate(over="ignore"):
+            return np.asarray(y, np.float32).astype(np.float16)
+    if out_dtype in ("bfloat16",):
+        return from_bf16_bits(bf16_bits(y))
+    raise ValueError(out_dtype)
+
+
+# ---------------------------------------------------------------- bit packing
+def pack_codes(codes, bits: int) -> bytes:
+    """LSB-first bitstream (loop_kv_nb06_primitives.py:15-24): code i occupies bits [bits*i, bits*i+bits)."""
+    a = np.asarray(codes, np.uint8).reshape(-1)
+    if bits not in (3, 4, 5) or (a >= (1 << bits)).any():
+        raise ValueError("Invalid packed code")
+    pos = np.arange(a.size, dtype=np.int64) * bits
+    out = np.zeros((a.size * bits + 7) // 8, dtype=np.uint8)
+    val = a.astype(np.uint16) << (pos % 8).astype(np.uint16)
+    np.bitwise_or.at(out, pos // 8, (val & 255).astype(np.uint8))
+    crossing = pos % 8 + bits > 8
+    np.bitwise_or.at(out, pos[crossing] // 8 + 1, (val[crossing] >> 8).astype(np.uint8))
+    return out.tobytes()
+
+
+def unpack_codes(payload, count: int, bits: int) -> np.ndarray:
+    """Vectorised inverse of ``pack_codes`` (the reference's scalar loop is :26-35)."""
+    b = np.frombuffer(bytes(payload), np.uint8) if not isinstance(payload, np.ndarray) else payload.reshape(-1)
+    b = np.concatenate([b, np.zeros(2, np.uint8)])
+    pos = np.arange(count, dtype=np.int64) * bits
+    lo = b[pos // 8].astype(np.uint32)
+    hi = b[pos // 8 + 1].astype(np.uint32)
+    return (((lo | (hi << 8)) >> (pos % 8).astype(np.uint32)) & ((1 << bits) - 1)).astype(np.uint8)
+
+
+def pack3(q) -> np.ndarray:
+    """INT3 3-byte-group packing (loop_kv_nb06_codec.py:6-15); identical bytes to pack_codes(q, 3)."""
+    return np.frombuffer(pack_codes(q, 3), np.uint8).copy()
+
+
+def unpack3(payload, shape) -> np.ndarray:
+    count = int(np.prod(shape))
+    return unpack_codes(np.asarray(payload, np.uint8), count, 3).reshape(shape)
+
+
+def block_code_bytes(bits: int) -> int:
+    return BLOCK * DIM * bits // 8
+
+
+# ---------------------------------------------------------------- group / headers / bytes
+def block_headers(start: int, n_blocks: int, bits: int, rows: int) -> np.ndarray:
+    """'<QHBB' per block: token offset, 64, bits, 0 (loop_kv_nb06_codec.py:32)."""
+    one = b"".join(struct.pack("<QHBB", start + i * BLOCK, BLOCK, bits, 0) for i in range(n_blocks))
+    return np.frombuffer(one * rows, np.uint8).reshape(rows, n_blocks, 12).copy()
+
+
+def planned_bytes(shape, compressed_tokens: int, bits):
+    """loop_kv_nb06_primitives.py:72-81."""
+    b, h, length, d = shape
+    if compressed_tokens % BLOCK or not 0 <= compressed_tokens <= length:
+        raise ValueError("Block accounting")
+    if bits is None:
+        return {"codes": 0, "metadata": 0, "native": b * h * length * d * 2, "block_headers": 0}
+    blocks = b * h * (compressed_tokens // BLOCK)
+    return {"codes": blocks * ((BLOCK * d * bits + 7) // 8),
+            "metadata": blocks * (BLOCK * 2 + d * 4),
+            "native": b * h * (length - compressed_tokens) * d * 2,
+            "block_headers": blocks * 12}
+
+
+# ---------------------------------------------------------------- attention (bridge)
+def repeat_kv(x, n_rep: int):
+    """[B,H,T,D] -> [B,H*n_rep,T,D], head i of the output uses kv head i // n_rep."""
+    return np.repeat(np.asarray(x), n_rep, axis=1)
+
+
+def bridge_attention(q, k_full, v_full, dtype=np.float64):
+    """softmax(q k^T * 1/sqrt(128)) v over all stored positions, single query.
+
+    q [B,Hq,1,128]; k_full, v_full [B,H,T,128] (restored K/V cast to the bridge
+    dtype and concatenated with the tail).  Computed in float64; the reference's
+    fp32/fp16 SDPA and ``finish`` differ from this by rounding only.
+    Returns (out [B,Hq,128], lse [B,Hq]).
+    """
+    q = np.asarray(q, dtype)
+    k = np.asarray(k_full, dtype)
+    v = np.asarray(v_full, dtype)
+    rep = q.shape[1] // k.shape[1]
+    k = repeat_kv(k, rep)
+    v = repeat_kv(v, rep)
+    s = np.einsum("bhqd,bhtd->bhqt", q, k) * SCALE
+    mx = s.max(-1, keepdims=True)
+    p = np.exp(s - mx)
+    z = p.sum(-1, keepdims=True)
+    out = np.einsum("bhqt,bhtd->bhqd", p / z, v)
+    lse = (np.log(z) + mx)[..., 0, 0]
+    return out[:, :, 0, :], lse
+
+
+def restore_full(q_codes, n16, m16, s16, tail, out_dtype):
+    """Reference bridge restore: restore_group(g, dtype) then cat with the tail
+    (loop_kv_nb06_codec.py:36-38, loop_kv_nb06_kernel.py:167-168).
+
+    q_codes [B,H,n,64,128]; tail [B,H,t,128] (float32 values of the tail dtype).
+    """
+    parts = []
+    if q_codes is not None and q_codes.shape[2] > 0:
+        y = nsn_decode(q_codes, n16, m16, s16, out_dtype)
+        b, h, n = q_codes.shape[:3]
+        parts.append(np.asarray(y, np.float32).reshape(b, h, n * BLOCK, DIM))
+    if tail is not None and tail.shape[2] > 0:
+        parts.append(np.asarray(tail, np.float32))
+    return np.concatenate(parts, axis=2)
+
+
+# Attention parity bar per output dtype, (rtol, atol).  fp16 is the bar the
+# benchmark specification states.  bf16 keeps 8 significant bits (16x coarser
+# than fp16); the reference's own bf16 SDPA bridge deviates from the exact
+# result by up to 0.8% on the golden cases, so bf16 outputs use 1e-2.
+TOLERANCE = {"float16": (2e-3, 1e-3), "bfloat16": (1e-2, 1e-2), "float32": (2e-3, 1e-3)}
+
+
+def within_tolerance(got, want, rtol=2e-3, atol=1e-3):
+    """The attention parity bar: |got - want| <= atol + rtol*|want| elementwise."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = np.abs(got - want)
+    return bool(np.all(err <= atol + rtol * np.abs(want))), float(err.max()) if err.size else 0.0

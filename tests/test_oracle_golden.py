@@ -1,0 +1,132 @@
+"""Pin the CPU oracle (oracle/nsn_oracle.py) to the reference's own outputs.
+
+The golden vectors were produced by running the reference's torch/NumPy code
+(tests/golden/make_golden.py).  Every comparison here is bit-exact except the
+attention bridge, which is compared at the parity tolerance.
+"""
+import numpy as np
+import pytest
+
+import golden_util as G
+from oracle import nsn_oracle as O
+
+
+def test_pack_codes_kats():
+    for case in G.index()["pack_codes"]["cases"]:
+        codes = G.get(case["key"] + "_codes")
+        want = G.get(case["key"] + "_bytes")
+        got = np.frombuffer(O.pack_codes(codes, case["bits"]), np.uint8)
+        assert got.tobytes() == want.tobytes(), case
+        assert np.array_equal(O.unpack_codes(want, case["count"], case["bits"]), codes)
+
+
+def test_pack3_pattern_and_byte_pairs():
+    for case in G.index()["pack3"]["cases"]:
+        n = case["n"]
+        a = ((np.arange(n) * 5 + 3) % 8).astype(np.uint8)
+        assert O.pack3(a).tobytes() == G.get(case["key"]).tobytes()
+        assert np.array_equal(O.unpack3(G.get(case["key"]), (n,)), a)
+    a = np.repeat(np.arange(256, dtype=np.uint8), 256)
+    b = np.tile(np.arange(256, dtype=np.uint8), 256)
+    payload = np.stack((a, b, a ^ b), -1).reshape(-1)
+    import hashlib
+    codes = O.unpack3(payload, (65536 * 8,))
+    assert hashlib.sha256(codes.tobytes()).hexdigest() == G.index()["byte_pairs"]["codes_sha256"]
+
+
+def test_planned_bytes_kats():
+    for c in G.index()["planned_bytes"]["cases"]:
+        assert O.planned_bytes(tuple(c["shape"]), c["compressed"], c["bits"]) == c["want"]
+    with pytest.raises(ValueError):
+        O.planned_bytes((1, 1, 100, 128), 65, 3)
+
+
+@pytest.mark.parametrize("name", sorted(G.index()["encode"]))
+def test_encode_decode_bit_exact(name):
+    x, strided, entry = G.encode_input(name)
+    for bits, rec in entry["bits"].items():
+        bits = int(bits)
+        q, n, m, s, status = O.nsn_encode(x, bits, strided)
+        if "raises" in rec:
+            assert status != 0, (name, bits)
+            continue
+        assert status == 0, (name, bits, status)
+        key = rec["key"]
+        packed = np.frombuffer(O.pack_codes(q, bits), np.uint8)
+        assert G.matches(key + "_packed", packed), (name, bits)
+        for tag, t in (("n", n), ("m", m), ("s", s)):
+            assert G.matches(f"{key}_{tag}", t.view(np.uint16)), (name, bits, tag)
+        for dt in ("float16", "bfloat16", "float32"):
+            if rec.get("dec_" + dt) is not True:
+                continue
+            y = O.nsn_decode(q, n, m, s, dt)
+            if dt == "float16":
+                yb = y.view(np.uint16)
+            elif dt == "bfloat16":
+                yb = O.bf16_bits(y)
+            else:
+                yb = y.view(np.uint32)
+            assert G.matches(f"{key}_dec_{dt}", yb), (name, bits, dt)
+        if bits == 3:
+            assert rec["int3_qdq_equals_nsn_qdq"]
+            dtype = entry["dtype"]
+            y = O.nsn_int3_qdq(x, dtype, strided)
+            yb = {"float16": lambda a: a.view(np.uint16), "bfloat16": O.bf16_bits,
+                  "float32": lambda a: a.view(np.uint32)}[dtype](y)
+            assert G.matches(f"{key}_int3_qdq", yb), name
+
+
+def test_group_headers():
+    for start, key in ((0, "group_cfg0_k_headers"), (320, "group_cfg0_k_headers_start320")):
+        h = G.get(key)
+        n = h.shape[2]
+        want = O.block_headers(start, n, 3, h.shape[1]).reshape(h.shape)
+        assert want.tobytes() == h.tobytes()
+
+
+def test_group_codes_and_restore():
+    from nsn_b200 import workloads
+    k, v, _, _, _ = workloads.np_config(0)
+    for name, src in (("cfg0_k", k), ("cfg0_v", v)):
+        x = src.astype(np.float32).reshape(1, 8, 16, 64, 128)
+        q, n, m, s, st = O.nsn_encode(x, 3)
+        assert st == 0
+        codes = np.stack([O.pack3(q[0, h, i]) for h in range(8) for i in range(16)]).reshape(1, 8, 16, 3072)
+        assert G.matches(f"group_{name}_codes", codes)
+        y16 = O.nsn_decode(q, n, m, s, "float16").reshape(1, 8, 1024, 128)
+        assert G.matches(f"group_{name}_restore_float16", y16.view(np.uint16))
+        yb = O.nsn_decode(q, n, m, s, "bfloat16").reshape(1, 8, 1024, 128)
+        assert G.matches(f"group_{name}_restore_bfloat16", O.bf16_bits(yb))
+
+
+@pytest.mark.parametrize("name", sorted(G.index()["attention"]))
+def test_bridge_attention_oracle(name):
+    e = G.index()["attention"][name]
+    dt = e["dtype"]
+    if name == "cfg0":
+        from nsn_b200 import workloads
+        k, v, q, nb, t = workloads.np_config(0)
+        kin, vin = k.astype(np.float32), v.astype(np.float32)
+        assert G.matches("attn_cfg0_k_in", k.view(np.uint16))
+    else:
+        kin = G.bits_to_float32(G.get(f"attn_{name}_k_in"), dt)
+        vin = G.bits_to_float32(G.get(f"attn_{name}_v_in"), dt)
+    q = G.bits_to_float32(G.get(f"attn_{name}_q"), dt)
+    nb, t, h = e["blocks"], e["tail"], e["h"]
+    fulls = []
+    for src in (kin, vin):
+        if nb:
+            sealed = src[:, :, :nb * 64].reshape(1, h, nb, 64, 128)
+            qq, n, m, s, st = O.nsn_encode(sealed, 3)
+            assert st == 0
+            full = O.restore_full(qq, n, m, s, src[:, :, nb * 64:], dt)
+        else:
+            full = src
+        fulls.append(full)
+    out, _ = O.bridge_attention(q, fulls[0], fulls[1])
+    ref = G.bits_to_float32(G.get(f"attn_{name}_sdpa"), dt).reshape(out.shape)
+    fin = G.bits_to_float32(G.get(f"attn_{name}_finish"), "float32").reshape(out.shape)
+    ok, err = O.within_tolerance(out, ref, *O.TOLERANCE[dt])
+    assert ok, (name, err)
+    ok, err = O.within_tolerance(out, fin, rtol=1e-5, atol=1e-5)
+    assert ok, (name, err)
