@@ -1,0 +1,360 @@
+"""Benchmark: batched packed-KV decode on B200 (cfg2 of the NSN packed-KV path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nsn|reference] [--batch B]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
+
+Workload (cfg2, seed 2): batch 64 sequences, 32 query heads / 8 kv heads, head
+dim 128; per-sequence context = U{32..256} sealed INT3 64-token blocks + a tail
+of U[0,63] fp16 tokens.  One step = for every sequence append one new K/V token,
+attend with one query over sealed blocks + tail (fused packed-KV decode
+attention), and seal+encode every tail that reached 64 tokens.  Sequences are
+sharded across ranks (greedy by packed bytes), no collective on the data path.
+Synthetic data (seeded torch generator per sequence, the specification's
+distributions); the reference measures on captured model K/V that is not
+available here.
+
+Prints one JSON line on rank 0.  `value` = decoded tokens/s of the whole job
+(batch / max-over-ranks device time per step); timed with CUDA events per step,
+L2 flushed (a 256 MiB write) before every timed step, outside the events.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HBM_FALLBACK = 6650.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return HBM_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ clocks sampling
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region (every 200 ms)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+def shard_sequences(blocks, tails, world, rank):
+    """Greedy balance of sequences across ranks by packed bytes (largest first)."""
+    order = sorted(range(len(blocks)), key=lambda i: -(int(blocks[i]) * 3712 + int(tails[i]) * 256))
+    load = [0] * world
+    owner = [0] * len(blocks)
+    for i in order:
+        r = min(range(world), key=lambda x: load[x])
+        owner[i] = r
+        load[r] += int(blocks[i]) * 3712 + int(tails[i]) * 256
+    return sorted(i for i in range(len(blocks)) if owner[i] == rank)
+
+
+def build_cache(seqs, blocks, tails, steps, device, hq=32, h=8):
+    from nsn_b200 import workloads
+    from nsn_b200.paged import PagedKVCache
+    c = workloads.CONFIGS[2]
+    max_blocks = int(max(blocks[i] for i in seqs)) + (steps + 64) // 64 + 2
+    cache = PagedKVCache(len(seqs), h, max_blocks, bits=3, dtype=torch.float16, device=device, hq=hq)
+    for j, i in enumerate(seqs):
+        T = int(blocks[i]) * 64 + int(tails[i])
+        gen = torch.Generator(device=device).manual_seed(c["seed"] * 100003 + i)
+        k = workloads.torch_kv(gen, (h, T, 128), c["k_outliers"], 0.5, device=device)
+        v = workloads.torch_kv(gen, (h, T, 128), (), c["v_sigma"], device=device)
+        cache.prefill(j, k, v)
+        del k, v
+    torch.cuda.synchronize(device)
+    cache.check()
+    return cache
+
+
+def step_inputs(n_seq, steps, device, hq=32, h=8, seed=2):
+    gen = torch.Generator(device=device).manual_seed(seed * 7919 + 17)
+    q = (torch.randn((steps, n_seq, hq, 128), generator=gen, device=device) / math.sqrt(128)).half()
+    kn = (torch.randn((steps, n_seq, h, 128), generator=gen, device=device)).half()
+    vn = (torch.randn((steps, n_seq, h, 128), generator=gen, device=device)).half()
+    return q, kn, vn
+
+
+# ------------------------------------------------------------------ CPU baseline (reference bridge port)
+def cpu_bridge_rate(n_seq_sample=2, budget_s=12.0, impl_label="port"):
+    """Decode tokens/s of the reference's CPU bridge (torch port) on a bounded cfg2 sample."""
+    from oracle import bridge_torch as B
+    from oracle import nsn_oracle as O
+    from nsn_b200 import workloads
+    import numpy as np
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    blocks, tails = workloads.np_cfg2_lengths()
+    idx = list(range(n_seq_sample))
+    rng = np.random.default_rng(2)
+    cases = []
+    for i in idx:
+        nb, t = int(blocks[i]), int(tails[i])
+        k = workloads.np_kv(rng, (1, 8, nb * 64 + t, 128), workloads.K_OUTLIERS_4, 0.5)
+        v = workloads.np_kv(rng, (1, 8, nb * 64 + t, 128), (), 0.5)
+        parts = []
+        for src in (k, v):
+            qc, n, m, s, _ = O.nsn_encode(src[:, :, :nb * 64].astype(np.float32).reshape(1, 8, nb, 64, 128), 3)
+            codes = torch.from_numpy(np.frombuffer(O.pack_codes(qc, 3), np.uint8).copy().reshape(1, 8, nb, 3072))
+            parts.append((codes, tuple(torch.from_numpy(x) for x in (n, m, s)), torch.from_numpy(src[:, :, nb * 64:])))
+        q = torch.from_numpy((rng.standard_normal((1, 32, 1, 128)) / math.sqrt(128)).astype(np.float16))
+        cases.append((q, parts))
+    B.bridge_decode(cases[0][0], *cases[0][1][0], *cases[0][1][1])  # warm-up
+    done = 0
+    t0 = time.perf_counter()
+    samples = []
+    while time.perf_counter() - t0 < budget_s or done < 5:
+        for q, parts in cases:
+            s0 = time.perf_counter()
+            B.bridge_decode(q, *parts[0], *parts[1])
+            samples.append(time.perf_counter() - s0)
+            done += 1
+        if done >= 200:
+            break
+    med = statistics.median(samples)
+    return {"value": 1.0 / med, "unit": "tokens/s", "cores": threads, "kind": impl_label,
+            "sample": f"reference CPU bridge (torch port: restore_group fp16 + cat + repeat_kv + SDPA) on "
+                      f"{len(cases)} cfg2 sequences ({int(blocks[0])},{int(blocks[1])} blocks), median of {done} "
+                      f"single-sequence decodes, torch threads={threads}"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU bridge on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    for _ in range(max(args.warmup, 0)):
+        pass
+    res = cpu_bridge_rate(budget_s=min(30.0, 3.0 * max(args.steps, 1)), impl_label="port")
+    v = res["value"]
+    line = {"metric": "decode tokens/s (batched packed-KV decode, cfg2)", "value": v, "unit": "tokens/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * 64 / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "cfg2-batched-64 (bridge: restore_group + cat + repeat_kv + SDPA on CPU)",
+                       "batch": 64, "hq": 32, "h": 8, "bits": 3},
+            "cpu_baseline": res, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ main GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="nsn", choices=["nsn", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from nsn_b200 import workloads
+    from nsn_b200 import _lib as L
+    blocks, tails = workloads.np_cfg2_lengths(args.batch)
+    seqs = shard_sequences(blocks, tails, world, rank)
+    total_steps = args.warmup + args.steps
+    cache = build_cache(seqs, blocks, tails, total_steps + 1, device)
+    n_seq = len(seqs)
+    q, kn, vn = step_inputs(n_seq, total_steps + 1, device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    # bytes one attention launch reads (measured at the step it runs; sealing changes them)
+    def attn_bytes():
+        nb = cache.n_blocks.long()
+        tl = cache.tail_len.long() + 1  # + the appended token
+        per_block = 3072 + 64 * 2 + 128 * 4
+        return int((2 * 8 * (nb * per_block + tl * 256)).sum() + 2 * n_seq * 32 * 256 + n_seq * 8 * 2 * 256)
+
+    for i in range(args.warmup):
+        cache.step(q[i], kn[i], vn[i])
+    torch.cuda.synchronize(device)
+    cache.check()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    bytes_per = []
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            bytes_per.append(attn_bytes() if i < 4 or i == args.steps - 1 else None)
+            flush.zero_()
+            s = args.warmup + i
+            ev[i][0].record(stream)
+            cache.attend(q[s], kn[s], vn[s])
+            ev[i][1].record(stream)
+            cache.seal(1)
+            ev[i][2].record(stream)
+        torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    cache.check()
+    attn_ms = [a.elapsed_time(b) for a, b, _ in ev]
+    step_ms = [a.elapsed_time(c) for a, _, c in ev]
+    mean_step = sum(step_ms) / len(step_ms)
+    mean_attn = sum(attn_ms) / len(attn_ms)
+    t = torch.tensor([mean_step, mean_attn], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    mean_step, mean_attn_max = t.tolist()
+    known = [b for b in bytes_per if b is not None]
+    bytes_attn = sum(known) / len(known)
+
+    # ---- end to end through the public API with host buffers (pinned), rank-local
+    e2e = None
+    if True:
+        qh = q[:4].cpu().pin_memory()
+        knh = kn[:4].cpu().pin_memory()
+        vnh = vn[:4].cpu().pin_memory()
+        outh = torch.empty((n_seq, 32, 128), dtype=torch.float16).pin_memory()
+        qd, knd, vnd = torch.empty_like(q[0]), torch.empty_like(kn[0]), torch.empty_like(vn[0])
+        e_steps = max(8, min(args.steps, 32))
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(e_steps):
+            qd.copy_(qh[i % 4], non_blocking=True)
+            knd.copy_(knh[i % 4], non_blocking=True)
+            vnd.copy_(vnh[i % 4], non_blocking=True)
+            o = cache.step(qd, knd, vnd)
+            outh.copy_(o, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        te = torch.tensor([e0.elapsed_time(e1) / e_steps], dtype=torch.float64, device=device)
+        if dist:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = te.item()
+        e2e = {"value": args.batch / (e2e_ms / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(qd.numel() * 2 + knd.numel() * 2 + vnd.numel() * 2),
+               "d2h_bytes_per_step": int(outh.numel() * 2), "ms_per_step": e2e_ms,
+               "path": "PagedKVCache.step (public API), pinned host q/k_new/v_new in, output out, per rank"}
+        cache.check()
+
+    hbm, peak_kind = peaks()
+    achieved = bytes_attn / (mean_attn / 1000.0) / 1e9  # this rank
+    clocks = clk.summary()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu = cpu_bridge_rate()
+        line = {
+            "metric": "decode tokens/s (batched packed-KV decode, cfg2)",
+            "value": args.batch / (mean_step / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": mean_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "cfg2-batched-64: append 1 token + fused INT3 decode attention + seal, "
+                                   "GQA 32:8, head_dim 128, ctx U{32..256} blocks + tail U[0,63]",
+                       "global_batch": args.batch, "hq": 32, "h": 8, "bits": 3, "parallelism": f"batch-shard{world}",
+                       "l2": "flushed (256 MiB write) before every timed step, outside the events",
+                       "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
+                       "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
+            "roofline": {"bound": "hbm", "kernel": "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_launch": bytes_attn},
+            "e2e": e2e,
+            "gpu_launches": 4 * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * nsnkv.h - C ABI of the B200 (sm_100a) implementation of NSN's packed-KV path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and never
+ * synchronises.  Argument errors are returned as negative int codes before
+ * anything is launched.  Data errors found on the device (non-finite input,
+ * fp16 metadata overflow/underflow, non-finite output) are OR-ed into a caller
+ * owned device int32 status word, which the caller reads when it chooses.
+ *
+ * Block format (identical to the reference codec, bit for bit):
+ *   one block = 64 tokens x 128 channels of one (sequence, kv head);
+ *   codes  : LSB-first bitstream, element i = token*128 + channel occupies
+ *            bits [bits*i, bits*i + bits); 3072 B (INT3) / 4096 B (INT4) /
+ *            5120 B (INT5) per block;
+ *   norm   : fp16 [64]   per-token L2 norm;
+ *   min    : fp16 [128]  per-channel minimum of the unit direction;
+ *   scale  : fp16 [128]  per-channel (max - min) / (2^bits - 1);
+ *   header : 12 bytes '<QHBB' = token offset u64, 64 u16, bits u8, 0 u8.
+ * fp16/bf16 values are passed as raw uint16_t bit patterns.
+ */
+#ifndef NSNKV_H
+#define NSNKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define NSNKV_OK 0
+#define NSNKV_ERR_ARG (-1)         /* bad size, null pointer, misaligned pointer, bad dtype/bits */
+#define NSNKV_ERR_LAUNCH (-2)      /* the CUDA launch itself failed */
+#define NSNKV_ERR_UNSUPPORTED (-3) /* valid but not built (e.g. a GQA group size without a kernel) */
+#define NSNKV_ERR_CUDA (-4)        /* a CUDA runtime call other than a launch failed */
+#define NSNKV_ERR_TOO_LARGE (-5)   /* request exceeds a fixed capacity of the entry point */
+
+/* device status bits (int32, OR-accumulated) */
+#define NSNKV_ST_INPUT_NONFINITE 1   /* NaN/Inf in x, q, a tail or a metadata value */
+#define NSNKV_ST_META_OVERFLOW 2     /* fp16 norm/min/scale overflowed or is non-finite */
+#define NSNKV_ST_META_UNDERFLOW 4    /* a nonzero norm or scale rounded to fp16 zero */
+#define NSNKV_ST_OUTPUT_NONFINITE 8  /* NaN/Inf in a reconstruction or attention output */
+#define NSNKV_ST_TIMEOUT 32          /* a bounded wait inside a kernel gave up */
+#define NSNKV_ST_CAPACITY 64         /* an appended token found its tail buffer full (not stored) */
+
+/* element dtypes */
+#define NSNKV_F16 0
+#define NSNKV_BF16 1
+#define NSNKV_F32 2
+
+int nsnkv_version(void);
+
+/* Bytes of one packed 64x128 block for `bits` (3, 4 or 5); 0 for other values. */
+int64_t nsnkv_block_code_bytes(int bits);
+
+/*
+ * Encode rows x blocks_per_row contiguous 64x128 blocks of x.
+ * Replaces nsn_encode (experiments/nb06/source/loop_kv_nb06_primitives.py:37-55)
+ * followed by pack3 / pack_codes (loop_kv_nb06_codec.py:6-15,
+ * loop_kv_nb06_primitives.py:15-24) and the header of encode_group
+ * (loop_kv_nb06_codec.py:28-34).
+ *   x          [rows][blocks_per_row][64][128] of x_dtype, contiguous, 16-byte aligned
+ *   norm_order 0: the 8-lane sum-of-squares order torch uses for contiguous
+ *              rows; 1: sequential order (torch's order for strided rows)
+ *   input block (r, i) is written to output block index
+ *              o = r*out_row_stride + out_offset + i  (contiguous when
+ *              out_row_stride == blocks_per_row and out_offset == 0)
+ *   codes      [o][block_code_bytes] packed output (may be NULL)
+ *   q_out      [rows*blocks_per_row][64][128] unpacked uint8 codes in input order (may be NULL)
+ *   norm       [o][64] fp16; mn, scale [o][128] fp16
+ *   headers    [o][12] (may be NULL); token offset header_start + 64*i
+ *   status     device int32, OR-ed with NSNKV_ST_* bits
+ */
+int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits, int norm_order,
+                        uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale,
+                        uint8_t *headers, int64_t header_start, int64_t out_row_stride, int64_t out_offset,
+                        int32_t *status, void *stream);
+
+/*
+ * Reconstruct rows of sealed blocks followed by an optional native tail.
+ * Replaces nsn_decode (loop_kv_nb06_primitives.py:57-66), restore_group
+ * (loop_kv_nb06_codec.py:36-38) and the VF01 bridge restore_v/materialize
+ * (experiments/ac08/source/loop_kv_vf01_kernel.py:47-54,120-126).
+ *   rows x blocks_per_row blocks, block (r, i) at index r*blocks_per_row + i
+ *   codes      packed [n][block_code_bytes] (codes_unpacked = 0) or
+ *              unpacked uint8 [n][64][128] (codes_unpacked = 1)
+ *   tail       [rows][tail_len][128] of dtype (may be NULL when tail_len = 0)
+ *   out        [rows][blocks_per_row*64 + tail_len][128] of dtype
+ * Bit-exact with the reference's CPU arithmetic (8-lane norm order).
+ */
+int nsnkv_restore(const uint8_t *codes, int codes_unpacked, const uint16_t *norm, const uint16_t *mn,
+                  const uint16_t *scale, int64_t rows, int64_t blocks_per_row, int bits,
+                  const void *tail, int64_t tail_len, int dtype, void *out, int32_t *status, void *stream);
+
+/*
+ * LSB-first bitstream pack / unpack of `count` codes (any count).
+ * Replaces pack_codes / unpack_codes_reference (loop_kv_nb06_primitives.py:15-35)
+ * and pack3 / unpack3 (loop_kv_nb06_codec.py:6-26).  pack sets
+ * NSNKV_ST_INPUT_NONFINITE in status when a code is >= 2^bits.
+ */
+int nsnkv_pack(const uint8_t *codes, int64_t count, int bits, uint8_t *out, int32_t *status, void *stream);
+int nsnkv_unpack(const uint8_t *payload, int64_t count, int bits, uint8_t *out, void *stream);
+
+/*
+ * Fused packed-KV decode attention, one query token per sequence.
+ * Replaces VF01/NB06 launch(g, kt, q, vg, vt) (loop_kv_vf01_kernel.py:128-139,
+ * experiments/nb06/source/loop_kv_nb06_kernel.py:142-154): _partial + _merge.
+ *
+ * Sequence b, kv head h attends over n_blocks[b] sealed blocks followed by
+ * tail_len[b] native tail tokens (plus the appended token when k_new != NULL).
+ * Query head j uses kv head j / (hq / h) (repeat_kv grouping).
+ *   q            [batch][hq][128] of dtype
+ *   k_*, v_*     block pools; block (b, h, i) has index
+ *                  h*blk_stride_head + page*blk_stride_page,
+ *                page = block_table ? block_table[b*table_stride + i] : i
+ *   n_blocks     per-sequence sealed block count (device, may be NULL: use n_blocks_const)
+ *   k_tail/v_tail  element (b, h, j, c) at ((b*tail_stride_seq + h*tail_stride_head + j)*128 + c)
+ *   tail_len     per-sequence tail length (device, may be NULL: use tail_len_const)
+ *   k_new/v_new  [batch][h][128] token appended at tail index tail_len[b] and
+ *                attended (may be NULL); written into the tail buffers
+ *   max_blocks   upper bound of n_blocks[b] (sizes the launch grid)
+ *   out          [batch][hq][128] of dtype; out_f32 (may be NULL) fp32 copy;
+ *   lse          [batch][hq] log-sum-exp of the scaled scores (may be NULL)
+ *   workspace    device scratch of nsnkv_decode_attn_workspace_bytes() bytes
+ * Scores use scale 1/sqrt(128); softmax and accumulation are fp32.
+ */
+int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
+                      const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
+                      const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min, const uint16_t *v_scale,
+                      int64_t blk_stride_head, int64_t blk_stride_page,
+                      const int32_t *block_table, int64_t table_stride,
+                      const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                      void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                      const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail,
+                      const void *k_new, const void *v_new,
+                      void *out, float *out_f32, float *lse,
+                      void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+
+/* Workspace bytes nsnkv_decode_attn needs for these sizes. */
+int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t max_blocks, int32_t max_tail);
+
+/*
+ * Seal full tails of a paged cache: for every sequence b whose tail holds
+ * 64 tokens (after an append), encode the 64x128 tail of each kv head into
+ * page block_table[b*table_stride + n_blocks[b]] of the K and V pools, then set
+ * tail_len[b] = 0 and n_blocks[b] += 1.  Sequences with shorter tails are left
+ * unchanged.  Replaces the per-slot compress_to/post_decode seal
+ * (experiments/nb06/source/loop_kv_nb06_packed.py:36-56) with the
+ * seal-at-64 policy.  pending_append = 1 counts the token appended by the
+ * preceding nsnkv_decode_attn (k_new != NULL) into the tail length.
+ */
+int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
+                          void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                          int32_t *tail_len, int32_t *n_blocks, int pending_append,
+                          const int32_t *block_table, int64_t table_stride,
+                          uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
+                          uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
+                          int64_t blk_stride_head, int64_t blk_stride_page,
+                          int32_t *status, void *stream);
+
+/*
+ * Combine per-shard attention partials (one row per shard) into the final
+ * output: out = sum_s exp(lse_s - L) * o_s with L = log sum_s exp(lse_s).
+ *   o [n_shards][rows][128] fp32, lse [n_shards][rows] fp32, out [rows][128] of dtype.
+ * Used by the sequence-split (split-KV) multi-GPU path after an all-gather.
+ */
+int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *lse, int dtype,
+                       void *out, float *out_f32, float *lse_out, int32_t *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSNKV_H */

@@ -1,0 +1,511 @@
+// NSN block codec for sm_100a: encoder, restore (bridge reconstruct), bit pack/unpack,
+// and the paged-cache seal.  All arithmetic that the reference performs on the CPU is
+// reproduced bit for bit: every multiply/add/divide is individually rounded (no FMA
+// contraction), square roots and divisions are IEEE, rounding is half-to-even, and the
+// per-token sum of squares follows torch's CPU reduction order (nsnkv_common.cuh).
+#include "nsnkv_common.cuh"
+
+namespace nsnkv {
+
+// Shared-memory workspace of one 64x128 block encode/decode.
+struct BlockSmem {
+  float x[kBlock][kDim + 1];  // +1 pad: row-parallel reads are bank-conflict free
+  float tok[kBlock];          // per-token norm (encode) or denominator (decode)
+  float chan_min[kDim];
+  float chan_scale[kDim];
+  uint8_t q[kBlock * kDim];
+  uint8_t packed[kBlock * kDim * 5 / 8];
+};
+
+template <typename T> __device__ __forceinline__ float load_elem(const T *p) { return Elem<T>::to_f(*p); }
+
+// Load one contiguous 64x128 block into s.x (as float), flag non-finite input.
+template <typename T>
+__device__ __forceinline__ int load_block(const T *src, BlockSmem &s) {
+  int bad = 0;
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte load
+  constexpr int kChunks = kBlock * kDim / kVec;
+  for (int k = threadIdx.x; k < kChunks; k += blockDim.x) {
+    int e = k * kVec;
+    int r = e / kDim, c = e % kDim;
+    uint4 raw = reinterpret_cast<const uint4 *>(src)[k];
+    const T *v = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      float f = Elem<T>::to_f(v[j]);
+      bad |= !isfinite(f);
+      s.x[r][c + j] = f;
+    }
+  }
+  return bad ? NSNKV_ST_INPUT_NONFINITE : 0;
+}
+
+// Pack s.q (8192 codes) into s.packed as the LSB-first bitstream.
+template <int BITS>
+__device__ __forceinline__ void pack_block(BlockSmem &s) {
+  for (int g = threadIdx.x; g < kBlock * kDim / 8; g += blockDim.x) {
+    const uint2 w = reinterpret_cast<const uint2 *>(s.q)[g];
+    uint64_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t code = ((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xFFu;
+      v |= static_cast<uint64_t>(code) << (BITS * j);
+    }
+#pragma unroll
+    for (int b = 0; b < BITS; ++b) s.packed[g * BITS + b] = static_cast<uint8_t>(v >> (8 * b));
+  }
+}
+
+// Encode the block held in s.x.  Outputs go to global memory (any may be null).
+// Mirrors nsn_encode (loop_kv_nb06_primitives.py:37-55) step for step.
+template <int BITS>
+__device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uint8_t *q_out,
+                               uint16_t *norm, uint16_t *mn, uint16_t *scale, int32_t *status, int in_status) {
+  const int tid = threadIdx.x;
+  constexpr float kLevels = static_cast<float>((1 << BITS) - 1);
+  int st = in_status;
+  // n = ||x||_2 per token, torch's CPU order.
+  if (tid < kBlock) {
+    float ss = norm_order == 0 ? sumsq_lanes8(&s.x[tid][0], 1) : sumsq_seq(&s.x[tid][0], 1);
+    float n = sqrtf(ss);
+    s.tok[tid] = n;
+    __half n16 = __float2half_rn(n);
+    float n16f = __half2float(n16);
+    if (!isfinite(n16f)) st |= NSNKV_ST_META_OVERFLOW;
+    if (n != 0.f && n16f == 0.f) st |= NSNKV_ST_META_UNDERFLOW;
+    if (norm) norm[tid] = __half_as_ushort(n16);
+  }
+  __syncthreads();
+  // d = x / max(n, eps)
+  for (int e = tid; e < kBlock * kDim; e += blockDim.x) {
+    int r = e / kDim, c = e % kDim;
+    s.x[r][c] = div_rn(s.x[r][c], fmaxf(s.tok[r], kEps));
+  }
+  __syncthreads();
+  // per-channel min / scale, then codes
+  for (int c = tid; c < kDim; c += blockDim.x) {
+    float lo = s.x[0][c], hi = s.x[0][c];
+    for (int r = 1; r < kBlock; ++r) {
+      lo = fminf(lo, s.x[r][c]);
+      hi = fmaxf(hi, s.x[r][c]);
+    }
+    float sc = div_rn(sub_rn(hi, lo), kLevels);
+    float denom = sc == 0.f ? 1.f : sc;
+    for (int r = 0; r < kBlock; ++r) {
+      float v = rintf(div_rn(sub_rn(s.x[r][c], lo), denom));
+      v = fminf(fmaxf(v, 0.f), kLevels);
+      uint8_t code = sc == 0.f ? 0 : static_cast<uint8_t>(v);
+      s.q[r * kDim + c] = code;
+    }
+    __half m16 = __float2half_rn(lo), s16 = __float2half_rn(sc);
+    float m16f = __half2float(m16), s16f = __half2float(s16);
+    if (!isfinite(m16f) || !isfinite(s16f)) st |= NSNKV_ST_META_OVERFLOW;
+    if (sc != 0.f && s16f == 0.f) st |= NSNKV_ST_META_UNDERFLOW;
+    if (mn) mn[c] = __half_as_ushort(m16);
+    if (scale) scale[c] = __half_as_ushort(s16);
+  }
+  __syncthreads();
+  if (q_out) {
+    for (int k = tid; k < kBlock * kDim / 16; k += blockDim.x)
+      reinterpret_cast<uint4 *>(q_out)[k] = reinterpret_cast<const uint4 *>(s.q)[k];
+  }
+  if (codes) {
+    pack_block<BITS>(s);
+    __syncthreads();
+    for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
+      reinterpret_cast<uint4 *>(codes)[k] = reinterpret_cast<const uint4 *>(s.packed)[k];
+  }
+  if (st) set_status(status, st);
+}
+
+__device__ __forceinline__ void write_header(uint8_t *h, int64_t offset, int bits) {
+  uint64_t off = static_cast<uint64_t>(offset);
+#pragma unroll
+  for (int b = 0; b < 8; ++b) h[b] = static_cast<uint8_t>(off >> (8 * b));
+  h[8] = kBlock & 0xFF;
+  h[9] = kBlock >> 8;
+  h[10] = static_cast<uint8_t>(bits);
+  h[11] = 0;
+}
+
+// Input block b = r*blocks_per_row + i is written to output block index
+// r*out_row_stride + out_offset + i (a contiguous [rows][blocks_per_row] layout when
+// out_row_stride == blocks_per_row and out_offset == 0; a head-major page pool otherwise).
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm_order, int64_t blocks_per_row,
+                                                            uint8_t *codes, uint8_t *q_out, uint16_t *norm,
+                                                            uint16_t *mn, uint16_t *scale, uint8_t *headers,
+                                                            int64_t header_start, int64_t out_row_stride,
+                                                            int64_t out_offset, int32_t *status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
+  const int64_t b = blockIdx.x;
+  const int64_t r = b / blocks_per_row, i = b % blocks_per_row;
+  const int64_t o = r * out_row_stride + out_offset + i;
+  int st = load_block<T>(x + b * kBlock * kDim, s);
+  __syncthreads();
+  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * code_bytes(BITS) : nullptr,
+                       q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, mn + o * kDim,
+                       scale + o * kDim, status, st);
+  if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
+}
+
+// ----------------------------------------------------------------- restore
+// d = m + s*q (separately rounded), y = n * (d / max(||d||, eps)), 0 where n == 0.
+// Mirrors nsn_decode (loop_kv_nb06_primitives.py:57-66).
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) restore_kernel(const uint8_t *codes, int codes_unpacked, const uint16_t *norm,
+                                                      const uint16_t *mn, const uint16_t *scale,
+                                                      int64_t blocks_per_row, int64_t row_tokens, T *out,
+                                                      int32_t *status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x;
+  int st = 0;
+  if (tid < kDim) {
+    s.chan_min[tid] = half_bits_to_f(mn[b * kDim + tid]);
+    s.chan_scale[tid] = half_bits_to_f(scale[b * kDim + tid]);
+    if (!isfinite(s.chan_min[tid]) || !isfinite(s.chan_scale[tid])) st |= NSNKV_ST_INPUT_NONFINITE;
+  }
+  if (codes_unpacked) {
+    const uint8_t *q = codes + b * kBlock * kDim;
+    for (int k = tid; k < kBlock * kDim / 16; k += blockDim.x)
+      reinterpret_cast<uint4 *>(s.q)[k] = reinterpret_cast<const uint4 *>(q)[k];
+  } else {
+    const uint8_t *src = codes + b * code_bytes(BITS);
+    for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
+      reinterpret_cast<uint4 *>(s.packed)[k] = reinterpret_cast<const uint4 *>(src)[k];
+  }
+  __syncthreads();
+  for (int e = tid; e < kBlock * kDim; e += blockDim.x) {
+    uint32_t code;
+    if (codes_unpacked) {
+      code = s.q[e];
+    } else {
+      int pos = e * BITS;
+      uint32_t lo = s.packed[pos >> 3];
+      uint32_t hi = (pos >> 3) + 1 < code_bytes(BITS) ? s.packed[(pos >> 3) + 1] : 0u;
+      code = ((lo | (hi << 8)) >> (pos & 7)) & ((1u << BITS) - 1u);
+    }
+    int r = e / kDim, c = e % kDim;
+    s.x[r][c] = add_rn(s.chan_min[c], mul_rn(s.chan_scale[c], static_cast<float>(code)));
+  }
+  __syncthreads();
+  if (tid < kBlock) {
+    float ss = sumsq_lanes8(&s.x[tid][0], 1);
+    s.tok[tid] = fmaxf(sqrtf(ss), kEps);
+  }
+  __syncthreads();
+  const int64_t row = b / blocks_per_row, blk = b % blocks_per_row;
+  T *dst = out + (row * row_tokens + blk * kBlock) * kDim;
+  for (int e = tid; e < kBlock * kDim; e += blockDim.x) {
+    int r = e / kDim, c = e % kDim;
+    float n = half_bits_to_f(norm[b * kBlock + r]);
+    float y = n == 0.f ? 0.f : mul_rn(n, div_rn(s.x[r][c], s.tok[r]));
+    T o = Elem<T>::from_f(y);
+    if (!isfinite(Elem<T>::to_f(o)) || !isfinite(n)) st |= (!isfinite(n) ? NSNKV_ST_INPUT_NONFINITE : NSNKV_ST_OUTPUT_NONFINITE);
+    dst[e] = o;
+  }
+  if (st) set_status(status, st);
+}
+
+template <typename T>
+__global__ void copy_tail_kernel(const T *tail, int64_t rows, int64_t tail_len, int64_t row_tokens, int64_t offset_tokens,
+                                 T *out, int32_t *status) {
+  const int64_t n = rows * tail_len * kDim;
+  int bad = 0;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = e / (tail_len * kDim), rem = e % (tail_len * kDim);
+    T v = tail[e];
+    bad |= !isfinite(Elem<T>::to_f(v));
+    out[r * row_tokens * kDim + offset_tokens * kDim + rem] = v;
+  }
+  if (bad) set_status(status, NSNKV_ST_INPUT_NONFINITE);
+}
+
+// ----------------------------------------------------------------- bitstream pack / unpack
+__global__ void pack_kernel(const uint8_t *codes, int64_t count, int bits, uint8_t *out, int32_t *status) {
+  const int64_t groups = (count + 7) / 8;
+  const int64_t total = (count * bits + 7) / 8;
+  int bad = 0;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint64_t v = 0;
+    for (int j = 0; j < 8; ++j) {
+      int64_t i = g * 8 + j;
+      if (i < count) {
+        uint32_t c = codes[i];
+        bad |= c >> bits;
+        v |= static_cast<uint64_t>(c & ((1u << bits) - 1u)) << (bits * j);
+      }
+    }
+    for (int b = 0; b < bits; ++b) {
+      int64_t o = g * bits + b;
+      if (o < total) out[o] = static_cast<uint8_t>(v >> (8 * b));
+    }
+  }
+  if (bad) set_status(status, NSNKV_ST_INPUT_NONFINITE);
+}
+
+__global__ void unpack_kernel(const uint8_t *payload, int64_t count, int bits, uint8_t *out) {
+  const int64_t groups = (count + 7) / 8;
+  const int64_t total = (count * bits + 7) / 8;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint64_t v = 0;
+    for (int b = 0; b < bits; ++b) {
+      int64_t o = g * bits + b;
+      if (o < total) v |= static_cast<uint64_t>(payload[o]) << (8 * b);
+    }
+    for (int j = 0; j < 8; ++j) {
+      int64_t i = g * 8 + j;
+      if (i < count) out[i] = static_cast<uint8_t>((v >> (bits * j)) & ((1u << bits) - 1u));
+    }
+  }
+}
+
+// ----------------------------------------------------------------- paged-cache seal
+// One CTA per (kv head, K|V, sequence).  A sequence whose tail holds 64 tokens
+// has that tail encoded into its next page; nothing else is touched here.
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_tail, int64_t tss, int64_t tsh,
+                                                   const int32_t *tail_len, const int32_t *n_blocks, int pending,
+                                                   const int32_t *table, int64_t table_stride, uint8_t *k_codes,
+                                                   uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
+                                                   uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
+                                                   uint16_t *v_scale, int64_t sh, int64_t sp, int32_t *status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
+  const int h = blockIdx.x, kv = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  if (tail_len[b] + pending < kBlock) return;
+  const int32_t page = table[b * table_stride + n_blocks[b]];
+  const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
+  const T *src = (kv == 0 ? k_tail : v_tail) + (b * tss + h * tsh) * kDim;
+  int st = load_block<T>(src, s);
+  __syncthreads();
+  if (kv == 0)
+    encode_in_smem<BITS>(s, 0, k_codes + blk * code_bytes(BITS), nullptr, k_norm + blk * kBlock, k_min + blk * kDim,
+                         k_scale + blk * kDim, status, st);
+  else
+    encode_in_smem<BITS>(s, 0, v_codes + blk * code_bytes(BITS), nullptr, v_norm + blk * kBlock, v_min + blk * kDim,
+                         v_scale + blk * kDim, status, st);
+}
+
+__global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_blocks, int pending) {
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < batch;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int32_t t = tail_len[b] + pending;
+    if (t >= kBlock) {
+      n_blocks[b] += 1;
+      t -= kBlock;
+    }
+    tail_len[b] = t;
+  }
+}
+
+// ----------------------------------------------------------------- host dispatch
+template <typename T>
+static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits, int norm_order, uint8_t *codes,
+                         uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale, uint8_t *headers,
+                         int64_t header_start, int64_t out_row_stride, int64_t out_offset, int32_t *status,
+                         cudaStream_t st) {
+  const size_t smem = sizeof(BlockSmem);
+  dim3 grid(static_cast<unsigned>(n_blocks));
+#define NSNKV_ENC(B)                                                                                      \
+  case B: {                                                                                               \
+    auto k = encode_blocks_kernel<T, B>;                                                                  \
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)       \
+      return NSNKV_ERR_CUDA;                                                                              \
+    k<<<grid, 256, smem, st>>>(static_cast<const T *>(x), norm_order, bpr, codes, q_out, norm, mn, scale, \
+                               headers, header_start, out_row_stride, out_offset, status);                \
+    break;                                                                                                \
+  }
+  switch (bits) {
+    NSNKV_ENC(3)
+    NSNKV_ENC(4)
+    NSNKV_ENC(5)
+    default:
+      return NSNKV_ERR_ARG;
+  }
+#undef NSNKV_ENC
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+template <typename T>
+static int launch_restore(const uint8_t *codes, int unpacked, const uint16_t *norm, const uint16_t *mn,
+                          const uint16_t *scale, int64_t rows, int64_t bpr, int bits, const void *tail,
+                          int64_t tail_len, void *out, int32_t *status, cudaStream_t st) {
+  const size_t smem = sizeof(BlockSmem);
+  const int64_t row_tokens = bpr * kBlock + tail_len;
+  const int64_t n = rows * bpr;
+  if (n > 0) {
+    dim3 grid(static_cast<unsigned>(n));
+#define NSNKV_RES(B)                                                                                       \
+  case B: {                                                                                                \
+    auto k = restore_kernel<T, B>;                                                                         \
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
+      return NSNKV_ERR_CUDA;                                                                               \
+    k<<<grid, 256, smem, st>>>(codes, unpacked, norm, mn, scale, bpr, row_tokens, static_cast<T *>(out),   \
+                               status);                                                                    \
+    break;                                                                                                 \
+  }
+    switch (bits) {
+      NSNKV_RES(3)
+      NSNKV_RES(4)
+      NSNKV_RES(5)
+      default:
+        return NSNKV_ERR_ARG;
+    }
+#undef NSNKV_RES
+  }
+  if (tail_len > 0) {
+    int64_t total = rows * tail_len * kDim;
+    unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4096));
+    copy_tail_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T *>(tail), rows, tail_len, row_tokens,
+                                                bpr * kBlock, static_cast<T *>(out), status);
+  }
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+template <typename T>
+static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tail, int64_t tss, int64_t tsh,
+                       int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
+                       uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
+                       uint16_t *vm, uint16_t *vs, int64_t sh, int64_t sp, int32_t *status, cudaStream_t st) {
+  const size_t smem = sizeof(BlockSmem);
+  dim3 grid(h, 2, static_cast<unsigned>(batch));
+#define NSNKV_SEAL(B)                                                                                      \
+  case B: {                                                                                                \
+    auto k = seal_kernel<T, B>;                                                                            \
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
+      return NSNKV_ERR_CUDA;                                                                               \
+    k<<<grid, 256, smem, st>>>(static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss, tsh,   \
+                               tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, sh, \
+                               sp, status);                                                                \
+    break;                                                                                                 \
+  }
+  switch (bits) {
+    NSNKV_SEAL(3)
+    NSNKV_SEAL(4)
+    NSNKV_SEAL(5)
+    default:
+      return NSNKV_ERR_ARG;
+  }
+#undef NSNKV_SEAL
+  seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending);
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+}  // namespace nsnkv
+
+using namespace nsnkv;
+
+extern "C" {
+
+int nsnkv_version(void) { return 1; }
+
+int64_t nsnkv_block_code_bytes(int bits) { return (bits >= 3 && bits <= 5) ? code_bytes(bits) : 0; }
+
+int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits, int norm_order,
+                        uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale,
+                        uint8_t *headers, int64_t header_start, int64_t out_row_stride, int64_t out_offset,
+                        int32_t *status, void *stream) {
+  if (rows < 0 || blocks_per_row < 0 || bits < 3 || bits > 5 || (norm_order != 0 && norm_order != 1))
+    return NSNKV_ERR_ARG;
+  const int64_t n_blocks = rows * blocks_per_row;
+  if (n_blocks == 0) return NSNKV_OK;
+  if (n_blocks > 0x7FFFFFFF || !x || !norm || !mn || !scale || !status || !aligned16(x)) return NSNKV_ERR_ARG;
+  if ((codes && !aligned16(codes)) || (q_out && !aligned16(q_out))) return NSNKV_ERR_ARG;
+  if (out_offset < 0 || (rows > 1 && out_row_stride < blocks_per_row)) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (x_dtype) {
+    case NSNKV_F16:
+      return launch_encode<__half>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
+                                   headers, header_start, out_row_stride, out_offset, status, st);
+    case NSNKV_BF16:
+      return launch_encode<__nv_bfloat16>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn,
+                                          scale, headers, header_start, out_row_stride, out_offset, status, st);
+    case NSNKV_F32:
+      return launch_encode<float>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
+                                  headers, header_start, out_row_stride, out_offset, status, st);
+    default:
+      return NSNKV_ERR_ARG;
+  }
+}
+
+int nsnkv_restore(const uint8_t *codes, int codes_unpacked, const uint16_t *norm, const uint16_t *mn,
+                  const uint16_t *scale, int64_t rows, int64_t blocks_per_row, int bits, const void *tail,
+                  int64_t tail_len, int dtype, void *out, int32_t *status, void *stream) {
+  if (rows < 0 || blocks_per_row < 0 || tail_len < 0 || bits < 3 || bits > 5 || !out || !status) return NSNKV_ERR_ARG;
+  if (rows * blocks_per_row > 0x7FFFFFFF) return NSNKV_ERR_ARG;
+  if (rows * blocks_per_row > 0 && (!codes || !norm || !mn || !scale || !aligned16(codes))) return NSNKV_ERR_ARG;
+  if (tail_len > 0 && !tail) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case NSNKV_F16:
+      return launch_restore<__half>(codes, codes_unpacked, norm, mn, scale, rows, blocks_per_row, bits, tail,
+                                    tail_len, out, status, st);
+    case NSNKV_BF16:
+      return launch_restore<__nv_bfloat16>(codes, codes_unpacked, norm, mn, scale, rows, blocks_per_row, bits,
+                                           tail, tail_len, out, status, st);
+    case NSNKV_F32:
+      return launch_restore<float>(codes, codes_unpacked, norm, mn, scale, rows, blocks_per_row, bits, tail,
+                                   tail_len, out, status, st);
+    default:
+      return NSNKV_ERR_ARG;
+  }
+}
+
+int nsnkv_pack(const uint8_t *codes, int64_t count, int bits, uint8_t *out, int32_t *status, void *stream) {
+  if (count < 0 || bits < 3 || bits > 5) return NSNKV_ERR_ARG;
+  if (count == 0) return NSNKV_OK;
+  if (!codes || !out || !status) return NSNKV_ERR_ARG;
+  int64_t groups = (count + 7) / 8;
+  unsigned blocks = static_cast<unsigned>(std::min<int64_t>((groups + 255) / 256, 8192));
+  pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(codes, count, bits, out, status);
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+int nsnkv_unpack(const uint8_t *payload, int64_t count, int bits, uint8_t *out, void *stream) {
+  if (count < 0 || bits < 3 || bits > 5) return NSNKV_ERR_ARG;
+  if (count == 0) return NSNKV_OK;
+  if (!payload || !out) return NSNKV_ERR_ARG;
+  int64_t groups = (count + 7) / 8;
+  unsigned blocks = static_cast<unsigned>(std::min<int64_t>((groups + 255) / 256, 8192));
+  unpack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(payload, count, bits, out);
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
+                          int64_t tail_stride_seq, int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks,
+                          int pending_append, const int32_t *block_table, int64_t table_stride, uint8_t *k_codes,
+                          uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm,
+                          uint16_t *v_min, uint16_t *v_scale, int64_t blk_stride_head, int64_t blk_stride_page,
+                          int32_t *status, void *stream) {
+  if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
+  if (batch == 0) return NSNKV_OK;
+  if (!k_tail || !v_tail || !tail_len || !n_blocks || !block_table || !k_codes || !v_codes || !status)
+    return NSNKV_ERR_ARG;
+  if (!aligned16(k_tail) || !aligned16(v_tail) || !aligned16(k_codes) || !aligned16(v_codes)) return NSNKV_ERR_ARG;
+  if (tail_stride_head < kBlock || tail_stride_seq < tail_stride_head * h) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case NSNKV_F16:
+      return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
+                                 n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
+                                 k_scale, v_codes, v_norm, v_min, v_scale, blk_stride_head, blk_stride_page, status,
+                                 st);
+    case NSNKV_BF16:
+      return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
+                                        tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
+                                        k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, blk_stride_head,
+                                        blk_stride_page, status, st);
+    default:
+      return NSNKV_ERR_ARG;
+  }
+}
+
+}  // extern "C"
