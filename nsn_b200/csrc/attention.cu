@@ -50,9 +50,11 @@ struct AttnArgs {
   int32_t *status;
 };
 
-constexpr int kThreads = 128;  // 4 warps: 4 x 16 tokens of a 64-token block
-constexpr int kHeads = 8;      // MMA N: query heads per kv head (G <= 8)
+constexpr int kThreads = 128;    // 4 warps: 4 x 16 tokens of a 64-token block
+constexpr int kHeads = 8;        // MMA N: query heads per kv head (G <= 8)
 constexpr int kVRow = kDim + 8;  // padded V tile row (272 B): ldmatrix rows hit distinct banks
+constexpr int kStages = 4;       // TMA ring depth (blocks in flight per CTA)
+constexpr int kMetaRow = kDim + kDim / 8;  // fp32 metadata row padded every 32 channels by 4 floats
 
 template <int BITS>
 struct Stage {
@@ -66,46 +68,24 @@ struct Stage {
   uint16_t vs[kDim];
 };
 
+// Per-block fp32 metadata in the form the restore uses: with x = 1 + code * 2^-BITS
+// (the code dropped into the top mantissa bits of 1.0f),
+//   d = min + scale*code = b*x + a,  b = scale * 2^BITS,  a = min - b.
+struct MetaF {
+  float ka[kMetaRow], kb[kMetaRow], va[kMetaRow], vb[kMetaRow];
+};
+
 template <int BITS>
 struct AttnSmem {
-  Stage<BITS> stage[2];
+  Stage<BITS> stage[kStages];
+  MetaF meta[2];
   uint16_t v16[kBlock][kVRow];  // restored V tile in the bridge dtype
-  float p[kHeads][kBlock];      // scores, then softmax weights of the current tile
-  float mrun[kHeads], lrun[kHeads], rescale[kHeads];
-  uint64_t full[2];
+  float sc[kHeads][kBlock];     // scores of the current tile
+  uint64_t full[kStages];
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-
-// Extract CPT codes of BITS bits starting at bit offset `bitoff` of the staged
-// bitstream `src` (4-byte aligned).  Codes are returned as exact float pairs.
-template <int BITS, int CPT>
-__device__ __forceinline__ void unpack_codes_f2(const uint8_t *src, int bitoff, float2 (&k2)[CPT / 2]) {
-  constexpr int kBitsSpan = BITS * CPT;
-  constexpr int kWords = (kBitsSpan + 31) / 32 + 1;
-  const uint32_t *w = reinterpret_cast<const uint32_t *>(src) + (bitoff >> 5);
-  const int sh = bitoff & 31;
-  uint32_t raw[kWords + 1];
-#pragma unroll
-  for (int i = 0; i < kWords; ++i) raw[i] = w[i];
-  raw[kWords] = 0;
-  uint32_t al[kWords];
-#pragma unroll
-  for (int i = 0; i < kWords; ++i) al[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
-#pragma unroll
-  for (int j = 0; j < CPT; ++j) {
-    constexpr uint32_t kMask = (1u << BITS) - 1u;
-    const int pos = BITS * j;
-    const int wi = pos >> 5, bi = pos & 31;
-    uint32_t v = (bi + BITS <= 32) ? (al[wi] >> bi) : __funnelshift_r(al[wi], al[wi + 1], bi);
-    // exact integer -> float via the 2^23 exponent trick (code < 2^23)
-    float f = __uint_as_float(0x4B000000u | (v & kMask)) - 8388608.0f;
-    if (j & 1)
-      k2[j >> 1].y = f;
-    else
-      k2[j >> 1].x = f;
-  }
-}
+__device__ __forceinline__ int meta_index(int c) { return c + (c >> 5) * 4; }
 
 // Round a float pair to the bridge dtype and pack it (low half = .x).
 template <typename T> __device__ __forceinline__ uint32_t pack2(float2 v);
@@ -148,26 +128,77 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *
 
 __device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
 
-// Restore one token row slice (32 channels of this lane) of a staged block:
-// returns the packed bridge-dtype pairs and flags non-finite intermediates.
+// Load the packed bits of this lane's 32 channels of token t, aligned so that
+// channel j's code starts at bit BITS*j of the returned word array.
+template <int BITS>
+struct RowBits {
+  static constexpr int kWords = (BITS * 32 + 31) / 32;
+  uint32_t w[kWords + 1];
+  __device__ __forceinline__ void load(const uint8_t *codes, int t, int cbase) {
+    const int bitoff = BITS * (t * kDim + cbase);
+    const uint32_t *p = reinterpret_cast<const uint32_t *>(codes) + (bitoff >> 5);
+    const int sh = bitoff & 31;
+    uint32_t raw[kWords + 2];
+#pragma unroll
+    for (int i = 0; i < kWords + 1; ++i) raw[i] = p[i];
+    raw[kWords + 1] = 0;
+#pragma unroll
+    for (int i = 0; i < kWords + 1; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+  }
+  // x_j = 1 + code_j * 2^-BITS as a float: the code placed in the top BITS mantissa bits.
+  __device__ __forceinline__ float x(int j) const {
+    constexpr int kTop = 23 - BITS;
+    const int pos = BITS * j, wi = pos >> 5, bi = pos & 31;
+    uint32_t v;
+    if (bi + BITS <= 32) {
+      v = kTop >= bi ? (w[wi] << (kTop - bi)) : (w[wi] >> (bi - kTop));
+    } else {
+      v = __funnelshift_r(w[wi], w[wi + 1], bi) << kTop;
+    }
+    return __uint_as_float((v & (((1u << BITS) - 1u) << kTop)) | 0x3F800000u);
+  }
+};
+
+// Restore rows t0 and t1 (this lane's 32 channels each) of a staged block and
+// round them to the bridge dtype: out*[m] packs channels cbase+2m, cbase+2m+1.
 template <int BITS, typename T>
-__device__ __forceinline__ void restore_row(const uint8_t *codes, int t, int cbase, const float2 (&m2)[16],
-                                            const float2 (&s2)[16], float n, uint32_t (&out)[16], int &st) {
-  float2 d[16];
-  unpack_codes_f2<BITS, 32>(codes, BITS * (t * kDim + cbase), d);
-  float2 ss2 = f2(0.f, 0.f);
+__device__ __forceinline__ void restore_rows(const uint8_t *codes, const float *ma, const float *mb, int t0, int t1,
+                                             int cbase, float n0, float n1, uint32_t (&out0)[16],
+                                             uint32_t (&out1)[16]) {
+  RowBits<BITS> r0, r1;
+  r0.load(codes, t0, cbase);
+  r1.load(codes, t1, cbase);
+  float2 d0[16], d1[16];
+  float2 ss0 = f2(0.f, 0.f), ss1 = f2(0.f, 0.f);
+  const int mi = meta_index(cbase);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 a4 = *reinterpret_cast<const float4 *>(&ma[mi + 4 * q]);
+    const float4 b4 = *reinterpret_cast<const float4 *>(&mb[mi + 4 * q]);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int m = 2 * q + e;
+      const float2 a2 = e ? f2(a4.z, a4.w) : f2(a4.x, a4.y);
+      const float2 b2 = e ? f2(b4.z, b4.w) : f2(b4.x, b4.y);
+      d0[m] = __ffma2_rn(b2, f2(r0.x(2 * m), r0.x(2 * m + 1)), a2);
+      d1[m] = __ffma2_rn(b2, f2(r1.x(2 * m), r1.x(2 * m + 1)), a2);
+      ss0 = __ffma2_rn(d0[m], d0[m], ss0);
+      ss1 = __ffma2_rn(d1[m], d1[m], ss1);
+    }
+  }
+  float s0 = ss0.x + ss0.y, s1 = ss1.x + ss1.y;
+  s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+  s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+  // norm / max(||d||, eps); the eps clamp only matters for an all-zero direction
+  const float al0 = n0 == 0.f ? 0.f : (s0 > 1e-24f ? n0 * rsqrtf(s0) : n0 * 1e12f);
+  const float al1 = n1 == 0.f ? 0.f : (s1 > 1e-24f ? n1 * rsqrtf(s1) : n1 * 1e12f);
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
-    d[m] = __ffma2_rn(s2[m], d[m], m2[m]);
-    ss2 = __ffma2_rn(d[m], d[m], ss2);
+    out0[m] = pack2<T>(__fmul2_rn(d0[m], f2(al0, al0)));
+    out1[m] = pack2<T>(__fmul2_rn(d1[m], f2(al1, al1)));
   }
-  float ss = ss2.x + ss2.y;
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  const float alpha = n == 0.f ? 0.f : n / fmaxf(sqrtf(ss), kEps);
-  if (!isfinite(n) || !isfinite(alpha)) st |= NSNKV_ST_INPUT_NONFINITE;
-#pragma unroll
-  for (int m = 0; m < 16; ++m) out[m] = pack2<T>(__fmul2_rn(d[m], f2(alpha, alpha)));
 }
 
 // Scores of this warp's 16 tokens for the 8 query-head columns: D = K16 q^T.
@@ -182,59 +213,89 @@ __device__ __forceinline__ void qk_mma(const uint32_t (&ka)[16], const uint32_t 
   }
 }
 
-// Softmax update of one 64-token tile for query head g (executed by one warp).
-// p[g][*] holds scaled scores (or -inf for invalid tokens); on exit it holds the
-// unnormalised weights exp(score - m_new); rescale[g] = exp(m_old - m_new).
-__device__ __forceinline__ void softmax_tile(float (&p)[kHeads][kBlock], float *mrun, float *lrun, float *rescale,
-                                             int g, int lane) {
-  constexpr float kLog2e = 1.4426950408889634f;
-  float x0 = p[g][2 * lane], x1 = p[g][2 * lane + 1];
-  float bmax = fmaxf(x0, x1);
+// Write scores (D fragments) of rows t0, t1 for heads 2tig, 2tig+1 < G.
+__device__ __forceinline__ void put_scores(float (&sc)[kHeads][kBlock], const float (&d)[4], int t0, int t1,
+                                           int tig, int G, bool v0, bool v1) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-  const float mold = mrun[g];
-  const float mnew = fmaxf(mold, bmax);
-  float r, p0, p1;
-  if (mnew == -INFINITY) {
-    r = 1.f;
-    p0 = p1 = 0.f;
-  } else {
-    r = exp2f((mold - mnew) * kLog2e);
-    p0 = exp2f((x0 - mnew) * kLog2e);
-    p1 = exp2f((x1 - mnew) * kLog2e);
+  for (int e = 0; e < 2; ++e) {
+    const int n = 2 * tig + e;
+    if (n < G) {
+      sc[n][t0] = v0 ? d[e] * kScale : -INFINITY;
+      sc[n][t1] = v1 ? d[2 + e] * kScale : -INFINITY;
+    }
   }
-  float sum = p0 + p1;
+}
+
+// Online softmax of one tile, per lane: lane (g, tig) owns query head g and the
+// 16 tokens of its P.V B fragments (16ks + 2tig + {0,1,8,9}); the 4 lanes of a
+// head cover all 64 tokens.  Returns the weights and rescales acc (heads 2tig,
+// 2tig+1) to the new running max.  mrun/lrun are this lane's head-g state.
+struct SoftState {
+  float m = -INFINITY, l = 0.f;
+};
+
+__device__ __forceinline__ void softmax_lane(const float (&sc)[kHeads][kBlock], int g, int tig, int G,
+                                             SoftState &ss, float (&p)[16], float (&acc)[2][4], int &st) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  float bmax = -INFINITY;
+  if (g < G) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  p[g][2 * lane] = p0;
-  p[g][2 * lane + 1] = p1;
-  __syncwarp();
-  if (lane == 0) {
-    lrun[g] = lrun[g] * r + sum;
-    mrun[g] = mnew;
-    rescale[g] = r;
+    for (int ks = 0; ks < 4; ++ks) {
+      const float2 a = *reinterpret_cast<const float2 *>(&sc[g][16 * ks + 2 * tig]);
+      const float2 b = *reinterpret_cast<const float2 *>(&sc[g][16 * ks + 2 * tig + 8]);
+      p[4 * ks] = a.x;
+      p[4 * ks + 1] = a.y;
+      p[4 * ks + 2] = b.x;
+      p[4 * ks + 3] = b.y;
+      bmax = fmaxf(bmax, fmaxf(fmaxf(a.x, a.y), fmaxf(b.x, b.y)));
+    }
+  }
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+  const float mnew = fmaxf(ss.m, bmax);
+  float r = 1.f, psum = 0.f;
+  if (g < G && mnew != -INFINITY) {
+    r = exp2f((ss.m - mnew) * kLog2e);
+    const float mb = mnew * kLog2e;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      p[i] = exp2f(fmaf(p[i], kLog2e, -mb));
+      psum += p[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = 0.f;
+  }
+  if (!isfinite(bmax) && bmax != -INFINITY) st |= NSNKV_ST_OUTPUT_NONFINITE;
+  psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+  psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+  ss.l = ss.l * r + psum;
+  ss.m = mnew;
+  // rescale factors of the accumulator columns (heads 2tig, 2tig+1) from their owners
+  const float r0 = __shfl_sync(0xffffffffu, r, 8 * tig);
+  const float r1 = __shfl_sync(0xffffffffu, r, 8 * tig + 4);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    acc[mt][0] *= r0;
+    acc[mt][1] *= r1;
+    acc[mt][2] *= r0;
+    acc[mt][3] *= r1;
   }
 }
 
 // acc[mt] += V^T P for this warp's two 16-channel tiles over the 64 tokens of the tile.
 template <typename T>
-__device__ __forceinline__ void pv_mma(const uint16_t (*v16)[kVRow], const float (&p)[kHeads][kBlock], int G,
-                                       int warp, int lane, float (&acc)[2][4]) {
-  const int g = lane >> 2, tig = lane & 3;
+__device__ __forceinline__ void pv_mma(const uint16_t (*v16)[kVRow], const float (&p)[16], int warp, int lane,
+                                       float (&acc)[2][4]) {
   const int mi = lane >> 3, r = lane & 7;
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
-    const int t0 = 16 * ks + 2 * tig;
-    uint32_t bhi0 = 0, bhi1 = 0, blo0 = 0, blo1 = 0;
-    if (g < G) {
-      const float2 pa = f2(p[g][t0], p[g][t0 + 1]);
-      const float2 pb = f2(p[g][t0 + 8], p[g][t0 + 9]);
-      bhi0 = pack2<T>(pa);
-      bhi1 = pack2<T>(pb);
-      const float2 ha = unpack2<T>(bhi0), hb = unpack2<T>(bhi1);
-      blo0 = pack2<T>(f2(pa.x - ha.x, pa.y - ha.y));
-      blo1 = pack2<T>(f2(pb.x - hb.x, pb.y - hb.y));
-    }
+    const float2 pa = f2(p[4 * ks], p[4 * ks + 1]);
+    const float2 pb = f2(p[4 * ks + 2], p[4 * ks + 3]);
+    const uint32_t bhi0 = pack2<T>(pa), bhi1 = pack2<T>(pb);
+    const float2 ha = unpack2<T>(bhi0), hb = unpack2<T>(bhi1);
+    const uint32_t blo0 = pack2<T>(f2(pa.x - ha.x, pa.y - ha.y));
+    const uint32_t blo1 = pack2<T>(f2(pb.x - hb.x, pb.y - hb.y));
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
       const int cm = 32 * warp + 16 * mt;
@@ -273,25 +334,10 @@ __device__ __forceinline__ void store_row32(uint16_t *dst, const uint32_t (&u)[1
   for (int i = 0; i < 4; ++i) p[i] = make_uint4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
 }
 
-// Write scores (D fragments) of this warp's rows t0, t1 for heads 2tig, 2tig+1 < G.
-__device__ __forceinline__ void put_scores(float (&p)[kHeads][kBlock], const float (&d)[4], int t0, int t1, int tig,
-                                           int G, bool v0, bool v1, int &st) {
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int n = 2 * tig + e;
-    if (n < G) {
-      const float s0 = v0 ? d[e] * kScale : -INFINITY;
-      const float s1 = v1 ? d[2 + e] * kScale : -INFINITY;
-      if ((v0 && !isfinite(s0)) || (v1 && !isfinite(s1))) st |= NSNKV_ST_OUTPUT_NONFINITE;
-      p[n][t0] = s0;
-      p[n][t1] = s1;
-    }
-  }
-}
-
 template <int BITS, typename T>
-__global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArgs a) {
   constexpr int CB = code_bytes(BITS);
+  constexpr float kTwoB = static_cast<float>(1 << BITS);
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS> &S = *reinterpret_cast<AttnSmem<BITS> *>(smem_raw);
 
@@ -322,11 +368,8 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a
     for (int i = 0; i < 16; ++i) bq[i] = 0u;
   }
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  if (tid < kHeads) {
-    S.mrun[tid] = -INFINITY;
-    S.lrun[tid] = 0.f;
-    S.rescale[tid] = 1.f;
-  }
+  SoftState sm;
+  float p[16];
 
   if (!is_raw) {
     const int blk0 = chunk * a.chunk_blocks;
@@ -346,72 +389,57 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a
       bulk_g2s(sg.vs, a.vs + bi * kDim, kDim * 2, &S.full[s]);
     };
     if (tid == 0) {
-      mbar_init(&S.full[0], 1);
-      mbar_init(&S.full[1], 1);
+#pragma unroll
+      for (int i = 0; i < kStages; ++i) mbar_init(&S.full[i], 1);
       fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-      issue(blk0, 0);
-      if (nloc > 1) issue(blk0 + 1, 1);
-    }
+    if (tid == 0)
+      for (int i = 0; i < kStages && i < nloc; ++i) issue(blk0 + i, i);
     for (int li = 0; li < nloc; ++li) {
-      const int s = li & 1;
-      const bool ok = mbar_wait_bounded(&S.full[s], (li >> 1) & 1, a.status);
+      const int s = li % kStages;
+      const bool ok = mbar_wait_bounded(&S.full[s], (li / kStages) & 1, a.status);
       if (__syncthreads_or(!ok)) {
-        // A staged copy never landed: give the other stage's copy (if issued) a
-        // bounded chance to finish, then leave; the timeout status tells the host.
-        if (tid == 0 && li + 1 < nloc) mbar_wait_bounded(&S.full[s ^ 1], ((li + 1) >> 1) & 1, a.status);
+        // A staged copy never landed: give the later copies a bounded chance to
+        // finish, then leave; the timeout status tells the host.
+        if (tid == 0)
+          for (int k = li + 1; k < nloc && k < li + kStages; ++k)
+            mbar_wait_bounded(&S.full[k % kStages], (k / kStages) & 1, a.status);
         return;
       }
       const Stage<BITS> &sg = S.stage[s];
-      float2 m2[16], s2[16];
-      // ---- K phase: restore + round this lane's two rows, scores by MMA
+      MetaF &mf = S.meta[li & 1];
+      {  // metadata of this block -> fp32 (a, b) pairs, one channel per thread
+        const int c = tid, ci = meta_index(c);
+        const float km = half_bits_to_f(sg.km[c]), ks = half_bits_to_f(sg.ks[c]);
+        const float vm = half_bits_to_f(sg.vm[c]), vs = half_bits_to_f(sg.vs[c]);
+        const float kb = ks * kTwoB, vb = vs * kTwoB;
+        mf.ka[ci] = km - kb;
+        mf.kb[ci] = kb;
+        mf.va[ci] = vm - vb;
+        mf.vb[ci] = vb;
+        bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
+        if (c < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[c])) || !isfinite(half_bits_to_f(sg.vn[c]));
+        if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
+      }
+      __syncthreads();
       {
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          m2[m] = __half22float2(*reinterpret_cast<const __half2 *>(&sg.km[cbase + 2 * m]));
-          s2[m] = __half22float2(*reinterpret_cast<const __half2 *>(&sg.ks[cbase + 2 * m]));
-          if (!finite2(m2[m]) || !finite2(s2[m])) st |= NSNKV_ST_INPUT_NONFINITE;
-        }
         uint32_t ka[16], kb[16];
-        restore_row<BITS, T>(sg.kc, t0, cbase, m2, s2, half_bits_to_f(sg.kn[t0]), ka, st);
-        restore_row<BITS, T>(sg.kc, t1, cbase, m2, s2, half_bits_to_f(sg.kn[t1]), kb, st);
+        restore_rows<BITS, T>(sg.kc, mf.ka, mf.kb, t0, t1, cbase, half_bits_to_f(sg.kn[t0]),
+                              half_bits_to_f(sg.kn[t1]), ka, kb);
         float d[4];
         qk_mma<T>(ka, kb, bq, d);
-        put_scores(S.p, d, t0, t1, tig, G, true, true, st);
-      }
-      // ---- V rows: restore + round into the shared V tile
-      {
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          m2[m] = __half22float2(*reinterpret_cast<const __half2 *>(&sg.vm[cbase + 2 * m]));
-          s2[m] = __half22float2(*reinterpret_cast<const __half2 *>(&sg.vs[cbase + 2 * m]));
-          if (!finite2(m2[m]) || !finite2(s2[m])) st |= NSNKV_ST_INPUT_NONFINITE;
-        }
-        uint32_t va[16];
-        restore_row<BITS, T>(sg.vc, t0, cbase, m2, s2, half_bits_to_f(sg.vn[t0]), va, st);
-        store_row32(&S.v16[t0][cbase], va);
-        restore_row<BITS, T>(sg.vc, t1, cbase, m2, s2, half_bits_to_f(sg.vn[t1]), va, st);
-        store_row32(&S.v16[t1][cbase], va);
+        put_scores(S.sc, d, t0, t1, tig, G, true, true);
+        restore_rows<BITS, T>(sg.vc, mf.va, mf.vb, t0, t1, cbase, half_bits_to_f(sg.vn[t0]),
+                              half_bits_to_f(sg.vn[t1]), ka, kb);
+        store_row32(&S.v16[t0][cbase], ka);
+        store_row32(&S.v16[t1][cbase], kb);
       }
       __syncthreads();
-      if (2 * warp < G) softmax_tile(S.p, S.mrun, S.lrun, S.rescale, 2 * warp, lane);
-      if (2 * warp + 1 < G) softmax_tile(S.p, S.mrun, S.lrun, S.rescale, 2 * warp + 1, lane);
-      __syncthreads();
-      {
-        const float r0 = S.rescale[2 * tig], r1 = S.rescale[2 * tig + 1];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          acc[mt][0] *= r0;
-          acc[mt][1] *= r1;
-          acc[mt][2] *= r0;
-          acc[mt][3] *= r1;
-        }
-        pv_mma<T>(S.v16, S.p, G, warp, lane, acc);
-      }
-      __syncthreads();
-      if (tid == 0 && li + 2 < nloc) issue(blk0 + li + 2, s);
+      // stage s is consumed: refill it with block li + kStages
+      if (tid == 0 && li + kStages < nloc) issue(blk0 + li + kStages, s);
+      softmax_lane(S.sc, g, tig, G, sm, p, acc, st);
+      pv_mma<T>(S.v16, p, warp, lane, acc);
     }
   } else {
     // ---- native rows (tail, appended token, or materialised K/V), 64-token tiles
@@ -423,7 +451,6 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a
     const int raw1 = min(tail_total, raw0 + raw_per_chunk);
     const bool can_store = tl < a.tsh;
     if (a.knew && !can_store && tl >= raw0 && tl < raw1 && tid == 0) st |= NSNKV_ST_CAPACITY;
-    __syncthreads();
     const int ntiles = (raw1 - raw0 + kBlock - 1) / kBlock;
     for (int tile = 0; tile < ntiles; ++tile) {
       const int j0 = raw0 + tile * kBlock + t0, j1 = raw0 + tile * kBlock + t1;
@@ -455,27 +482,15 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a
           store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(vtb) + static_cast<int64_t>(j1) * kDim) + cbase, vb);
         }
       }
+      if (tile > 0) __syncthreads();  // previous tile's P.V has finished reading sc / v16
       float d[4];
       qk_mma<T>(ka, kb, bq, d);
-      put_scores(S.p, d, t0, t1, tig, G, v0, v1, st);
+      put_scores(S.sc, d, t0, t1, tig, G, v0, v1);
       store_row32(&S.v16[t0][cbase], va);
       store_row32(&S.v16[t1][cbase], vb);
       __syncthreads();
-      if (2 * warp < G) softmax_tile(S.p, S.mrun, S.lrun, S.rescale, 2 * warp, lane);
-      if (2 * warp + 1 < G) softmax_tile(S.p, S.mrun, S.lrun, S.rescale, 2 * warp + 1, lane);
-      __syncthreads();
-      {
-        const float r0 = S.rescale[2 * tig], r1 = S.rescale[2 * tig + 1];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          acc[mt][0] *= r0;
-          acc[mt][1] *= r1;
-          acc[mt][2] *= r0;
-          acc[mt][3] *= r1;
-        }
-        pv_mma<T>(S.v16, S.p, G, warp, lane, acc);
-      }
-      __syncthreads();
+      softmax_lane(S.sc, g, tig, G, sm, p, acc, st);
+      pv_mma<T>(S.v16, p, warp, lane, acc);
     }
   }
 
@@ -493,10 +508,10 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const AttnArgs a
       }
     }
   }
-  if (tid < G) {
-    const int64_t row = (b * a.hq + h * G + tid) * a.max_chunks + chunk;
-    a.part_ml[row * 2] = S.mrun[tid];
-    a.part_ml[row * 2 + 1] = S.lrun[tid];
+  if (warp == 0 && tig == 0 && g < G) {
+    const int64_t row = (b * a.hq + h * G + g) * a.max_chunks + chunk;
+    a.part_ml[row * 2] = sm.m;
+    a.part_ml[row * 2 + 1] = sm.l;
   }
   if (st) set_status(a.status, st);
 }
@@ -561,12 +576,12 @@ __global__ void __launch_bounds__(128) merge_shards_kernel(int n_shards, int64_t
 static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t max_tail) {
   // Aim for >= 4 CTAs per SM (148 SMs) while keeping the partials small.
   const int64_t units = batch * h;
-  const int64_t target = 148 * 4;
+  const int64_t target = 148 * 12;
   const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
   int64_t per_unit = (target + units - 1) / units;  // desired chunks per (seq, head)
   int64_t ch = (work + per_unit - 1) / per_unit;
   if (ch < 4) ch = 4;
-  if (ch > 64) ch = 64;
+  if (ch > 16) ch = 16;
   return static_cast<int>(ch);
 }
 
