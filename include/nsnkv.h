@@ -142,6 +142,40 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
 int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t max_blocks, int32_t max_tail);
 
 /*
+ * nsnkv_decode_attn without a workspace argument, for callers that cannot allocate
+ * device memory: code running where cudaMalloc is not allowed or not wanted (a
+ * serving loop that must not call into the allocator or implicitly synchronise the
+ * device, a host runtime without access to the framework's caching allocator, an
+ * embedding that owns all device memory itself).  This entry point has no
+ * counterpart in the reference.
+ *
+ * Arguments and results are those of nsnkv_decode_attn minus workspace /
+ * workspace_bytes.  The split-KV partials live in a fixed device array of
+ * NSNKV_NOALLOC_SCRATCH_BYTES (16 MiB) compiled into the library; every GPU that
+ * loads the library holds it until the process exits.  Requests whose
+ * nsnkv_decode_attn_workspace_bytes() exceed it return NSNKV_ERR_TOO_LARGE
+ * (e.g. batch 64 x 32 query heads x 16k-token contexts does not fit; one 32k-token
+ * sequence does).  The first call on each device looks up the array's device
+ * address with that device current (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  No call allocates (no cudaMalloc/cudaFree or any
+ * allocating library routine).  All calls share the array and it keeps the last
+ * call's contents; nothing in it needs to start at zero, but calls that overlap on
+ * the GPU (for example on two streams of the same device) race on it.
+ */
+#define NSNKV_NOALLOC_SCRATCH_BYTES (16ll << 20)
+int nsnkv_decode_attn_noalloc(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
+                              const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
+                              const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
+                              const uint16_t *v_min, const uint16_t *v_scale,
+                              int64_t blk_stride_head, int64_t blk_stride_page,
+                              const int32_t *block_table, int64_t table_stride,
+                              const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                              void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                              const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail,
+                              const void *k_new, const void *v_new,
+                              void *out, float *out_f32, float *lse, int32_t *status, void *stream);
+
+/*
  * Seal full tails of a paged cache: for every sequence b whose tail holds
  * 64 tokens (after an append), encode the 64x128 tail of each kv head into
  * page block_table[b*table_stride + n_blocks[b]] of the K and V pools, then set

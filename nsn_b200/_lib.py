@@ -20,6 +20,7 @@ ERR_LAUNCH = -2
 ERR_UNSUPPORTED = -3
 ERR_CUDA = -4
 ERR_TOO_LARGE = -5
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 ST_INPUT_NONFINITE = 1
 ST_META_OVERFLOW = 2
@@ -49,6 +50,13 @@ SIGNATURES = [
                                   P, c_int32, c_int32,
                                   P, P, P, P, P, P, c_int64, P, P]),
     ("nsnkv_decode_attn_workspace_bytes", c_int64, [c_int64, c_int, c_int, c_int32, c_int32]),
+    ("nsnkv_decode_attn_noalloc", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
+                                          P, P, P, P, P, P, P, P,
+                                          c_int64, c_int64, P, c_int64,
+                                          P, c_int32, c_int32,
+                                          P, P, c_int64, c_int64,
+                                          P, c_int32, c_int32,
+                                          P, P, P, P, P, P, P]),
     ("nsnkv_seal_full_tails", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P, c_int64,
                                       P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),

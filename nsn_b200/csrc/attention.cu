@@ -21,6 +21,8 @@
 // Native rows (the tail, an appended token, or fully materialised K/V) use the same
 // code without the unpack.  A merge kernel combines chunk partials with a
 // log-sum-exp reduction (the reference's merge, loop_kv_af01_kernel.py:70-84).
+#include <mutex>
+
 #include "nsnkv_common.cuh"
 
 namespace nsnkv {
@@ -716,3 +718,56 @@ int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------- allocation-free variant
+// Scratch for nsnkv_decode_attn_noalloc: the split-KV partials live in this fixed,
+// file-scope device array instead of a caller-provided workspace.  Every GPU that
+// loads the library holds NSNKV_NOALLOC_SCRATCH_BYTES of it until the process exits.
+// In host code `g_noalloc_scratch` is only a host-side stand-in for the symbol, not a
+// device address; the device address is obtained once per device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NSNKV_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void *g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up on the first
+// call for that device (with that device current) and cached afterwards.
+int noalloc_scratch(void **out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return NSNKV_ERR_CUDA;
+  if (dev >= kMaxDevices) return NSNKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[dev]) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return NSNKV_ERR_CUDA;
+    g_scratch_address[dev] = ptr;
+  }
+  *out = g_scratch_address[dev];
+  return NSNKV_OK;
+}
+}  // namespace
+
+extern "C" int nsnkv_decode_attn_noalloc(
+    int64_t batch, int hq, int h, int bits, int dtype, const void *q, const uint8_t *k_codes, const uint16_t *k_norm,
+    const uint16_t *k_min, const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
+    const uint16_t *v_min, const uint16_t *v_scale, int64_t blk_stride_head, int64_t blk_stride_page,
+    const int32_t *block_table, int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const,
+    int32_t max_blocks, void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+    const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new,
+    void *out, float *out_f32, float *lse, int32_t *status, void *stream) {
+  const int64_t need = nsnkv_decode_attn_workspace_bytes(batch, hq, h, max_blocks, max_tail);
+  if (need <= 0) return NSNKV_ERR_ARG;
+  if (need > NSNKV_NOALLOC_SCRATCH_BYTES) return NSNKV_ERR_TOO_LARGE;
+  void *scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != NSNKV_OK) return rc;
+  // The partials need no clearing: every entry the merge reads is written earlier in
+  // the same call.  Calls that overlap on the GPU share the array and race.
+  return nsnkv_decode_attn(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
+                           v_scale, blk_stride_head, blk_stride_page, block_table, table_stride, n_blocks,
+                           n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
+                           tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, scratch,
+                           NSNKV_NOALLOC_SCRATCH_BYTES, status, stream);
+}
