@@ -1,0 +1,99 @@
+"""Sequence-split (split-KV) decode across GPUs with a log-sum-exp merge.
+
+For one long sequence (cfg4: 2047 INT5 blocks + 64-token tail, GQA 64:8), rank r
+of N holds a contiguous range of sealed blocks (the last rank also holds the
+native tail).  Each rank runs the fused attention over its range and keeps the
+fp32 context and the log-sum-exp of its scores per query head; the (o, lse)
+rows of all ranks are all-gathered (NCCL over NVLink / NVSwitch, about 33 KB per
+rank at cfg4) and combined by ``nsnkv_merge_shards``:
+
+    L = log sum_r exp(lse_r),  out = sum_r exp(lse_r - L) * o_r.
+
+This is the reference's intra-GPU tile merge (experiments/ac08/source/
+loop_kv_af01_kernel.py:70-84) lifted across GPUs.  The data path has no other
+exchange; no TMA load ever reads another GPU's memory.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from . import primitives as w
+from .kernel import decode_attention, group_pool
+
+
+def shard_range(n_blocks: int, world: int, rank: int):
+    """Contiguous, balanced block range [start, end) of `rank` (every rank gets >= 1 block if n_blocks >= world)."""
+    base, extra = divmod(n_blocks, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def gather_partials(o: torch.Tensor, lse: torch.Tensor, group=None):
+    """All-gather per-rank (o [rows,128] fp32, lse [rows] fp32) -> ([N,rows,128], [N,rows])."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    o = o.contiguous()
+    lse = lse.contiguous()
+    # concatenated along dim 0 (the layout every backend accepts), viewed as [N, rows, ...]
+    O = torch.empty((world * o.shape[0],) + tuple(o.shape[1:]), dtype=o.dtype, device=o.device)
+    S = torch.empty((world * lse.shape[0],), dtype=lse.dtype, device=lse.device)
+    dist.all_gather_into_tensor(O, o, group=group)
+    dist.all_gather_into_tensor(S, lse, group=group)
+    return O.view((world,) + tuple(o.shape)), S.view(world, lse.shape[0])
+
+
+def merge_shards(O: torch.Tensor, S: torch.Tensor, dtype=torch.float16, out=None, out_f32=None, lse_out=None,
+                 status=None):
+    """Combine gathered partials on the GPU with nsnkv_merge_shards."""
+    L.require_cuda()
+    n, rows = S.shape[0], S.shape[1]
+    dev = O.device
+    if out is None:
+        out = torch.empty((rows, 128), dtype=dtype, device=dev)
+    if status is None:
+        status = L.status_tensor(dev)
+    L.check(L.load().nsnkv_merge_shards(n, rows, L.ptr(O), L.ptr(S), L.DTYPE_CODE[dtype], L.ptr(out),
+                                        L.ptr(out_f32), L.ptr(lse_out), L.ptr(status), L.stream_handle(dev)),
+            "nsnkv_merge_shards")
+    return out, status
+
+
+class ShardedSequence:
+    """One rank's share of a long sequence: its block range of K/V (reference group
+    layout [1, h, n_r, ...]) plus, on the last rank, the native tail."""
+
+    def __init__(self, k_group, v_group, k_tail, v_tail, h, hq, bits):
+        self.kg, self.vg = k_group, v_group
+        self.kt, self.vt = k_tail, v_tail
+        self.h, self.hq, self.bits = h, hq, bits
+        self.n = 0 if k_group is None else k_group["codes"].shape[2]
+        self.t = 0 if k_tail is None else k_tail.shape[2]
+        dev = (k_group["codes"] if k_group is not None else k_tail).device
+        self.o = torch.empty((hq, 128), dtype=torch.float32, device=dev)
+        self.lse = torch.empty((hq,), dtype=torch.float32, device=dev)
+        self.status = L.status_tensor(dev)
+
+    def local(self, q):
+        """Fused attention over this rank's share -> fp32 (o, lse) per query head."""
+        out = torch.empty((1, self.hq, 128), dtype=q.dtype, device=q.device)
+        decode_attention(q.reshape(1, self.hq, 128), group_pool(self.kg, self.h) if self.n else None,
+                         group_pool(self.vg, self.h) if self.n else None, h=self.h, bits=self.bits,
+                         blk_stride_head=self.n, blk_stride_page=1, n_blocks=self.n, max_blocks=self.n,
+                         k_tail=self.kt if self.t else None, v_tail=self.vt if self.t else None,
+                         tail_stride_seq=self.h * self.t, tail_stride_head=self.t, tail_len=self.t, max_tail=self.t,
+                         out=out, out_f32=self.o.reshape(1, self.hq, 128), lse=self.lse.reshape(1, self.hq),
+                         status=self.status)
+        return self.o, self.lse
+
+    def decode(self, q, group=None, out=None):
+        """Split-KV decode of q [1, hq, 1, 128]: local partials, all-gather, merge."""
+        o, lse = self.local(q)
+        O, S = gather_partials(o, lse, group)
+        res, _ = merge_shards(O, S, dtype=q.dtype, out=out, status=self.status)
+        return res
+
+    def check(self):
+        st = int(self.status.item())
+        if st:
+            w._status_to_error(st, "Nonfinite decode input", output_msg="Nonfinite decode output")
