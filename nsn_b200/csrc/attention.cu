@@ -52,8 +52,9 @@ struct AttnArgs {
   int32_t *status;
 };
 
-constexpr int kThreads = 128;    // 4 warps: 4 x 16 tokens of a 64-token block
-constexpr int kHeads = 8;        // MMA N: query heads per kv head (G <= 8)
+constexpr int kThreads = 128;    // 4 warps; warp w owns tokens 16w..16w+15 of every block
+constexpr int kWarps = kThreads / 32;
+constexpr int kHeads = 8;        // MMA rows/columns for the query heads of one kv head (G <= 8)
 constexpr int kVRow = kDim + 8;  // padded V tile row (272 B): ldmatrix rows hit distinct banks
 constexpr int kStages = 4;       // TMA ring depth (blocks in flight per CTA)
 constexpr int kMetaRow = kDim + kDim / 8;  // fp32 metadata row padded every 32 channels by 4 floats
@@ -70,24 +71,40 @@ struct Stage {
   uint16_t vs[kDim];
 };
 
-// Per-block fp32 metadata in the form the restore uses: with x = 1 + code * 2^-BITS
-// (the code dropped into the top mantissa bits of 1.0f),
-//   d = min + scale*code = b*x + a,  b = scale * 2^BITS,  a = min - b.
+// Per-block fp32 metadata in the form the restore uses.  A code k is dropped into
+// mantissa bits [p, p+BITS) of 1.0f, giving x = 1 + k*2^(p-23); then
+//   d = min + scale*k = b*x + a,   b = scale * 2^(23-p),   a = min - b.
 struct MetaF {
   float ka[kMetaRow], kb[kMetaRow], va[kMetaRow], vb[kMetaRow];
+};
+
+struct MergeSmem {  // cross-warp combine at the end of a chunk (aliases the V tiles)
+  float acc[kWarps][kHeads][kDim];
+  float m[kWarps][kHeads];
+  float l[kWarps][kHeads];
 };
 
 template <int BITS>
 struct AttnSmem {
   Stage<BITS> stage[kStages];
   MetaF meta[2];
-  uint16_t v16[kBlock][kVRow];  // restored V tile in the bridge dtype
-  float sc[kHeads][kBlock];     // scores of the current tile
+  union {
+    uint16_t v16[kWarps][16][kVRow];  // each warp's restored V rows (bridge dtype)
+    MergeSmem merge;
+  } u;
   uint64_t full[kStages];
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ int meta_index(int c) { return c + (c >> 5) * 4; }
+
+// Mantissa position of code j (0..31 within a lane's 32-channel group).  INT3 codes
+// are handled in pairs: one shift puts code 2m at bits 17..19 and code 2m+1 at
+// 20..22, and two masks turn them into two floats.
+template <int BITS>
+__host__ __device__ constexpr int code_pos(int j) {
+  return BITS == 3 ? ((j & 1) ? 20 : 17) : 23 - BITS;
+}
 
 // Round a float pair to the bridge dtype and pack it (low half = .x).
 template <typename T> __device__ __forceinline__ uint32_t pack2(float2 v);
@@ -102,23 +119,25 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float2 v) {
 template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t u) { return Elem<T>::to_f2(u); }
 
 template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
 template <>
-__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                                        uint32_t b1) {
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *smem_row) {
@@ -130,49 +149,67 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *
 
 __device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
 
-// Load the packed bits of this lane's 32 channels of token t, aligned so that
-// channel j's code starts at bit BITS*j of the returned word array.
+// The packed codes of one lane's 32 channels of one token row.  A row is 4*BITS
+// words and a lane's group BITS words, so the group is always word aligned.
 template <int BITS>
-struct RowBits {
-  static constexpr int kWords = (BITS * 32 + 31) / 32;
-  uint32_t w[kWords + 1];
-  __device__ __forceinline__ void load(const uint8_t *codes, int t, int cbase) {
-    const int bitoff = BITS * (t * kDim + cbase);
-    const uint32_t *p = reinterpret_cast<const uint32_t *>(codes) + (bitoff >> 5);
-    const int sh = bitoff & 31;
-    uint32_t raw[kWords + 2];
+struct RowCodes {
+  uint32_t w[BITS];
+  __device__ __forceinline__ void load(const uint8_t *codes, int t, int tig) {
+    const uint32_t *p = reinterpret_cast<const uint32_t *>(codes) + t * 4 * BITS + tig * BITS;
 #pragma unroll
-    for (int i = 0; i < kWords + 1; ++i) raw[i] = p[i];
-    raw[kWords + 1] = 0;
-#pragma unroll
-    for (int i = 0; i < kWords + 1; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+    for (int i = 0; i < BITS; ++i) w[i] = p[i];
   }
-  // x_j = 1 + code_j * 2^-BITS as a float: the code placed in the top BITS mantissa bits.
-  __device__ __forceinline__ float x(int j) const {
-    constexpr int kTop = 23 - BITS;
-    const int pos = BITS * j, wi = pos >> 5, bi = pos & 31;
-    uint32_t v;
-    if (bi + BITS <= 32) {
-      v = kTop >= bi ? (w[wi] << (kTop - bi)) : (w[wi] >> (bi - kTop));
-    } else {
-      v = __funnelshift_r(w[wi], w[wi + 1], bi) << kTop;
+  // The group's bits moved so that bit `pos` lands at bit `dst` (both compile-time).
+  __device__ __forceinline__ uint32_t place(int pos, int dst) const {
+    const int wi = pos >> 5, bi = pos & 31;
+    if (bi == dst) return w[wi];
+    if (bi > dst) return __funnelshift_r(w[wi], wi + 1 < BITS ? w[wi + 1] : 0u, bi - dst);
+    return __funnelshift_l(wi > 0 ? w[wi - 1] : 0u, w[wi], dst - bi);
+  }
+  // x for codes 2m and 2m+1 (see MetaF).
+  __device__ __forceinline__ float2 xpair(int m) const {
+    if (BITS == 3) {
+      const uint32_t ws = place(6 * m, 17);
+      return f2(__uint_as_float((ws & 0x000E0000u) | 0x3F800000u), __uint_as_float((ws & 0x00700000u) | 0x3F800000u));
     }
-    return __uint_as_float((v & (((1u << BITS) - 1u) << kTop)) | 0x3F800000u);
+    constexpr int p = 23 - BITS;
+    constexpr uint32_t mask = ((1u << BITS) - 1u) << p;
+    const uint32_t w0 = place(BITS * 2 * m, p), w1 = place(BITS * (2 * m + 1), p);
+    return f2(__uint_as_float((w0 & mask) | 0x3F800000u), __uint_as_float((w1 & mask) | 0x3F800000u));
   }
 };
 
-// Restore rows t0 and t1 (this lane's 32 channels each) of a staged block and
-// round them to the bridge dtype: out*[m] packs channels cbase+2m, cbase+2m+1.
-template <int BITS, typename T>
-__device__ __forceinline__ void restore_rows(const uint8_t *codes, const float *ma, const float *mb, int t0, int t1,
-                                             int cbase, float n0, float n1, uint32_t (&out0)[16],
-                                             uint32_t (&out1)[16]) {
-  RowBits<BITS> r0, r1;
-  r0.load(codes, t0, cbase);
-  r1.load(codes, t1, cbase);
-  float2 d0[16], d1[16];
+// d for this lane's 32 channels of one row, plus the full-row sum of squares.
+template <int BITS>
+__device__ __forceinline__ float row_dirs(const RowCodes<BITS> &rc, const float *ma, const float *mb, int mi,
+                                          float2 (&d)[16]) {
   float2 ss0 = f2(0.f, 0.f), ss1 = f2(0.f, 0.f);
-  const int mi = meta_index(cbase);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 a4 = *reinterpret_cast<const float4 *>(&ma[mi + 4 * q]);
+    const float4 b4 = *reinterpret_cast<const float4 *>(&mb[mi + 4 * q]);
+    d[2 * q] = __ffma2_rn(f2(b4.x, b4.y), rc.xpair(2 * q), f2(a4.x, a4.y));
+    d[2 * q + 1] = __ffma2_rn(f2(b4.z, b4.w), rc.xpair(2 * q + 1), f2(a4.z, a4.w));
+    ss0 = __ffma2_rn(d[2 * q], d[2 * q], ss0);
+    ss1 = __ffma2_rn(d[2 * q + 1], d[2 * q + 1], ss1);
+  }
+  float s = (ss0.x + ss1.x) + (ss0.y + ss1.y);
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  return s;
+}
+
+// Restore two rows (this lane's 32 channels of tokens t0 and t1) with their work
+// interleaved, renormalise and round to the bridge dtype: out0/out1 pack channel pairs.
+template <int BITS, typename T>
+__device__ __forceinline__ void restore_two_rows(const uint8_t *codes, const float *ma, const float *mb, int mi,
+                                                 int t0, int t1, int tig, float n0, float n1, uint32_t (&out0)[16],
+                                                 uint32_t (&out1)[16]) {
+  RowCodes<BITS> r0, r1;
+  r0.load(codes, t0, tig);
+  r1.load(codes, t1, tig);
+  float2 d0[16], d1[16];
+  float2 s0 = f2(0.f, 0.f), s1 = f2(0.f, 0.f);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const float4 a4 = *reinterpret_cast<const float4 *>(&ma[mi + 4 * q]);
@@ -182,20 +219,19 @@ __device__ __forceinline__ void restore_rows(const uint8_t *codes, const float *
       const int m = 2 * q + e;
       const float2 a2 = e ? f2(a4.z, a4.w) : f2(a4.x, a4.y);
       const float2 b2 = e ? f2(b4.z, b4.w) : f2(b4.x, b4.y);
-      d0[m] = __ffma2_rn(b2, f2(r0.x(2 * m), r0.x(2 * m + 1)), a2);
-      d1[m] = __ffma2_rn(b2, f2(r1.x(2 * m), r1.x(2 * m + 1)), a2);
-      ss0 = __ffma2_rn(d0[m], d0[m], ss0);
-      ss1 = __ffma2_rn(d1[m], d1[m], ss1);
+      d0[m] = __ffma2_rn(b2, r0.xpair(m), a2);
+      d1[m] = __ffma2_rn(b2, r1.xpair(m), a2);
+      s0 = __ffma2_rn(d0[m], d0[m], s0);
+      s1 = __ffma2_rn(d1[m], d1[m], s1);
     }
   }
-  float s0 = ss0.x + ss0.y, s1 = ss1.x + ss1.y;
-  s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-  s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-  s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-  s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-  // norm / max(||d||, eps); the eps clamp only matters for an all-zero direction
-  const float al0 = n0 == 0.f ? 0.f : (s0 > 1e-24f ? n0 * rsqrtf(s0) : n0 * 1e12f);
-  const float al1 = n1 == 0.f ? 0.f : (s1 > 1e-24f ? n1 * rsqrtf(s1) : n1 * 1e12f);
+  float ss0 = s0.x + s0.y, ss1 = s1.x + s1.y;
+  ss0 += __shfl_xor_sync(0xffffffffu, ss0, 1);
+  ss1 += __shfl_xor_sync(0xffffffffu, ss1, 1);
+  ss0 += __shfl_xor_sync(0xffffffffu, ss0, 2);
+  ss1 += __shfl_xor_sync(0xffffffffu, ss1, 2);
+  const float al0 = n0 == 0.f ? 0.f : (ss0 > 1e-24f ? n0 * rsqrtf(ss0) : n0 * 1e12f);
+  const float al1 = n1 == 0.f ? 0.f : (ss1 > 1e-24f ? n1 * rsqrtf(ss1) : n1 * 1e12f);
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
     out0[m] = pack2<T>(__fmul2_rn(d0[m], f2(al0, al0)));
@@ -203,110 +239,9 @@ __device__ __forceinline__ void restore_rows(const uint8_t *codes, const float *
   }
 }
 
-// Scores of this warp's 16 tokens for the 8 query-head columns: D = K16 q^T.
-template <typename T>
-__device__ __forceinline__ void qk_mma(const uint32_t (&ka)[16], const uint32_t (&kb)[16], const uint32_t (&bq)[16],
-                                       float (&d)[4]) {
-  d[0] = d[1] = d[2] = d[3] = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t a[4] = {ka[2 * j], kb[2 * j], ka[2 * j + 1], kb[2 * j + 1]};
-    mma16816<T>(d, a, bq[2 * j], bq[2 * j + 1]);
-  }
-}
-
-// Write scores (D fragments) of rows t0, t1 for heads 2tig, 2tig+1 < G.
-__device__ __forceinline__ void put_scores(float (&sc)[kHeads][kBlock], const float (&d)[4], int t0, int t1,
-                                           int tig, int G, bool v0, bool v1) {
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int n = 2 * tig + e;
-    if (n < G) {
-      sc[n][t0] = v0 ? d[e] * kScale : -INFINITY;
-      sc[n][t1] = v1 ? d[2 + e] * kScale : -INFINITY;
-    }
-  }
-}
-
-// Online softmax of one tile, per lane: lane (g, tig) owns query head g and the
-// 16 tokens of its P.V B fragments (16ks + 2tig + {0,1,8,9}); the 4 lanes of a
-// head cover all 64 tokens.  Returns the weights and rescales acc (heads 2tig,
-// 2tig+1) to the new running max.  mrun/lrun are this lane's head-g state.
-struct SoftState {
-  float m = -INFINITY, l = 0.f;
-};
-
-__device__ __forceinline__ void softmax_lane(const float (&sc)[kHeads][kBlock], int g, int tig, int G,
-                                             SoftState &ss, float (&p)[16], float (&acc)[2][4], int &st) {
-  constexpr float kLog2e = 1.4426950408889634f;
-  float bmax = -INFINITY;
-  if (g < G) {
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const float2 a = *reinterpret_cast<const float2 *>(&sc[g][16 * ks + 2 * tig]);
-      const float2 b = *reinterpret_cast<const float2 *>(&sc[g][16 * ks + 2 * tig + 8]);
-      p[4 * ks] = a.x;
-      p[4 * ks + 1] = a.y;
-      p[4 * ks + 2] = b.x;
-      p[4 * ks + 3] = b.y;
-      bmax = fmaxf(bmax, fmaxf(fmaxf(a.x, a.y), fmaxf(b.x, b.y)));
-    }
-  }
-  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
-  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
-  const float mnew = fmaxf(ss.m, bmax);
-  float r = 1.f, psum = 0.f;
-  if (g < G && mnew != -INFINITY) {
-    r = exp2f((ss.m - mnew) * kLog2e);
-    const float mb = mnew * kLog2e;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      p[i] = exp2f(fmaf(p[i], kLog2e, -mb));
-      psum += p[i];
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) p[i] = 0.f;
-  }
-  if (!isfinite(bmax) && bmax != -INFINITY) st |= NSNKV_ST_OUTPUT_NONFINITE;
-  psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-  psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-  ss.l = ss.l * r + psum;
-  ss.m = mnew;
-  // rescale factors of the accumulator columns (heads 2tig, 2tig+1) from their owners
-  const float r0 = __shfl_sync(0xffffffffu, r, 8 * tig);
-  const float r1 = __shfl_sync(0xffffffffu, r, 8 * tig + 4);
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    acc[mt][0] *= r0;
-    acc[mt][1] *= r1;
-    acc[mt][2] *= r0;
-    acc[mt][3] *= r1;
-  }
-}
-
-// acc[mt] += V^T P for this warp's two 16-channel tiles over the 64 tokens of the tile.
-template <typename T>
-__device__ __forceinline__ void pv_mma(const uint16_t (*v16)[kVRow], const float (&p)[16], int warp, int lane,
-                                       float (&acc)[2][4]) {
-  const int mi = lane >> 3, r = lane & 7;
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-    const float2 pa = f2(p[4 * ks], p[4 * ks + 1]);
-    const float2 pb = f2(p[4 * ks + 2], p[4 * ks + 3]);
-    const uint32_t bhi0 = pack2<T>(pa), bhi1 = pack2<T>(pb);
-    const float2 ha = unpack2<T>(bhi0), hb = unpack2<T>(bhi1);
-    const uint32_t blo0 = pack2<T>(f2(pa.x - ha.x, pa.y - ha.y));
-    const uint32_t blo1 = pack2<T>(f2(pb.x - hb.x, pb.y - hb.y));
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const int cm = 32 * warp + 16 * mt;
-      uint32_t a[4];
-      ldmatrix_x4_trans(a, &v16[16 * ks + r + 8 * (mi >> 1)][cm + 8 * (mi & 1)]);
-      mma16816<T>(acc[mt], a, bhi0, bhi1);
-      mma16816<T>(acc[mt], a, blo0, blo1);
-    }
-  }
+// norm / max(||d||, eps) from the row sum of squares (0 when the stored norm is 0).
+__device__ __forceinline__ float renorm(float n, float ss) {
+  return n == 0.f ? 0.f : (ss > 1e-24f ? n * rsqrtf(ss) : n * 1e12f);
 }
 
 template <typename T>
@@ -330,21 +265,108 @@ __device__ __forceinline__ int check_row32(const uint32_t (&u)[16]) {
   return bad ? NSNKV_ST_INPUT_NONFINITE : 0;
 }
 
+// Round 32 floats (16 pairs) to the bridge dtype and store them as 64 contiguous bytes.
+template <typename T>
+__device__ __forceinline__ void store_pairs(uint16_t *dst, const float2 (&d)[16]) {
+  uint4 *p = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    p[i] = make_uint4(pack2<T>(d[4 * i]), pack2<T>(d[4 * i + 1]), pack2<T>(d[4 * i + 2]), pack2<T>(d[4 * i + 3]));
+}
+
 __device__ __forceinline__ void store_row32(uint16_t *dst, const uint32_t (&u)[16]) {
   uint4 *p = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
   for (int i = 0; i < 4; ++i) p[i] = make_uint4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
 }
 
+// Per-warp online softmax state and accumulator.  Lane (g, tig) owns query head g
+// (m, l) and the accumulator of channels 16mt + {g, g+8}, heads 2tig, 2tig+1.
+struct WarpState {
+  float m = -INFINITY, l = 0.f;
+  float acc[8][4];
+};
+
+// Scores of this warp's 16-token tile for query head g, from one K row (n-tile) at a
+// time: s[0..1] = tokens {2tig, 2tig+1} (row t0 of each lane), s[2..3] = tokens
+// {8+2tig, 9+2tig} (row t1).  D[head][token] = q . k over the 8 channel slices; A rows
+// 8..15 are zero.
+template <typename T>
+__device__ __forceinline__ void qk_rows(const uint32_t (&aq)[16], const uint32_t (&k)[16], float (&s)[4]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mma16816<T>(s, aq[2 * j], 0u, aq[2 * j + 1], 0u, k[2 * j], k[2 * j + 1]);
+}
+
+// Online softmax of one 16-token tile and the P.V update.  sc holds the raw scores
+// (sc[0..1] tokens 2tig, 2tig+1; sc[2..3] tokens 8+2tig, 9+2tig; head g), v16 the tile's
+// V rows in the bridge dtype; valid[i] masks token i.
+template <typename T>
+__device__ __forceinline__ void warp_softmax_pv(WarpState &ws, const float (&raw)[4], const uint16_t (*v16)[kVRow],
+                                                const bool (&valid)[4], int G, int lane, int &st) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int g = lane >> 2, tig = lane & 3;
+  float sc[4];
+  float bmax = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sc[i] = valid[i] ? raw[i] * kScale : -INFINITY;
+    if (valid[i] && g < G && !isfinite(sc[i])) st |= NSNKV_ST_OUTPUT_NONFINITE;
+    bmax = fmaxf(bmax, sc[i]);
+  }
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+  const float mnew = fmaxf(ws.m, bmax);
+  float r = 1.f, psum = 0.f, p[4];
+  if (g < G && mnew != -INFINITY) {
+    r = exp2f((ws.m - mnew) * kLog2e);
+    const float mb = mnew * kLog2e;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p[i] = exp2f(fmaf(sc[i], kLog2e, -mb));
+      psum += p[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = 0.f;
+  }
+  psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+  psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+  ws.l = ws.l * r + psum;
+  ws.m = mnew;
+  // rescale the accumulator only when some head's running max moved in this warp
+  if (!__all_sync(0xffffffffu, r == 1.f)) {
+    const float r0 = __shfl_sync(0xffffffffu, r, 8 * tig), r1 = __shfl_sync(0xffffffffu, r, 8 * tig + 4);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      ws.acc[mt][0] *= r0;
+      ws.acc[mt][1] *= r1;
+      ws.acc[mt][2] *= r0;
+      ws.acc[mt][3] *= r1;
+    }
+  }
+  // B fragments of P (tokens 2tig, 2tig+1 | 8+2tig, 9+2tig; column = head g), split into
+  // hi + lo halves of the bridge dtype so the weights keep fp32 accuracy
+  const uint32_t bh0 = pack2<T>(f2(p[0], p[1])), bh1 = pack2<T>(f2(p[2], p[3]));
+  const float2 ha = unpack2<T>(bh0), hb = unpack2<T>(bh1);
+  const uint32_t bl0 = pack2<T>(f2(p[0] - ha.x, p[1] - ha.y)), bl1 = pack2<T>(f2(p[2] - hb.x, p[3] - hb.y));
+  const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    uint32_t a[4];
+    ldmatrix_x4_trans(a, &v16[rr + 8 * (mi >> 1)][16 * mt + 8 * (mi & 1)]);
+    mma16816<T>(ws.acc[mt], a[0], a[1], a[2], a[3], bh0, bh1);
+    mma16816<T>(ws.acc[mt], a[0], a[1], a[2], a[3], bl0, bl1);
+  }
+}
+
 template <int BITS, typename T>
-__global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
   constexpr int CB = code_bytes(BITS);
-  constexpr float kTwoB = static_cast<float>(1 << BITS);
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS> &S = *reinterpret_cast<AttnSmem<BITS> *>(smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, tig = lane & 3, cbase = 32 * tig;
+  const int g = lane >> 2, tig = lane & 3, cbase = 32 * tig, mi = meta_index(cbase);
   const int t0 = 16 * warp + g, t1 = t0 + 8;
   const int chunk = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -360,18 +382,20 @@ __global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArg
   const bool is_raw = chunk >= n_sealed_chunks;
 
   int st = 0;
-  // B fragments of q: column n = g is query head h*G + g (zero when g >= G).
-  uint32_t bq[16];
+  // A fragments of q (rows = query heads h*G + g, zero when g >= G; rows 8..15 zero)
+  uint32_t aq[16];
   if (g < G) {
-    load_row32<T>(static_cast<const T *>(a.q) + ((b * a.hq) + h * G + g) * kDim, cbase, bq);
-    st |= check_row32<T>(bq);
+    load_row32<T>(static_cast<const T *>(a.q) + ((b * a.hq) + h * G + g) * kDim, cbase, aq);
+    st |= check_row32<T>(aq);
   } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) bq[i] = 0u;
+    for (int i = 0; i < 16; ++i) aq[i] = 0u;
   }
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  SoftState sm;
-  float p[16];
+  WarpState ws;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) ws.acc[mt][0] = ws.acc[mt][1] = ws.acc[mt][2] = ws.acc[mt][3] = 0.f;
+  uint16_t (*v16)[kVRow] = S.u.v16[warp];
+  const bool all_valid[4] = {true, true, true, true};
 
   if (!is_raw) {
     const int blk0 = chunk * a.chunk_blocks;
@@ -394,13 +418,28 @@ __global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArg
 #pragma unroll
       for (int i = 0; i < kStages; ++i) mbar_init(&S.full[i], 1);
       fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0)
       for (int i = 0; i < kStages && i < nloc; ++i) issue(blk0 + i, i);
+    }
+    __syncthreads();  // no thread may poll a barrier before thread 0 has initialised it
+    const float fac = static_cast<float>(1 << (23 - code_pos<BITS>(tid & 31)));
     for (int li = 0; li < nloc; ++li) {
       const int s = li % kStages;
       const bool ok = mbar_wait_bounded(&S.full[s], (li / kStages) & 1, a.status);
+      const Stage<BITS> &sg = S.stage[s];
+      MetaF &mf = S.meta[li & 1];
+      if (ok) {  // fp32 metadata of this block, one channel per thread
+        const int ci = meta_index(tid);
+        const float km = half_bits_to_f(sg.km[tid]), ks = half_bits_to_f(sg.ks[tid]);
+        const float vm = half_bits_to_f(sg.vm[tid]), vs = half_bits_to_f(sg.vs[tid]);
+        const float kb_ = ks * fac, vb_ = vs * fac;
+        mf.ka[ci] = km - kb_;
+        mf.kb[ci] = kb_;
+        mf.va[ci] = vm - vb_;
+        mf.vb[ci] = vb_;
+        bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
+        if (tid < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[tid])) || !isfinite(half_bits_to_f(sg.vn[tid]));
+        if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
+      }
       if (__syncthreads_or(!ok)) {
         // A staged copy never landed: give the later copies a bounded chance to
         // finish, then leave; the timeout status tells the host.
@@ -409,42 +448,46 @@ __global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArg
             mbar_wait_bounded(&S.full[k % kStages], (k / kStages) & 1, a.status);
         return;
       }
-      const Stage<BITS> &sg = S.stage[s];
-      MetaF &mf = S.meta[li & 1];
-      {  // metadata of this block -> fp32 (a, b) pairs, one channel per thread
-        const int c = tid, ci = meta_index(c);
-        const float km = half_bits_to_f(sg.km[c]), ks = half_bits_to_f(sg.ks[c]);
-        const float vm = half_bits_to_f(sg.vm[c]), vs = half_bits_to_f(sg.vs[c]);
-        const float kb = ks * kTwoB, vb = vs * kTwoB;
-        mf.ka[ci] = km - kb;
-        mf.kb[ci] = kb;
-        mf.va[ci] = vm - vb;
-        mf.vb[ci] = vb;
-        bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
-        if (c < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[c])) || !isfinite(half_bits_to_f(sg.vn[c]));
-        if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
-      }
-      __syncthreads();
+      // every warp has finished block li-1: its stage takes block li-1+kStages
+      if (tid == 0 && li >= 1 && li - 1 + kStages < nloc) issue(blk0 + li - 1 + kStages, (li - 1) % kStages);
+      // ---- V rows t0, t1: restore, renormalise, round to the bridge dtype (the value
+      // restore_group stores) into this warp's V tile
       {
-        uint32_t ka[16], kb[16];
-        restore_rows<BITS, T>(sg.kc, mf.ka, mf.kb, t0, t1, cbase, half_bits_to_f(sg.kn[t0]),
-                              half_bits_to_f(sg.kn[t1]), ka, kb);
-        float d[4];
-        qk_mma<T>(ka, kb, bq, d);
-        put_scores(S.sc, d, t0, t1, tig, G, true, true);
-        restore_rows<BITS, T>(sg.vc, mf.va, mf.vb, t0, t1, cbase, half_bits_to_f(sg.vn[t0]),
-                              half_bits_to_f(sg.vn[t1]), ka, kb);
-        store_row32(&S.v16[t0][cbase], ka);
-        store_row32(&S.v16[t1][cbase], kb);
+        uint32_t u0[16], u1[16];
+        restore_two_rows<BITS, T>(sg.vc, mf.va, mf.vb, mi, t0, t1, tig, half_bits_to_f(sg.vn[t0]),
+                                  half_bits_to_f(sg.vn[t1]), u0, u1);
+        store_row32(&v16[g][cbase], u0);
+        store_row32(&v16[g + 8][cbase], u1);
       }
-      __syncthreads();
-      // stage s is consumed: refill it with block li + kStages
-      if (tid == 0 && li + kStages < nloc) issue(blk0 + li + kStages, s);
-      softmax_lane(S.sc, g, tig, G, sm, p, acc, st);
-      pv_mma<T>(S.v16, p, warp, lane, acc);
+      // ---- K rows t0, t1: the same restore, then the scores of both rows
+      float sraw[4];
+      {
+        uint32_t k0[16], k1[16];
+        restore_two_rows<BITS, T>(sg.kc, mf.ka, mf.kb, mi, t0, t1, tig, half_bits_to_f(sg.kn[t0]),
+                                  half_bits_to_f(sg.kn[t1]), k0, k1);
+        // four independent accumulation chains per row (two slices each) shorten the
+        // dependent MMA sequence; their sum is the score
+        float s0[4][4], s1[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s0[c][i] = s1[c][i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          mma16816<T>(s0[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k0[2 * j], k0[2 * j + 1]);
+          mma16816<T>(s1[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k1[2 * j], k1[2 * j + 1]);
+        }
+        sraw[0] = (s0[0][0] + s0[1][0]) + (s0[2][0] + s0[3][0]);
+        sraw[1] = (s0[0][1] + s0[1][1]) + (s0[2][1] + s0[3][1]);
+        sraw[2] = (s1[0][0] + s1[1][0]) + (s1[2][0] + s1[3][0]);
+        sraw[3] = (s1[0][1] + s1[1][1]) + (s1[2][1] + s1[3][1]);
+      }
+      __syncwarp();
+      warp_softmax_pv<T>(ws, sraw, v16, all_valid, G, lane, st);
+      __syncwarp();
     }
   } else {
-    // ---- native rows (tail, appended token, or materialised K/V), 64-token tiles
+    // ---- native rows (tail, appended token, or materialised K/V), per warp 16 rows of each 64-row tile
     const T *ktb = static_cast<const T *>(a.kt) + (b * a.tss + h * a.tsh) * kDim;
     const T *vtb = static_cast<const T *>(a.vt) + (b * a.tss + h * a.tsh) * kDim;
     const T *kn_row = a.knew ? static_cast<const T *>(a.knew) + (b * a.h + h) * kDim : nullptr;
@@ -484,36 +527,57 @@ __global__ void __launch_bounds__(kThreads, 4) attn_partial_kernel(const AttnArg
           store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(vtb) + static_cast<int64_t>(j1) * kDim) + cbase, vb);
         }
       }
-      if (tile > 0) __syncthreads();  // previous tile's P.V has finished reading sc / v16
-      float d[4];
-      qk_mma<T>(ka, kb, bq, d);
-      put_scores(S.sc, d, t0, t1, tig, G, v0, v1);
-      store_row32(&S.v16[t0][cbase], va);
-      store_row32(&S.v16[t1][cbase], vb);
-      __syncthreads();
-      softmax_lane(S.sc, g, tig, G, sm, p, acc, st);
-      pv_mma<T>(S.v16, p, warp, lane, acc);
+      store_row32(&v16[g][cbase], va);
+      store_row32(&v16[g + 8][cbase], vb);
+      // validity of tokens 2tig, 2tig+1, 8+2tig, 9+2tig of this warp's 16 rows
+      const int jb = raw0 + tile * kBlock + 16 * warp;
+      const bool valid[4] = {jb + 2 * tig < raw1, jb + 2 * tig + 1 < raw1, jb + 8 + 2 * tig < raw1,
+                             jb + 9 + 2 * tig < raw1};
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      qk_rows<T>(aq, ka, s0);
+      qk_rows<T>(aq, kb, s1);
+      const float sraw[4] = {s0[0], s0[1], s1[0], s1[1]};
+      __syncwarp();
+      warp_softmax_pv<T>(ws, sraw, v16, valid, G, lane, st);
+      __syncwarp();
     }
   }
 
-  // ---- partial of this chunk: acc holds channels 32w + 16mt + {g, g+8}, heads 2tig, 2tig+1
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int n = 2 * tig + e;
-    if (n < G) {
-      const int64_t row = (b * a.hq + h * G + n) * a.max_chunks + chunk;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const int c = 32 * warp + 16 * mt + g;
-        a.part_o[row * kDim + c] = acc[mt][e];
-        a.part_o[row * kDim + c + 8] = acc[mt][2 + e];
-      }
-    }
+  // ---- combine the four warps' partials and write this chunk's partial
+  __syncthreads();
+  MergeSmem &M = S.u.merge;
+  if (tig == 0) {
+    M.m[warp][g] = ws.m;
+    M.l[warp][g] = ws.l;
   }
-  if (warp == 0 && tig == 0 && g < G) {
-    const int64_t row = (b * a.hq + h * G + g) * a.max_chunks + chunk;
-    a.part_ml[row * 2] = sm.m;
-    a.part_ml[row * 2 + 1] = sm.l;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int c = 16 * mt + g;
+    M.acc[warp][2 * tig][c] = ws.acc[mt][0];
+    M.acc[warp][2 * tig + 1][c] = ws.acc[mt][1];
+    M.acc[warp][2 * tig][c + 8] = ws.acc[mt][2];
+    M.acc[warp][2 * tig + 1][c + 8] = ws.acc[mt][3];
+  }
+  __syncthreads();
+  constexpr float kLog2e = 1.4426950408889634f;
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
+    float o = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
+      o += wt * M.acc[w][n][c];
+      l += wt * M.l[w][n];
+    }
+    const int64_t row = (b * a.hq + h * G + n) * a.max_chunks + chunk;
+    a.part_o[row * kDim + c] = o;
+    if (c == 0) {
+      a.part_ml[row * 2] = mx;
+      a.part_ml[row * 2 + 1] = l;
+    }
   }
   if (st) set_status(a.status, st);
 }
