@@ -203,6 +203,96 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ cfg4: sequence-split decode + full-context encode
+def run_cfg4(args, rank, world, local, dist):
+    """One 131072-token INT5 sequence (2047 blocks + 64 tail, GQA 64:8) split across ranks."""
+    from nsn_b200 import codec, workloads
+    from nsn_b200.splitkv import ShardedSequence, shard_range
+    device = torch.device("cuda", local)
+    c = workloads.CONFIGS[4]
+    nb_total, h, hq, bits = c["blocks"], c["h"], c["hq"], c["bits"]
+    s, e = shard_range(nb_total, world, rank)
+    last = rank == world - 1
+    n = e - s
+    # each block is drawn from its own seeded generator, so every world size sees the same data
+    ks, vs = [], []
+    for blk in range(s, e + (1 if last else 0)):
+        T = 64
+        gen = torch.Generator(device=device).manual_seed(c["seed"] * 1000003 + blk)
+        ks.append(workloads.torch_kv(gen, (h, T, 128), c["k_outliers"], 0.5, device=device))
+        vs.append(workloads.torch_kv(gen, (h, T, 128), (), c["v_sigma"], device=device))
+    k = torch.stack(ks[:n], 1).reshape(1, h, n, 64, 128)
+    v = torch.stack(vs[:n], 1).reshape(1, h, n, 64, 128)
+    kt = ks[n].reshape(1, h, 64, 128).contiguous() if last else None
+    vt = vs[n].reshape(1, h, 64, 128).contiguous() if last else None
+    del ks, vs
+    stream = torch.cuda.current_stream(device)
+    # full-context encode (prefill quantisation of this rank's K and V blocks), timed
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        g = codec.encode_group(k, s * 64, bits=bits)
+        vg = codec.encode_group(v, s * 64, bits=bits)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    g = codec.encode_group(k, s * 64, bits=bits)
+    vg = codec.encode_group(v, s * 64, bits=bits)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    enc_ms = e0.elapsed_time(e1)
+    del k, v
+    sh = ShardedSequence(g, vg, kt, vt, h, hq, bits)
+    gen = torch.Generator(device=device).manual_seed(4 * 7919)
+    qs = (torch.randn((args.warmup + args.steps, 1, hq, 1, 128), generator=gen, device=device) / math.sqrt(128)).half()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for i in range(args.warmup):
+        sh.decode(qs[i])
+    torch.cuda.synchronize(device)
+    sh.check()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            if dist:
+                dist.barrier()
+            ev[i][0].record(stream)
+            sh.decode(qs[args.warmup + i])
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(device)
+    sh.check()
+    step_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    t = torch.tensor([step_ms, enc_ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, enc_ms_max = t.tolist()
+    total_bytes = 2 * 8 * (nb_total * 5760 + 64 * 256) + 2 * hq * 256
+    total_enc_bytes = 2 * (nb_total * 8 * 64 * 128 * 2 + nb_total * 8 * 5760)
+    hbm, peak_kind = peaks()
+    if rank == 0:
+        line = {"metric": "decode tokens/s (split-KV long-context decode, cfg4)", "value": 1000.0 / step_ms,
+                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": "cfg4-long-131k-int5: 2047 INT5 blocks + 64 tail, GQA 64:8, split-KV "
+                                       "(local fused attention + NCCL all-gather of (o, lse) + merge kernel)",
+                           "global_batch": 1, "context": 131072, "parallelism": f"seq-split{world}",
+                           "l2": "flushed before every timed step"},
+                "decode_gbs_whole_job": total_bytes / (step_ms / 1000.0) / 1e9,
+                "encode": {"ms_max_over_ranks": enc_ms_max, "bytes_total": total_enc_bytes,
+                           "gbs_whole_job": total_enc_bytes / (enc_ms_max / 1000.0) / 1e9,
+                           "what": "encode_group of all 131072 tokens x 8 kv heads, K and V (read fp16, write INT5 "
+                                   "codes + fp16 metadata + headers)"},
+                "roofline": {"bound": "hbm", "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                             "achieved": total_bytes / (step_ms / 1000.0) / 1e9 / world,
+                             "frac": total_bytes / (step_ms / 1000.0) / 1e9 / world / hbm,
+                             "note": "per GPU: whole-job packed bytes / step time / GPUs"},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ main GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -212,6 +302,8 @@ def main():
     ap.add_argument("--impl", default="nsn", choices=["nsn", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
+                    help="2: batched decode (the default bench line); 4: split-KV long context + encode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -227,6 +319,14 @@ def main():
                                 device_id=torch.device("cuda", local))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    if args.config == 4:
+        torch.cuda.set_device(local)
+        run_cfg4(args, rank, world, local, dist)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

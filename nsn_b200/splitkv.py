@@ -74,9 +74,10 @@ class ShardedSequence:
         self.lse = torch.empty((hq,), dtype=torch.float32, device=dev)
         self.status = L.status_tensor(dev)
 
-    def local(self, q):
+    def local(self, q, out=None):
         """Fused attention over this rank's share -> fp32 (o, lse) per query head."""
-        out = torch.empty((1, self.hq, 128), dtype=q.dtype, device=q.device)
+        if out is None:
+            out = torch.empty((1, self.hq, 128), dtype=q.dtype, device=q.device)
         decode_attention(q.reshape(1, self.hq, 128), group_pool(self.kg, self.h) if self.n else None,
                          group_pool(self.vg, self.h) if self.n else None, h=self.h, bits=self.bits,
                          blk_stride_head=self.n, blk_stride_page=1, n_blocks=self.n, max_blocks=self.n,
@@ -87,7 +88,15 @@ class ShardedSequence:
         return self.o, self.lse
 
     def decode(self, q, group=None, out=None):
-        """Split-KV decode of q [1, hq, 1, 128]: local partials, all-gather, merge."""
+        """Split-KV decode of q [1, hq, 1, 128]: local partials, all-gather, merge.
+
+        Without an initialised process group (or with one rank) the local pass
+        already covers the whole sequence and its output is returned as is."""
+        import torch.distributed as dist
+        if not dist.is_initialized() or dist.get_world_size(group) == 1:
+            res = torch.empty((self.hq, 128), dtype=q.dtype, device=q.device) if out is None else out
+            self.local(q, out=res.view(1, self.hq, 128))
+            return res
         o, lse = self.local(q)
         O, S = gather_partials(o, lse, group)
         res, _ = merge_shards(O, S, dtype=q.dtype, out=out, status=self.status)
