@@ -3,6 +3,8 @@
 // reproduced bit for bit: every multiply/add/divide is individually rounded (no FMA
 // contraction), square roots and divisions are IEEE, rounding is half-to-even, and the
 // per-token sum of squares follows torch's CPU reduction order (nsnkv_common.cuh).
+#include <type_traits>
+
 #include "nsnkv_common.cuh"
 
 namespace nsnkv {
@@ -16,6 +18,11 @@ struct BlockSmem {
   uint8_t q[kBlock * kDim];
   uint8_t packed[kBlock * kDim * 5 / 8];
 };
+
+// Running channel minimum in token order with torch's CPU tie rule: of equal values the
+// later one is kept, so the minimum of a channel whose smallest value is zero carries the
+// sign of its last zero (+0 and -0 compare equal; the sign reaches the fp16 min meta).
+__device__ __forceinline__ float min_keep_last(float acc, float v) { return acc < v ? acc : v; }
 
 template <typename T> __device__ __forceinline__ float load_elem(const T *p) { return Elem<T>::to_f(*p); }
 
@@ -86,7 +93,7 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uin
   for (int c = tid; c < kDim; c += blockDim.x) {
     float lo = s.x[0][c], hi = s.x[0][c];
     for (int r = 1; r < kBlock; ++r) {
-      lo = fminf(lo, s.x[r][c]);
+      lo = min_keep_last(lo, s.x[r][c]);
       hi = fmaxf(hi, s.x[r][c]);
     }
     float sc = div_rn(sub_rn(hi, lo), kLevels);
@@ -114,6 +121,197 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uin
     __syncthreads();
     for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
       reinterpret_cast<uint4 *>(codes)[k] = reinterpret_cast<const uint4 *>(s.packed)[k];
+  }
+  if (st) set_status(status, st);
+}
+
+// ----------------------------------------------------------------- fp16 block encoder
+// The same encode as encode_in_smem with every thread busy in every phase: a 64x128
+// fp16 block is staged once in shared memory, each per-token and per-channel divisor
+// gets one correctly rounded reciprocal, and the quotients of its elements are
+// formed by quotient correction instead of a full IEEE division each:
+//
+//   y = RN(1/b),  q = RN(a*y),  then twice  q = RN(q + RN(a - b*q)*y)   (a - b*q by FMA)
+//
+// (Markstein's correction step, P. Markstein, "IA-64 and Elementary Functions",
+// Prentice Hall 2000, ch. 8: with y within half an ulp of 1/b and q within one ulp
+// of a/b, one correction gives the correctly rounded a/b; the first correction brings
+// RN(a*y) within that ulp).  The argument needs every intermediate in the normal
+// range, which holds for the fp16 encoder's operands: directions divide |x| <= 65504
+// by b in [1e-12, 128^0.5 * 65504], codes divide d - min in [0, 2] by a scale that is
+// either 1 or at least ~1e-22.  bf16 and fp32 inputs, whose range breaks that
+// argument, keep the IEEE-division encoder above.
+constexpr int kXRow = kDim / 2 + 4;  // 32-bit words per staged row: 64 channel pairs + 16-byte pad
+
+struct FastSmem {
+  uint32_t x[kBlock][kXRow];  // fp16 pairs; the pad keeps the norm phase's column reads conflict-free
+  float tb[kBlock];           // max(n, eps) per token
+  float ty[kBlock];           // RN(1 / tb)
+  float2 pmin[4][kDim / 2];   // per-channel-pair partial min / max of the four token quarters
+  float2 pmax[4][kDim / 2];
+  uint8_t q[kBlock * kDim];   // codes, row-major (token, channel)
+};
+
+struct Recip2 {
+  float2 y;   // RN(1/b) per lane
+  float2 nb;  // -b per lane
+};
+
+__device__ __forceinline__ float2 div2_by(float2 a, const Recip2 &r) {
+  float2 q = __fmul2_rn(a, r.y);
+  float2 e = __ffma2_rn(q, r.nb, a);
+  q = __ffma2_rn(e, r.y, q);
+  e = __ffma2_rn(q, r.nb, a);
+  return __ffma2_rn(e, r.y, q);
+}
+
+// 32 consecutive codes (one per byte of w) -> BITS words of the LSB-first bitstream.
+template <int BITS>
+__device__ __forceinline__ void pack32(const uint32_t (&w)[8], uint32_t (&out)[BITS]) {
+  constexpr uint32_t m = (1u << BITS) - 1u;
+  constexpr uint32_t kM1 = m * 0x00010001u;             // codes of bytes 0 and 2 in place
+  constexpr uint32_t kM2 = (m << BITS) * 0x00010001u;   // codes of bytes 1 and 3 moved down next to them
+  constexpr uint32_t kF = (1u << (2 * BITS)) - 1u;
+  uint64_t acc = 0;
+  int nbits = 0, o = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t p = (w[k] & kM1) | ((w[k] >> (8 - BITS)) & kM2);
+    const uint32_t f = (p & kF) | ((p >> (16 - 2 * BITS)) & (kF << (2 * BITS)));
+    acc |= static_cast<uint64_t>(f) << nbits;
+    nbits += 4 * BITS;
+    if (nbits >= 32) {
+      out[o++] = static_cast<uint32_t>(acc);
+      acc >>= 32;
+      nbits -= 32;
+    }
+  }
+}
+
+// Encode one contiguous 64x128 fp16 block (256 threads).  Outputs as encode_in_smem;
+// codes and q_out may be null.
+template <int BITS>
+__device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
+                                  uint16_t *scale, int32_t *status, FastSmem &s) {
+  const int t = threadIdx.x;
+  constexpr uint32_t kL = (1u << BITS) - 1u;
+  int st = 0;
+  {
+    const uint4 *g = reinterpret_cast<const uint4 *>(src);
+    uint4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = g[t + 256 * j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = t + 256 * j;
+      *reinterpret_cast<uint4 *>(&s.x[k >> 4][(k & 15) * 4]) = v[j];
+    }
+  }
+  __syncthreads();
+  // n = ||x||_2 per token in torch's CPU order: thread (r, g) runs lanes 2g and 2g+1
+  // of the eight interleaved accumulators, then the lanes are added 0..7.
+  {
+    const int r = t >> 2, g = t & 3;
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float2 v = Elem<__half>::to_f2(s.x[r][4 * k + g]);
+      const float2 sq = __fmul2_rn(v, v);
+      acc = k == 0 ? sq : __fadd2_rn(acc, sq);
+    }
+    const int base = t & 28;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lx = __shfl_sync(0xffffffffu, acc.x, base + j);
+      const float ly = __shfl_sync(0xffffffffu, acc.y, base + j);
+      ss = j == 0 ? add_rn(lx, ly) : add_rn(add_rn(ss, lx), ly);
+    }
+    // |x| <= 65504 keeps 128 squares finite: a non-finite sum means a non-finite input
+    if (!isfinite(ss)) st |= NSNKV_ST_INPUT_NONFINITE;
+    if (g == 0) {
+      const float n = __fsqrt_rn(ss);
+      const float b = fmaxf(n, kEps);
+      s.tb[r] = b;
+      s.ty[r] = __frcp_rn(b);
+      const __half n16 = __float2half_rn(n);
+      const float n16f = __half2float(n16);
+      if (!isfinite(n16f)) st |= NSNKV_ST_META_OVERFLOW;
+      if (n != 0.f && n16f == 0.f) st |= NSNKV_ST_META_UNDERFLOW;
+      norm[r] = __half_as_ushort(n16);
+    }
+  }
+  __syncthreads();
+  // d = x / max(n, eps) for channel pair cp over the token quarter tg; channel min / max
+  const int cp = t & 63, tg = t >> 6;
+  float2 d[16];
+  float2 lo = make_float2(INFINITY, INFINITY), hi = make_float2(-INFINITY, -INFINITY);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int r = 16 * tg + i;
+    const float2 v = Elem<__half>::to_f2(s.x[r][cp]);
+    const float b = s.tb[r], y = s.ty[r];
+    float2 q = div2_by(v, Recip2{make_float2(y, y), make_float2(-b, -b)});
+    q.x = copysignf(q.x, v.x);  // the corrections turn -0 into +0; x / b keeps the sign of a zero x
+    q.y = copysignf(q.y, v.y);
+    d[i] = q;
+    lo = make_float2(min_keep_last(lo.x, q.x), min_keep_last(lo.y, q.y));
+    hi = make_float2(fmaxf(hi.x, q.x), fmaxf(hi.y, q.y));
+  }
+  s.pmin[tg][cp] = lo;
+  s.pmax[tg][cp] = hi;
+  __syncthreads();
+  lo = s.pmin[0][cp];
+  hi = s.pmax[0][cp];
+#pragma unroll
+  for (int j = 1; j < 4; ++j) {  // token order, so a tie still resolves to the later token
+    const float2 a = s.pmin[j][cp], b = s.pmax[j][cp];
+    lo = make_float2(min_keep_last(lo.x, a.x), min_keep_last(lo.y, a.y));
+    hi = make_float2(fmaxf(hi.x, b.x), fmaxf(hi.y, b.y));
+  }
+  const float scx = div_rn(sub_rn(hi.x, lo.x), static_cast<float>(kL));
+  const float scy = div_rn(sub_rn(hi.y, lo.y), static_cast<float>(kL));
+  const float dx = scx == 0.f ? 1.f : scx, dy = scy == 0.f ? 1.f : scy;
+  if (tg == 0) {
+    const __half2 m16 = __floats2half2_rn(lo.x, lo.y), s16 = __floats2half2_rn(scx, scy);
+    const float2 m16f = __half22float2(m16), s16f = __half22float2(s16);
+    if (!isfinite(m16f.x) || !isfinite(m16f.y) || !isfinite(s16f.x) || !isfinite(s16f.y))
+      st |= NSNKV_ST_META_OVERFLOW;
+    if ((scx != 0.f && s16f.x == 0.f) || (scy != 0.f && s16f.y == 0.f)) st |= NSNKV_ST_META_UNDERFLOW;
+    *reinterpret_cast<__half2 *>(mn + 2 * cp) = m16;
+    *reinterpret_cast<__half2 *>(scale + 2 * cp) = s16;
+  }
+  // codes: rint((d - min) / scale) clamped to [0, L].  d - min >= 0, so adding 1.5 * 2^23
+  // rounds the quotient to the nearest integer, ties to even, into the low mantissa bits.
+  // A channel whose scale is 0 divides by 1 values below 2^-126 * 31: its codes are 0.
+  {
+    const Recip2 rc{make_float2(__frcp_rn(dx), __frcp_rn(dy)), make_float2(-dx, -dy)};
+    const float2 nlo = make_float2(-lo.x, -lo.y);
+    const float2 magic = make_float2(12582912.f, 12582912.f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 w = __fadd2_rn(div2_by(__fadd2_rn(d[i], nlo), rc), magic);
+      const uint32_t c0 = min(__float_as_uint(w.x) - 0x4B400000u, kL);
+      const uint32_t c1 = min(__float_as_uint(w.y) - 0x4B400000u, kL);
+      *reinterpret_cast<uint16_t *>(&s.q[(16 * tg + i) * kDim + 2 * cp]) = static_cast<uint16_t>(c0 | (c1 << 8));
+    }
+  }
+  __syncthreads();
+  {
+    const uint4 a = reinterpret_cast<const uint4 *>(s.q)[2 * t];
+    const uint4 b = reinterpret_cast<const uint4 *>(s.q)[2 * t + 1];
+    if (q_out) {
+      reinterpret_cast<uint4 *>(q_out)[2 * t] = a;
+      reinterpret_cast<uint4 *>(q_out)[2 * t + 1] = b;
+    }
+    if (codes) {
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t out[BITS];
+      pack32<BITS>(w, out);
+      uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + BITS * t;
+#pragma unroll
+      for (int i = 0; i < BITS; ++i) dst[i] = out[i];
+    }
   }
   if (st) set_status(status, st);
 }
@@ -147,6 +345,23 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
   encode_in_smem<BITS>(s, norm_order, codes ? codes + o * code_bytes(BITS) : nullptr,
                        q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, mn + o * kDim,
                        scale + o * kDim, status, st);
+  if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256, 4) encode_blocks_fast_kernel(const __half *x, int64_t blocks_per_row,
+                                                                   uint8_t *codes, uint8_t *q_out, uint16_t *norm,
+                                                                   uint16_t *mn, uint16_t *scale, uint8_t *headers,
+                                                                   int64_t header_start, int64_t out_row_stride,
+                                                                   int64_t out_offset, int32_t *status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
+  const int64_t b = blockIdx.x;
+  const int64_t r = b / blocks_per_row, i = b % blocks_per_row;
+  const int64_t o = r * out_row_stride + out_offset + i;
+  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * code_bytes(BITS) : nullptr,
+                          q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, mn + o * kDim,
+                          scale + o * kDim, status, s);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
 }
 
@@ -284,6 +499,16 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
   const int32_t page = table[b * table_stride + n_blocks[b]];
   const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
   const T *src = (kv == 0 ? k_tail : v_tail) + (b * tss + h * tsh) * kDim;
+  if constexpr (std::is_same<T, __half>::value) {
+    FastSmem &f = *reinterpret_cast<FastSmem *>(smem_raw);
+    if (kv == 0)
+      encode_block_fast<BITS>(src, k_codes + blk * code_bytes(BITS), nullptr, k_norm + blk * kBlock,
+                              k_min + blk * kDim, k_scale + blk * kDim, status, f);
+    else
+      encode_block_fast<BITS>(src, v_codes + blk * code_bytes(BITS), nullptr, v_norm + blk * kBlock,
+                              v_min + blk * kDim, v_scale + blk * kDim, status, f);
+    return;
+  }
   int st = load_block<T>(src, s);
   __syncthreads();
   if (kv == 0)
@@ -312,8 +537,29 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
                          uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale, uint8_t *headers,
                          int64_t header_start, int64_t out_row_stride, int64_t out_offset, int32_t *status,
                          cudaStream_t st) {
-  const size_t smem = sizeof(BlockSmem);
   dim3 grid(static_cast<unsigned>(n_blocks));
+  if (std::is_same<T, __half>::value && norm_order == 0) {
+    const size_t smem = sizeof(FastSmem);
+#define NSNKV_ENC_FAST(B)                                                                                  \
+  case B: {                                                                                                \
+    auto k = encode_blocks_fast_kernel<B>;                                                                 \
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
+      return NSNKV_ERR_CUDA;                                                                               \
+    k<<<grid, 256, smem, st>>>(static_cast<const __half *>(x), bpr, codes, q_out, norm, mn, scale, headers, \
+                               header_start, out_row_stride, out_offset, status);                          \
+    break;                                                                                                 \
+  }
+    switch (bits) {
+      NSNKV_ENC_FAST(3)
+      NSNKV_ENC_FAST(4)
+      NSNKV_ENC_FAST(5)
+      default:
+        return NSNKV_ERR_ARG;
+    }
+#undef NSNKV_ENC_FAST
+    return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+  }
+  const size_t smem = sizeof(BlockSmem);
 #define NSNKV_ENC(B)                                                                                      \
   case B: {                                                                                               \
     auto k = encode_blocks_kernel<T, B>;                                                                  \
@@ -375,7 +621,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
                        uint16_t *vm, uint16_t *vs, int64_t sh, int64_t sp, int32_t *status, cudaStream_t st) {
-  const size_t smem = sizeof(BlockSmem);
+  const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
   case B: {                                                                                                \

@@ -204,6 +204,17 @@ def gen_encode():
     x = torch.linspace(-1, 1, 64 * 128).reshape(1, 1, 1, 64, 128)
     encode_case("linspace", x)
 
+    # Channels whose smallest value is a zero of either sign (the min meta's sign is
+    # decided by the reduction's tie rule); the last 16 channels also hold negatives.
+    g2 = torch.Generator().manual_seed(PILOT_SEED + 11)
+    x = torch.rand(1, 1, 2, 64, 128, generator=g2) + 0.1
+    zero = torch.rand(1, 1, 2, 64, 128, generator=g2) < 0.1
+    neg = torch.rand(1, 1, 2, 64, 128, generator=g2) < 0.5
+    x = torch.where(zero, torch.where(neg, torch.tensor(-0.0), torch.tensor(0.0)), x)
+    x[..., 112:] -= 0.6
+    encode_case("signed_zero_min", x.to(torch.float16))
+    encode_case("signed_zero_min_bf16", x.to(torch.bfloat16))
+
 
 # ------------------------------------------------------------------ encode_group / restore_group
 def gen_group():

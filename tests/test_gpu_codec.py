@@ -138,3 +138,52 @@ def test_int5_round_trip_and_restore_against_oracle():
     back = P.unpack_codes(r["codes"].reshape(-1), 2 * 37 * 8192, 5)
     q, _ = P.nsn_encode(x, 5)
     assert torch.equal(back, q.reshape(-1))
+
+
+def _fp16_stress_blocks(rng, n):
+    """fp16 blocks [n, 64, 128] from six families that reach the encoder's corners."""
+    fam = []
+    # heavy-tailed tokens with outlier channels
+    x = rng.standard_normal((n, 64, 128)).astype(np.float32) * rng.lognormal(0, 2.0, (n, 64, 1)).astype(np.float32)
+    x[..., ::17] *= 50
+    fam.append(np.clip(x, -4000, 4000))
+    # random finite fp16 bit patterns: every exponent, subnormals, +-0
+    b = rng.integers(0, 1 << 16, (n, 64, 128), dtype=np.uint32).astype(np.uint16)
+    b[(b & 0x7C00) == 0x7C00] &= 0xBBFF
+    fam.append(b.view(np.float16).astype(np.float32))
+    # sparse rows: mostly exact zeros of both signs
+    x = rng.standard_normal((n, 64, 128)).astype(np.float32)
+    x[rng.random((n, 64, 128)) < 0.95] = 0.0
+    x[rng.random((n, 64, 128)) < 0.3] *= -1.0
+    x[(x == 0) & (rng.random((n, 64, 128)) < 0.5)] = -0.0
+    fam.append(x)
+    # constant channels and constant tokens
+    x = rng.standard_normal((n, 64, 128)).astype(np.float32)
+    x[:, :, ::3] = x[:, :1, ::3]
+    x[:, ::5, :] = 0.25
+    fam.append(x)
+    # subnormal-only magnitudes
+    x = (rng.integers(-1023, 1024, (n, 64, 128)) * 2.0 ** -24).astype(np.float32)
+    fam.append(x)
+    # near the fp16 maximum (norms overflow fp16: the status word must say so)
+    x = rng.uniform(-65504, 65504, (n, 64, 128)).astype(np.float32)
+    fam.append(x)
+    return [f.astype(np.float16) for f in fam]
+
+
+@pytest.mark.parametrize("bits", [3, 4, 5])
+def test_fp16_encoder_stress_matches_oracle(bits):
+    """The fp16 encoder (reciprocal + quotient correction) equals the oracle bit for bit
+    on 6 x 384 blocks per width: codes, packed bytes, fp16 metadata and status."""
+    from nsn_b200 import primitives as P
+    rng = np.random.default_rng(100 + bits)
+    for fi, x16 in enumerate(_fp16_stress_blocks(rng, 384)):
+        x = torch.from_numpy(x16).cuda().reshape(3, 128, 64, 128)
+        r = P.encode_blocks(x, bits, packed=True, unpacked=True, check=False)
+        q, n, m, s, st = O.nsn_encode(x16.astype(np.float32).reshape(3, 128, 64, 128), bits)
+        assert int(r["status"].item()) == st, (fi, int(r["status"].item()), st)
+        assert np.array_equal(r["q"].cpu().numpy(), q), fi
+        for t, ref in zip(r["metas"], (n, m, s)):
+            assert np.array_equal(bits16(t).reshape(-1), ref.view(np.uint16).reshape(-1)), fi
+        want = np.frombuffer(O.pack_codes(q, bits), np.uint8)
+        assert np.array_equal(r["codes"].cpu().numpy().reshape(-1), want), fi
