@@ -127,9 +127,9 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uin
 
 // ----------------------------------------------------------------- fp16 block encoder
 // The same encode as encode_in_smem with every thread busy in every phase: a 64x128
-// fp16 block is staged once in shared memory, each per-token and per-channel divisor
-// gets one correctly rounded reciprocal, and the quotients of its elements are
-// formed by quotient correction instead of a full IEEE division each:
+// fp16 block is staged once in shared memory as fp32, each per-token and per-channel
+// divisor gets one correctly rounded reciprocal, and the quotients of its elements
+// are formed by quotient correction instead of a full IEEE division each:
 //
 //   y = RN(1/b),  q = RN(a*y),  then twice  q = RN(q + RN(a - b*q)*y)   (a - b*q by FMA)
 //
@@ -141,15 +141,20 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uin
 // by b in [1e-12, 128^0.5 * 65504], codes divide d - min in [0, 2] by a scale that is
 // either 1 or at least ~1e-22.  bf16 and fp32 inputs, whose range breaks that
 // argument, keep the IEEE-division encoder above.
-constexpr int kXRow = kDim / 2 + 4;  // 32-bit words per staged row: 64 channel pairs + 16-byte pad
+//
+// Directions are formed negated, nd = x / (-b): with a negative divisor the
+// corrections keep the sign of a zero quotient (x / b of -0 is -0, and the
+// correction's "+ RN(a - b*q)*y" would otherwise turn -0 into +0).  min d = -max nd and
+// max d = -min nd exactly.
+constexpr int kXRowF = kDim + 8;  // fp32 words per staged row; the pad makes the norm phase's reads conflict-free
 
 struct FastSmem {
-  uint32_t x[kBlock][kXRow];  // fp16 pairs; the pad keeps the norm phase's column reads conflict-free
-  float tb[kBlock];           // max(n, eps) per token
-  float ty[kBlock];           // RN(1 / tb)
-  float2 pmin[4][kDim / 2];   // per-channel-pair partial min / max of the four token quarters
-  float2 pmax[4][kDim / 2];
-  uint8_t q[kBlock * kDim];   // codes, row-major (token, channel)
+  float x[kBlock][kXRowF];   // the block as fp32
+  float nyt[kBlock];         // -RN(1 / max(n, eps)) per token
+  float bt[kBlock];          // max(n, eps) per token
+  float2 pmax[4][kDim / 2];  // per channel pair and token quarter: max of nd (= -min d) ...
+  float2 pmin[4][kDim / 2];  // ... and min of nd (= -max d)
+  uint8_t q[kBlock * kDim];  // codes, row-major (token, channel)
 };
 
 struct Recip2 {
@@ -163,6 +168,17 @@ __device__ __forceinline__ float2 div2_by(float2 a, const Recip2 &r) {
   q = __ffma2_rn(e, r.y, q);
   e = __ffma2_rn(q, r.nb, a);
   return __ffma2_rn(e, r.y, q);
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // 32 consecutive codes (one per byte of w) -> BITS words of the LSB-first bitstream.
@@ -190,23 +206,34 @@ __device__ __forceinline__ void pack32(const uint32_t (&w)[8], uint32_t (&out)[B
 
 // Encode one contiguous 64x128 fp16 block (256 threads).  Outputs as encode_in_smem;
 // codes and q_out may be null.
+// Stage one contiguous 64x128 fp16 block into s.x as fp32 (all 256 threads).  Thread k
+// of a row's 16 writes its 32 bytes as two 16-byte halves, the second half first on
+// odd-numbered quarters of the row, so each quarter-warp store covers all 32 banks.
+__device__ __forceinline__ void stage_block(const __half *src, FastSmem &s) {
+  const uint4 *g = reinterpret_cast<const uint4 *>(src);
+  uint4 v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = g[threadIdx.x + 256 * j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = threadIdx.x + 256 * j;
+    float *dst = &s.x[k >> 4][(k & 15) * 8];
+    const float2 a = Elem<__half>::to_f2(v[j].x), b = Elem<__half>::to_f2(v[j].y);
+    const float2 c = Elem<__half>::to_f2(v[j].z), d = Elem<__half>::to_f2(v[j].w);
+    const float4 lo = make_float4(a.x, a.y, b.x, b.y), hi = make_float4(c.x, c.y, d.x, d.y);
+    const int swap = (k >> 2) & 1;
+    *reinterpret_cast<float4 *>(dst + 4 * swap) = swap ? hi : lo;
+    *reinterpret_cast<float4 *>(dst + 4 * (swap ^ 1)) = swap ? lo : hi;
+  }
+}
+
 template <int BITS>
 __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
                                   uint16_t *scale, int32_t *status, FastSmem &s) {
   const int t = threadIdx.x;
   constexpr uint32_t kL = (1u << BITS) - 1u;
   int st = 0;
-  {
-    const uint4 *g = reinterpret_cast<const uint4 *>(src);
-    uint4 v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = g[t + 256 * j];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k = t + 256 * j;
-      *reinterpret_cast<uint4 *>(&s.x[k >> 4][(k & 15) * 4]) = v[j];
-    }
-  }
+  stage_block(src, s);
   __syncthreads();
   // n = ||x||_2 per token in torch's CPU order: thread (r, g) runs lanes 2g and 2g+1
   // of the eight interleaved accumulators, then the lanes are added 0..7.
@@ -215,7 +242,7 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_
     float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      const float2 v = Elem<__half>::to_f2(s.x[r][4 * k + g]);
+      const float2 v = *reinterpret_cast<const float2 *>(&s.x[r][8 * k + 2 * g]);
       const float2 sq = __fmul2_rn(v, v);
       acc = k == 0 ? sq : __fadd2_rn(acc, sq);
     }
@@ -232,8 +259,8 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_
     if (g == 0) {
       const float n = __fsqrt_rn(ss);
       const float b = fmaxf(n, kEps);
-      s.tb[r] = b;
-      s.ty[r] = __frcp_rn(b);
+      s.bt[r] = b;
+      s.nyt[r] = -__frcp_rn(b);
       const __half n16 = __float2half_rn(n);
       const float n16f = __half2float(n16);
       if (!isfinite(n16f)) st |= NSNKV_ST_META_OVERFLOW;
@@ -242,33 +269,39 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_
     }
   }
   __syncthreads();
-  // d = x / max(n, eps) for channel pair cp over the token quarter tg; channel min / max
+  // nd = x / -max(n, eps) for channel pair cp over token quarter tg, with its max / min
   const int cp = t & 63, tg = t >> 6;
-  float2 d[16];
-  float2 lo = make_float2(INFINITY, INFINITY), hi = make_float2(-INFINITY, -INFINITY);
+  float2 nd[16];
+  float2 mx = make_float2(-INFINITY, -INFINITY), mnv = make_float2(INFINITY, INFINITY);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int r = 16 * tg + i;
-    const float2 v = Elem<__half>::to_f2(s.x[r][cp]);
-    const float b = s.tb[r], y = s.ty[r];
-    float2 q = div2_by(v, Recip2{make_float2(y, y), make_float2(-b, -b)});
-    q.x = copysignf(q.x, v.x);  // the corrections turn -0 into +0; x / b keeps the sign of a zero x
-    q.y = copysignf(q.y, v.y);
-    d[i] = q;
-    lo = make_float2(min_keep_last(lo.x, q.x), min_keep_last(lo.y, q.y));
-    hi = make_float2(fmaxf(hi.x, q.x), fmaxf(hi.y, q.y));
+  for (int j = 0; j < 4; ++j) {
+    const float4 ny4 = *reinterpret_cast<const float4 *>(&s.nyt[16 * tg + 4 * j]);
+    const float4 b4 = *reinterpret_cast<const float4 *>(&s.bt[16 * tg + 4 * j]);
+    const float nyv[4] = {ny4.x, ny4.y, ny4.z, ny4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * j + e;
+      const float2 v = *reinterpret_cast<const float2 *>(&s.x[16 * tg + i][2 * cp]);
+      nd[i] = div2_by(v, Recip2{make_float2(nyv[e], nyv[e]), make_float2(bv[e], bv[e])});
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = 4 * j + e;
+      mx = make_float2(max3(mx.x, nd[i].x, nd[i + 1].x), max3(mx.y, nd[i].y, nd[i + 1].y));
+      mnv = make_float2(min3(mnv.x, nd[i].x, nd[i + 1].x), min3(mnv.y, nd[i].y, nd[i + 1].y));
+    }
   }
-  s.pmin[tg][cp] = lo;
-  s.pmax[tg][cp] = hi;
+  s.pmax[tg][cp] = mx;
+  s.pmin[tg][cp] = mnv;
   __syncthreads();
-  lo = s.pmin[0][cp];
-  hi = s.pmax[0][cp];
-#pragma unroll
-  for (int j = 1; j < 4; ++j) {  // token order, so a tie still resolves to the later token
-    const float2 a = s.pmin[j][cp], b = s.pmax[j][cp];
-    lo = make_float2(min_keep_last(lo.x, a.x), min_keep_last(lo.y, a.y));
-    hi = make_float2(fmaxf(hi.x, b.x), fmaxf(hi.y, b.y));
+  {
+    const float2 a0 = s.pmax[0][cp], a1 = s.pmax[1][cp], a2 = s.pmax[2][cp], a3 = s.pmax[3][cp];
+    const float2 b0 = s.pmin[0][cp], b1 = s.pmin[1][cp], b2 = s.pmin[2][cp], b3 = s.pmin[3][cp];
+    mx = make_float2(max3(a0.x, a1.x, fmaxf(a2.x, a3.x)), max3(a0.y, a1.y, fmaxf(a2.y, a3.y)));
+    mnv = make_float2(min3(b0.x, b1.x, fminf(b2.x, b3.x)), min3(b0.y, b1.y, fminf(b2.y, b3.y)));
   }
+  // channel min / max of d; a zero min gets its sign fixed below
+  const float2 lo = make_float2(-mx.x, -mx.y), hi = make_float2(-mnv.x, -mnv.y);
   const float scx = div_rn(sub_rn(hi.x, lo.x), static_cast<float>(kL));
   const float scy = div_rn(sub_rn(hi.y, lo.y), static_cast<float>(kL));
   const float dx = scx == 0.f ? 1.f : scx, dy = scy == 0.f ? 1.f : scy;
@@ -281,22 +314,47 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_
     *reinterpret_cast<__half2 *>(mn + 2 * cp) = m16;
     *reinterpret_cast<__half2 *>(scale + 2 * cp) = s16;
   }
-  // codes: rint((d - min) / scale) clamped to [0, L].  d - min >= 0, so adding 1.5 * 2^23
-  // rounds the quotient to the nearest integer, ties to even, into the low mantissa bits.
-  // A channel whose scale is 0 divides by 1 values below 2^-126 * 31: its codes are 0.
+  // codes: rint((d - min) / scale), d - min = RN(max nd - nd) >= 0.  Adding 1.5 * 2^23
+  // rounds the quotient (at most L * (1 + 2^-23)) to the nearest integer, ties to
+  // even, into the low mantissa byte.  A channel whose scale is 0 divides by 1 values
+  // below 2^-126 * 31: its codes are 0.
   {
     const Recip2 rc{make_float2(__frcp_rn(dx), __frcp_rn(dy)), make_float2(-dx, -dy)};
-    const float2 nlo = make_float2(-lo.x, -lo.y);
     const float2 magic = make_float2(12582912.f, 12582912.f);
+    const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float2 w = __fadd2_rn(div2_by(__fadd2_rn(d[i], nlo), rc), magic);
-      const uint32_t c0 = min(__float_as_uint(w.x) - 0x4B400000u, kL);
-      const uint32_t c1 = min(__float_as_uint(w.y) - 0x4B400000u, kL);
-      *reinterpret_cast<uint16_t *>(&s.q[(16 * tg + i) * kDim + 2 * cp]) = static_cast<uint16_t>(c0 | (c1 << 8));
+      const float2 w = __fadd2_rn(div2_by(__ffma2_rn(nd[i], neg1, mx), rc), magic);
+      const uint32_t pair = __byte_perm(__float_as_uint(w.x), __float_as_uint(w.y), 0x0040);
+      *reinterpret_cast<uint16_t *>(&s.q[(16 * tg + i) * kDim + 2 * cp]) = static_cast<uint16_t>(pair);
     }
   }
-  __syncthreads();
+  // torch keeps the later of equal values in its channel min, so a zero min carries the
+  // sign of the channel's last zero in token order (rare: only channels without negatives)
+  const int zero_min = tg == 0 && (lo.x == 0.f || lo.y == 0.f);
+  if (__syncthreads_or(zero_min)) {
+    uint32_t z = 0;  // per channel: 0 no zero, 1 last zero is +0, 2 last zero is -0 (of d = -nd)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (nd[i].x == 0.f) z = (z & ~3u) | (signbit(nd[i].x) ? 1u : 2u);
+      if (nd[i].y == 0.f) z = (z & ~12u) | ((signbit(nd[i].y) ? 1u : 2u) << 2);
+    }
+    reinterpret_cast<uint32_t *>(&s.pmax[0][0])[tg * (kDim / 2) + cp] = z;
+    __syncthreads();
+    if (zero_min) {
+      uint16_t *m = mn + 2 * cp;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if ((c == 0 ? lo.x : lo.y) != 0.f) continue;
+        uint32_t last = 0;
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t zj = (reinterpret_cast<const uint32_t *>(&s.pmax[0][0])[j * (kDim / 2) + cp] >> (2 * c)) & 3u;
+          if (zj) last = zj;
+        }
+        m[c] = last == 2 ? 0x8000u : 0x0000u;
+      }
+    }
+  }
   {
     const uint4 a = reinterpret_cast<const uint4 *>(s.q)[2 * t];
     const uint4 b = reinterpret_cast<const uint4 *>(s.q)[2 * t + 1];
