@@ -1,33 +1,27 @@
 // Fused packed-KV decode attention for sm_100a (split-KV, flash-decoding style).
 //
-// One CTA owns (chunk of up to 8 sealed blocks | up to 512 native rows, kv head h,
-// sequence b) and serves all G = hq/h <= 8 query heads of that kv head, so every packed
+// One CTA (4 warps) owns (chunk of sealed blocks | a chunk of native rows, kv head h,
+// sequence b) and serves all G = hq/h query heads of that kv head, so every packed
 // byte is read from HBM exactly once (the reference's NB06 _partial re-reads each kv
 // block G times, experiments/nb06/source/loop_kv_nb06_kernel.py:54-114).
 //
-// Warp roles (14 warps):
-//   producer (warp 12)  TMA bulk copies (cp.async.bulk) of each block's codes and fp16
-//                       metadata into a 6-stage ring, then the block's fp32 restore
-//                       coefficients; mbarriers full / ready / empty.
-//   restore (warps 0-7) warp w restores channels 32(w%4)..+31 of tokens 32(w/4)..+31 (lane =
-//                       token, so the channel group's coefficients are warp-uniform loads):
-//                       d = min + scale*code (fp32), the row's sum of squares from the four
-//                       warps of its token half, k = (norm / max(||d||, eps)) * d rounded to
-//                       the bridge dtype -- the value restore_group stores -- written into a
-//                       shared tile in the tensor core's no-swizzle operand layout.
-//   MMA (warp 13)       one thread issues tcgen05.mma: scores D1 = K . Q^T (M = 64 tokens,
-//                       N = 8 heads, TMEM, double buffered) and, later, D2 += V^T . P^T
-//                       (M = 128 channels, N = 16: 8 heads of P rounded to the bridge dtype
-//                       + 8 heads of its remainder, so the weights keep fp32 accuracy).
-//   softmax (warps 8-11) warp 8+q reads the scores of tokens 16q..16q+15 out of TMEM
-//                       (lanes 0..15 of TMEM quadrant q) and builds their P rows.
-// Each chunk runs in two phases: all K blocks first (scores kept in shared memory and
-// the exact chunk maximum found), then all V blocks with P = exp(s - max) at that
-// final maximum, so the TMEM accumulator is never rescaled.  The chunk's (o, max, sum)
-// partial is combined with the others by the merge kernel (log-sum-exp, the reference's
-// merge, loop_kv_af01_kernel.py:70-84).
+// Per 64-token block, staged in shared memory by the TMA engine (cp.async.bulk,
+// double buffered, completion on mbarriers):
+//   K phase  warp w takes tokens 16w..16w+15; lane (g, tig) unpacks tokens g and g+8,
+//            channels 32*tig..32*tig+31 in registers: d = min + scale*code (fp32),
+//            row norm over a 4-lane shuffle, k = (norm/max(||d||,eps)) * d rounded to
+//            the bridge dtype (fp16/bf16) -- the value restore_group would store --
+//            and the packed pairs are used directly as the A fragments of
+//            mma.m16n8k16 against q (B fragments, 8 query-head columns) -> scores.
+//   softmax  running max / sum per query head, 2 heads per warp.
+//   V phase  V rows are restored and rounded the same way into a padded shared tile;
+//            P.V runs as mma.m16n8k16 with A = V^T loaded by ldmatrix.trans and
+//            B = P split into hi + lo halves (fp32-accurate weights); warp w owns
+//            channels 32w..32w+31 of the accumulator.
+// Native rows (the tail, an appended token, or fully materialised K/V) use the same
+// code without the unpack.  A merge kernel combines chunk partials with a
+// log-sum-exp reduction (the reference's merge, loop_kv_af01_kernel.py:70-84).
 #include <mutex>
-#include <type_traits>
 
 #include "nsnkv_common.cuh"
 
@@ -58,53 +52,47 @@ struct AttnArgs {
   int32_t *status;
 };
 
-constexpr int kHeads = 8;                  // query heads of one kv head (G <= 8)
-constexpr int kMetaRow = kDim + kDim / 8;  // fp32 coefficient row padded every 32 channels by 4 floats
-constexpr int kRestoreWarps = 8;           // warp w: channel group w%4 of tokens 32(w/4)..32(w/4)+31
-constexpr int kSoftmaxWarp0 = 8;           // warps 8..11: warp % 4 = TMEM quadrant of its tokens
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 12;
-constexpr int kMmaWarp = 13;
-constexpr int kThreads = 14 * 32;
-constexpr int kStages = 6;                 // TMA ring depth
-constexpr int kChunk = 8;                  // 64-token units per chunk (and phase)
-constexpr int kTmemCols = 32;              // scores at columns [0, 8) and [8, 16), P.V accumulator at [16, 32)
-constexpr int kScRow = kChunk * kBlock + 4;  // padded score row: the 8 heads' rows start in distinct banks
+constexpr int kThreads = 128;    // 4 warps; warp w owns tokens 16w..16w+15 of every block
+constexpr int kWarps = kThreads / 32;
+constexpr int kHeads = 8;        // MMA rows/columns for the query heads of one kv head (G <= 8)
+constexpr int kVRow = kDim + 8;  // padded V tile row (272 B): ldmatrix rows hit distinct banks
+constexpr int kStages = 4;       // TMA ring depth (blocks in flight per CTA)
+constexpr int kMetaRow = kDim + kDim / 8;  // fp32 metadata row padded every 32 channels by 4 floats
 
-// One block (K or V) as staged by the producer.  The restore coefficients: a code k is
-// dropped into mantissa bits [p, p+BITS) of 1.0f, giving x = 1 + k*2^(p-23); then
-//   d = min + scale*k = b*x + a,   b = scale * 2^(23-p),   a = min - b.
 template <int BITS>
 struct Stage {
-  uint8_t codes[code_bytes(BITS)];
-  uint16_t norm[kBlock];
-  uint16_t mn[kDim];
-  uint16_t sc[kDim];
-  float fa[kMetaRow];
-  float fb[kMetaRow];
+  uint8_t kc[code_bytes(BITS)];
+  uint8_t vc[code_bytes(BITS)];
+  uint16_t kn[kBlock];
+  uint16_t km[kDim];
+  uint16_t ks[kDim];
+  uint16_t vn[kBlock];
+  uint16_t vm[kDim];
+  uint16_t vs[kDim];
+};
+
+// Per-block fp32 metadata in the form the restore uses.  A code k is dropped into
+// mantissa bits [p, p+BITS) of 1.0f, giving x = 1 + k*2^(p-23); then
+//   d = min + scale*k = b*x + a,   b = scale * 2^(23-p),   a = min - b.
+struct MetaF {
+  float ka[kMetaRow], kb[kMetaRow], va[kMetaRow], vb[kMetaRow];
+};
+
+struct MergeSmem {  // cross-warp combine at the end of a chunk (aliases the V tiles)
+  float acc[kWarps][kHeads][kDim];
+  float m[kWarps][kHeads];
+  float l[kWarps][kHeads];
 };
 
 template <int BITS>
 struct AttnSmem {
   Stage<BITS> stage[kStages];
-  // Restored K tiles are the B operand of Q.K^T (K-major: element (token t, channel c)
-  // at byte (t/8)*2048 + (c/8)*128 + (t%8)*16 + (c%8)*2); V tiles the A operand of
-  // V^T.P^T (MN-major: byte (c/8)*1024 + (t/8)*128 + (t%8)*16 + (c%8)*2).
-  alignas(128) uint16_t tile[2][kBlock * kDim];
-  // P, B operand of V^T.P^T (MN-major, N = 16: heads 0..7 P in the bridge dtype, 8..15 the
-  // remainder): element (row n, token t) at byte (n/8)*1024 + (t/8)*128 + (t%8)*16 + (n%8)*2,
-  // so one token's 8 heads are 16 contiguous bytes.
-  alignas(128) uint16_t ptile[2][16 * kBlock];
-  // q rows of this kv head, B operand of K.Q^T (K-major, N = 8): byte (c/8)*128 + g*16 + (c%8)*2.
-  alignas(128) uint16_t qtile[8 * kDim];
-  alignas(16) float scores[kHeads][kScRow];
-  float red[kSoftmaxWarps][kHeads];  // per-warp head maxima / sums of the softmax warps
-  float ssp[2][4][kBlock];           // per unit parity: sum-of-squares partial of each channel group
-  uint64_t full[kStages], ready[kStages], empty[kStages];
-  uint64_t tfull[2], tempty[2], pfull[2], pempty[2], d1full[2], d1empty[2];
-  uint64_t d2full, done;
-  uint32_t tmem_base;
-  int abort;
+  MetaF meta[2];
+  union {
+    uint16_t v16[kWarps][16][kVRow];  // each warp's restored V rows (bridge dtype)
+    MergeSmem merge;
+  } u;
+  uint64_t full[kStages];
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
@@ -130,101 +118,36 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float2 v) {
 }
 template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t u) { return Elem<T>::to_f2(u); }
 
-__device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
-
-// ----------------------------------------------------------------- tcgen05 / TMEM
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// Shared-memory operand descriptor, no swizzle: core matrices of 8 rows x 16 bytes
-// stored contiguously; lbo = byte distance of core matrices along K, sbo = along M/N.
-// Fields: start>>4 [0,14), lbo>>4 [16,30), sbo>>4 [32,46), version 1 [46,48), layout 0.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
-}
-
-// Instruction descriptor of tcgen05.mma kind::f16 with an fp32 accumulator: D format
-// [4,6) = 1, A/B format [7,10)/[10,13) = 0 f16 | 1 bf16, A/B major [15]/[16] (0 K-major,
-// 1 MN-major), N>>3 at [17,23), M>>4 at [24,29).
 template <typename T>
-__host__ __device__ constexpr uint32_t umma_idesc(int m, int n, int a_mn, int b_mn) {
-  return (1u << 4) | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7) |
-         ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | (static_cast<uint32_t>(a_mn) << 15) |
-         (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-
-// One arrival on bar once every tcgen05.mma issued so far by this thread has completed.
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// Orders this thread's shared-memory writes before later reads by the tensor core.
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-// Lane i of the warp reads TMEM lane (taddr lane + i), 16 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Bounded wait that also gives up once another role has timed out (abort flag).  Each
-// try sleeps until the phase completes or kTrySleepNs pass; at most kTryWaits tries.
-constexpr uint32_t kTrySleepNs = 10000;
-constexpr uint32_t kTryWaits = 1u << 15;  // ~0.33 s in all
-
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(kTrySleepNs)
-      : "memory");
-  return ok != 0;
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, int32_t *status, volatile int *abort) {
-  for (int i = 0; i < 64; ++i)  // short spin first: a sleeping thread resumes late
-    if (mbar_try_wait(bar, parity)) return true;
-  for (uint32_t i = 0; i < kTryWaits; ++i) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
-    if (*abort) return false;
-  }
-  *abort = 1;
-  set_status(status, NSNKV_ST_TIMEOUT);
-  return false;
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *smem_row) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
 }
+
+__device__ __forceinline__ bool finite2(float2 v) { return isfinite(v.x) && isfinite(v.y); }
 
 // The packed codes of one lane's 32 channels of one token row.  A row is 4*BITS
 // words and a lane's group BITS words, so the group is always word aligned.
@@ -243,7 +166,7 @@ struct RowCodes {
     if (bi > dst) return __funnelshift_r(w[wi], wi + 1 < BITS ? w[wi + 1] : 0u, bi - dst);
     return __funnelshift_l(wi > 0 ? w[wi - 1] : 0u, w[wi], dst - bi);
   }
-  // x for codes 2m and 2m+1 (see Stage).
+  // x for codes 2m and 2m+1 (see MetaF).
   __device__ __forceinline__ float2 xpair(int m) const {
     if (BITS == 3) {
       const uint32_t ws = place(6 * m, 17);
@@ -256,36 +179,69 @@ struct RowCodes {
   }
 };
 
-// norm / max(||d||, eps) from the row sum of squares (0 when the stored norm is 0).
-__device__ __forceinline__ float renorm(float n, float ss) {
-  return n == 0.f ? 0.f : (ss > 1e-24f ? n * rsqrtf(ss) : n * 1e12f);
-}
-
-// This lane's 32 channels (group cg) of token t: d = min + scale*code (fp32, pairs) and
-// their sum of squares.
+// d for this lane's 32 channels of one row, plus the full-row sum of squares.
 template <int BITS>
-__device__ __forceinline__ float restore_part(const uint8_t *codes, const float *ma, const float *mb, int mi, int t,
-                                              int cg, float2 (&d)[16]) {
-  RowCodes<BITS> rc;
-  rc.load(codes, t, cg);
-  float2 s0 = f2(0.f, 0.f), s1 = f2(0.f, 0.f);
+__device__ __forceinline__ float row_dirs(const RowCodes<BITS> &rc, const float *ma, const float *mb, int mi,
+                                          float2 (&d)[16]) {
+  float2 ss0 = f2(0.f, 0.f), ss1 = f2(0.f, 0.f);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const float4 a4 = *reinterpret_cast<const float4 *>(&ma[mi + 4 * q]);
     const float4 b4 = *reinterpret_cast<const float4 *>(&mb[mi + 4 * q]);
     d[2 * q] = __ffma2_rn(f2(b4.x, b4.y), rc.xpair(2 * q), f2(a4.x, a4.y));
     d[2 * q + 1] = __ffma2_rn(f2(b4.z, b4.w), rc.xpair(2 * q + 1), f2(a4.z, a4.w));
-    s0 = __ffma2_rn(d[2 * q], d[2 * q], s0);
-    s1 = __ffma2_rn(d[2 * q + 1], d[2 * q + 1], s1);
+    ss0 = __ffma2_rn(d[2 * q], d[2 * q], ss0);
+    ss1 = __ffma2_rn(d[2 * q + 1], d[2 * q + 1], ss1);
   }
-  return (s0.x + s1.x) + (s0.y + s1.y);
+  float s = (ss0.x + ss1.x) + (ss0.y + ss1.y);
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  return s;
 }
 
-// k = al * d rounded to the bridge dtype; out packs channel pairs.
-template <typename T>
-__device__ __forceinline__ void restore_finish(const float2 (&d)[16], float al, uint32_t (&out)[16]) {
+// Restore two rows (this lane's 32 channels of tokens t0 and t1) with their work
+// interleaved, renormalise and round to the bridge dtype: out0/out1 pack channel pairs.
+template <int BITS, typename T>
+__device__ __forceinline__ void restore_two_rows(const uint8_t *codes, const float *ma, const float *mb, int mi,
+                                                 int t0, int t1, int tig, float n0, float n1, uint32_t (&out0)[16],
+                                                 uint32_t (&out1)[16]) {
+  RowCodes<BITS> r0, r1;
+  r0.load(codes, t0, tig);
+  r1.load(codes, t1, tig);
+  float2 d0[16], d1[16];
+  float2 s0 = f2(0.f, 0.f), s1 = f2(0.f, 0.f);
 #pragma unroll
-  for (int m = 0; m < 16; ++m) out[m] = pack2<T>(__fmul2_rn(d[m], f2(al, al)));
+  for (int q = 0; q < 8; ++q) {
+    const float4 a4 = *reinterpret_cast<const float4 *>(&ma[mi + 4 * q]);
+    const float4 b4 = *reinterpret_cast<const float4 *>(&mb[mi + 4 * q]);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int m = 2 * q + e;
+      const float2 a2 = e ? f2(a4.z, a4.w) : f2(a4.x, a4.y);
+      const float2 b2 = e ? f2(b4.z, b4.w) : f2(b4.x, b4.y);
+      d0[m] = __ffma2_rn(b2, r0.xpair(m), a2);
+      d1[m] = __ffma2_rn(b2, r1.xpair(m), a2);
+      s0 = __ffma2_rn(d0[m], d0[m], s0);
+      s1 = __ffma2_rn(d1[m], d1[m], s1);
+    }
+  }
+  float ss0 = s0.x + s0.y, ss1 = s1.x + s1.y;
+  ss0 += __shfl_xor_sync(0xffffffffu, ss0, 1);
+  ss1 += __shfl_xor_sync(0xffffffffu, ss1, 1);
+  ss0 += __shfl_xor_sync(0xffffffffu, ss0, 2);
+  ss1 += __shfl_xor_sync(0xffffffffu, ss1, 2);
+  const float al0 = n0 == 0.f ? 0.f : (ss0 > 1e-24f ? n0 * rsqrtf(ss0) : n0 * 1e12f);
+  const float al1 = n1 == 0.f ? 0.f : (ss1 > 1e-24f ? n1 * rsqrtf(ss1) : n1 * 1e12f);
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    out0[m] = pack2<T>(__fmul2_rn(d0[m], f2(al0, al0)));
+    out1[m] = pack2<T>(__fmul2_rn(d1[m], f2(al1, al1)));
+  }
+}
+
+// norm / max(||d||, eps) from the row sum of squares (0 when the stored norm is 0).
+__device__ __forceinline__ float renorm(float n, float ss) {
+  return n == 0.f ? 0.f : (ss > 1e-24f ? n * rsqrtf(ss) : n * 1e12f);
 }
 
 template <typename T>
@@ -309,20 +265,109 @@ __device__ __forceinline__ int check_row32(const uint32_t (&u)[16]) {
   return bad ? NSNKV_ST_INPUT_NONFINITE : 0;
 }
 
+// Round 32 floats (16 pairs) to the bridge dtype and store them as 64 contiguous bytes.
+template <typename T>
+__device__ __forceinline__ void store_pairs(uint16_t *dst, const float2 (&d)[16]) {
+  uint4 *p = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    p[i] = make_uint4(pack2<T>(d[4 * i]), pack2<T>(d[4 * i + 1]), pack2<T>(d[4 * i + 2]), pack2<T>(d[4 * i + 3]));
+}
+
 __device__ __forceinline__ void store_row32(uint16_t *dst, const uint32_t (&u)[16]) {
   uint4 *p = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
   for (int i = 0; i < 4; ++i) p[i] = make_uint4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]);
 }
 
-template <int BITS, typename T>
-__global__ void __launch_bounds__(kThreads, 2) attn_partial_kernel(const AttnArgs a) {
-  constexpr int CB = code_bytes(BITS);
+// Per-warp online softmax state and accumulator.  Lane (g, tig) owns query head g
+// (m, l) and the accumulator of channels 16mt + {g, g+8}, heads 2tig, 2tig+1.
+struct WarpState {
+  float m = -INFINITY, l = 0.f;
+  float acc[8][4];
+};
+
+// Scores of this warp's 16-token tile for query head g, from one K row (n-tile) at a
+// time: s[0..1] = tokens {2tig, 2tig+1} (row t0 of each lane), s[2..3] = tokens
+// {8+2tig, 9+2tig} (row t1).  D[head][token] = q . k over the 8 channel slices; A rows
+// 8..15 are zero.
+template <typename T>
+__device__ __forceinline__ void qk_rows(const uint32_t (&aq)[16], const uint32_t (&k)[16], float (&s)[4]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mma16816<T>(s, aq[2 * j], 0u, aq[2 * j + 1], 0u, k[2 * j], k[2 * j + 1]);
+}
+
+// Online softmax of one 16-token tile and the P.V update.  sc holds the raw scores
+// (sc[0..1] tokens 2tig, 2tig+1; sc[2..3] tokens 8+2tig, 9+2tig; head g), v16 the tile's
+// V rows in the bridge dtype; valid[i] masks token i.
+template <typename T>
+__device__ __forceinline__ void warp_softmax_pv(WarpState &ws, const float (&raw)[4], const uint16_t (*v16)[kVRow],
+                                                const bool (&valid)[4], int G, int lane, int &st) {
   constexpr float kLog2e = 1.4426950408889634f;
+  const int g = lane >> 2, tig = lane & 3;
+  float sc[4];
+  float bmax = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sc[i] = valid[i] ? raw[i] * kScale : -INFINITY;
+    if (valid[i] && g < G && !isfinite(sc[i])) st |= NSNKV_ST_OUTPUT_NONFINITE;
+    bmax = fmaxf(bmax, sc[i]);
+  }
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+  bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+  const float mnew = fmaxf(ws.m, bmax);
+  float r = 1.f, psum = 0.f, p[4];
+  if (g < G && mnew != -INFINITY) {
+    r = exp2f((ws.m - mnew) * kLog2e);
+    const float mb = mnew * kLog2e;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p[i] = exp2f(fmaf(sc[i], kLog2e, -mb));
+      psum += p[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = 0.f;
+  }
+  psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+  psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+  ws.l = ws.l * r + psum;
+  ws.m = mnew;
+  // rescale the accumulator only when some head's running max moved in this warp
+  if (!__all_sync(0xffffffffu, r == 1.f)) {
+    const float r0 = __shfl_sync(0xffffffffu, r, 8 * tig), r1 = __shfl_sync(0xffffffffu, r, 8 * tig + 4);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      ws.acc[mt][0] *= r0;
+      ws.acc[mt][1] *= r1;
+      ws.acc[mt][2] *= r0;
+      ws.acc[mt][3] *= r1;
+    }
+  }
+  // B fragments of P (tokens 2tig, 2tig+1 | 8+2tig, 9+2tig; column = head g), split into
+  // hi + lo halves of the bridge dtype so the weights keep fp32 accuracy
+  const uint32_t bh0 = pack2<T>(f2(p[0], p[1])), bh1 = pack2<T>(f2(p[2], p[3]));
+  const float2 ha = unpack2<T>(bh0), hb = unpack2<T>(bh1);
+  const uint32_t bl0 = pack2<T>(f2(p[0] - ha.x, p[1] - ha.y)), bl1 = pack2<T>(f2(p[2] - hb.x, p[3] - hb.y));
+  const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    uint32_t a[4];
+    ldmatrix_x4_trans(a, &v16[rr + 8 * (mi >> 1)][16 * mt + 8 * (mi & 1)]);
+    mma16816<T>(ws.acc[mt], a[0], a[1], a[2], a[3], bh0, bh1);
+    mma16816<T>(ws.acc[mt], a[0], a[1], a[2], a[3], bl0, bl1);
+  }
+}
+
+template <int BITS, typename T>
+__global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
+  constexpr int CB = code_bytes(BITS);
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS> &S = *reinterpret_cast<AttnSmem<BITS> *>(smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tig = lane & 3, cbase = 32 * tig, mi = meta_index(cbase);
+  const int t0 = 16 * warp + g, t1 = t0 + 8;
   const int chunk = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int G = a.hq / a.h;
@@ -333,337 +378,208 @@ __global__ void __launch_bounds__(kThreads, 2) attn_partial_kernel(const AttnArg
   const int n_sealed_chunks = (nb + a.chunk_blocks - 1) / a.chunk_blocks;
   const int raw_per_chunk = a.chunk_blocks * kBlock;
   const int n_chunks = n_sealed_chunks + (tail_total + raw_per_chunk - 1) / raw_per_chunk;
-  if (chunk >= n_chunks) return;  // the whole CTA, before any barrier or TMEM allocation
+  if (chunk >= n_chunks) return;
   const bool is_raw = chunk >= n_sealed_chunks;
-  int blk0 = 0, raw0 = 0, raw1 = 0, n = 0;
-  if (!is_raw) {
-    blk0 = chunk * a.chunk_blocks;
-    n = min(nb, blk0 + a.chunk_blocks) - blk0;
-  } else {
-    raw0 = (chunk - n_sealed_chunks) * raw_per_chunk;
-    raw1 = min(tail_total, raw0 + raw_per_chunk);
-    n = (raw1 - raw0 + kBlock - 1) / kBlock;
-  }
-  const int units = 2 * n;  // K units 0..n-1, then V units n..2n-1
-  volatile int *abort = &S.abort;
+
   int st = 0;
+  // A fragments of q (rows = query heads h*G + g, zero when g >= G; rows 8..15 zero)
+  uint32_t aq[16];
+  if (g < G) {
+    load_row32<T>(static_cast<const T *>(a.q) + ((b * a.hq) + h * G + g) * kDim, cbase, aq);
+    st |= check_row32<T>(aq);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) aq[i] = 0u;
+  }
+  WarpState ws;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) ws.acc[mt][0] = ws.acc[mt][1] = ws.acc[mt][2] = ws.acc[mt][3] = 0.f;
+  uint16_t (*v16)[kVRow] = S.u.v16[warp];
+  const bool all_valid[4] = {true, true, true, true};
 
-  // ---- set-up: barriers, TMEM, the q operand
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&S.full[i], 1);
-      mbar_init(&S.ready[i], 1);
-      mbar_init(&S.empty[i], kRestoreWarps);
+  if (!is_raw) {
+    const int blk0 = chunk * a.chunk_blocks;
+    const int nloc = min(nb, blk0 + a.chunk_blocks) - blk0;
+    auto issue = [&](int i, int s) {
+      const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
+      const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
+      Stage<BITS> &sg = S.stage[s];
+      mbar_expect_tx(&S.full[s], 2 * CB + 2 * (kBlock * 2 + 2 * kDim * 2));
+      bulk_g2s(sg.kc, a.kc + bi * CB, CB, &S.full[s]);
+      bulk_g2s(sg.vc, a.vc + bi * CB, CB, &S.full[s]);
+      bulk_g2s(sg.kn, a.kn + bi * kBlock, kBlock * 2, &S.full[s]);
+      bulk_g2s(sg.km, a.km + bi * kDim, kDim * 2, &S.full[s]);
+      bulk_g2s(sg.ks, a.ks + bi * kDim, kDim * 2, &S.full[s]);
+      bulk_g2s(sg.vn, a.vn + bi * kBlock, kBlock * 2, &S.full[s]);
+      bulk_g2s(sg.vm, a.vm + bi * kDim, kDim * 2, &S.full[s]);
+      bulk_g2s(sg.vs, a.vs + bi * kDim, kDim * 2, &S.full[s]);
+    };
+    if (tid == 0) {
+#pragma unroll
+      for (int i = 0; i < kStages; ++i) mbar_init(&S.full[i], 1);
+      fence_mbar_init();
+      for (int i = 0; i < kStages && i < nloc; ++i) issue(blk0 + i, i);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&S.tfull[i], kRestoreWarps);
-      mbar_init(&S.tempty[i], 1);
-      mbar_init(&S.pfull[i], kSoftmaxWarps);
-      mbar_init(&S.pempty[i], 1);
-      mbar_init(&S.d1full[i], 1);
-      mbar_init(&S.d1empty[i], kSoftmaxWarps);
-    }
-    mbar_init(&S.d2full, 1);
-    mbar_init(&S.done, 1);
-    S.abort = 0;
-    fence_mbar_init();
-  }
-  if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&S.tmem_base)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (warp == kSoftmaxWarp0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int pc = lane + 32 * i, r = pc & 7, c8 = pc >> 3;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < G) {
-        v = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.q) + ((b * a.hq) + h * G + r) * kDim + 8 * c8);
-        if (!finite2(unpack2<T>(v.x)) || !finite2(unpack2<T>(v.y)) || !finite2(unpack2<T>(v.z)) ||
-            !finite2(unpack2<T>(v.w)))
-          st |= NSNKV_ST_INPUT_NONFINITE;
-      }
-      *reinterpret_cast<uint4 *>(&S.qtile[c8 * 64 + r * 8]) = v;
-    }
-    fence_async_smem();
-  }
-  tc_fence_before();
-  __syncthreads();  // barriers initialised, TMEM address and q tile visible
-  tc_fence_after();
-  const uint32_t tmem = S.tmem_base;
-
-  if (warp < kRestoreWarps) {
-    // ---------------- restore: channel group cg of tokens 32*th..32*th+31 (lane = token)
-    const int cg = warp & 3, th = warp >> 2, t = 32 * th + lane, mi = meta_index(32 * cg);
-    const bool can_store = tl < a.tsh;
-    if (is_raw && a.knew && !can_store && tl >= raw0 && tl < raw1 && tid == 0) st |= NSNKV_ST_CAPACITY;
-    for (int u = 0; u < units; ++u) {
-      const bool isv = u >= n;
-      const int ui = isv ? u - n : u;
-      const int s = u % kStages;
-      if (!is_raw && !__all_sync(0xffffffffu, tc_wait(&S.ready[s], (u / kStages) & 1, a.status, abort))) break;
-      if (u >= 2 && !__all_sync(0xffffffffu, tc_wait(&S.tempty[u & 1], ((u >> 1) - 1) & 1, a.status, abort))) break;
-      uint32_t row[16];
-      if (!is_raw) {
-        const Stage<BITS> &sg = S.stage[s];
-        float2 d[16];
-        S.ssp[u & 1][cg][t] = restore_part<BITS>(sg.codes, sg.fa, sg.fb, mi, t, cg, d);
-        // the four channel groups of this token half exchange their partial sums
-        asm volatile("bar.sync %0, 128;" ::"r"(2 + th) : "memory");
-        const float ss = (S.ssp[u & 1][0][t] + S.ssp[u & 1][1][t]) + (S.ssp[u & 1][2][t] + S.ssp[u & 1][3][t]);
-        restore_finish<T>(d, renorm(half_bits_to_f(sg.norm[t]), ss), row);
-      } else {
-        const int j = raw0 + ui * kBlock + t;
-        const T *base = static_cast<const T *>(isv ? a.vt : a.kt) + (b * a.tss + h * a.tsh) * kDim;
-        const void *fresh_v = isv ? a.vnew : a.knew;
-        const T *fresh = fresh_v ? static_cast<const T *>(fresh_v) + (b * a.h + h) * kDim : nullptr;
-        if (j < raw1) {
-          const bool is_new = fresh && j == tl;
-          load_row32<T>(is_new ? fresh : base + static_cast<int64_t>(j) * kDim, 32 * cg, row);
-          st |= check_row32<T>(row);
-          // the appended token is written into the tail buffer at index tl
-          if (is_new && can_store)
-            store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(base) + static_cast<int64_t>(j) * kDim) + 32 * cg,
-                        row);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) row[i] = 0u;
-        }
-      }
-      uint16_t *tile = S.tile[u & 1];
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int c8 = 4 * cg + jj;
-        const int off = isv ? c8 * 512 + (t >> 3) * 64 + (t & 7) * 8 : (t >> 3) * 1024 + c8 * 64 + (t & 7) * 8;
-        *reinterpret_cast<uint4 *>(tile + off) = make_uint4(row[4 * jj], row[4 * jj + 1], row[4 * jj + 2], row[4 * jj + 3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&S.tfull[u & 1]);
-        if (!is_raw) mbar_arrive(&S.empty[s]);
-      }
-    }
-    // ---------------- epilogue: warps 0..3 read the P.V accumulator of channels 32w..32w+31
-    if (warp < 4 && __all_sync(0xffffffffu, tc_wait(&S.d2full, 0, a.status, abort))) {
-      tc_fence_after();
-      uint32_t r[16];
-      tmem_ld16(tmem + (static_cast<uint32_t>(32 * warp) << 16) + 16u, r);
-      tmem_wait_ld();
-      const int c = 32 * warp + lane;
-#pragma unroll
-      for (int gg = 0; gg < kHeads; ++gg) {
-        if (gg < G) {
-          const int64_t prow = (b * a.hq + h * G + gg) * a.max_chunks + chunk;
-          a.part_o[prow * kDim + c] = __uint_as_float(r[gg]) + __uint_as_float(r[kHeads + gg]);
-        }
-      }
-    }
-  } else if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + kSoftmaxWarps) {
-    // ---------------- softmax: K phase (scores, exact chunk maximum) then V phase (P).
-    // Lane l < 16 of warp 8+q owns token 16q + l of every unit.
-    const int q = warp - kSoftmaxWarp0, t = 16 * q + (lane & 15);
-    const bool act = lane < 16;
-    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
-    float m[kHeads];
-#pragma unroll
-    for (int g = 0; g < kHeads; ++g) m[g] = -INFINITY;
-    bool ok = true;
-    for (int u = 0; u < n; ++u) {
-      ok = __all_sync(0xffffffffu, tc_wait(&S.d1full[u & 1], (u >> 1) & 1, a.status, abort));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t r[8];
-      tmem_ld8(tq + 8u * (u & 1), r);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.d1empty[u & 1]);
-      const int valid = is_raw ? min(kBlock, raw1 - (raw0 + u * kBlock)) : kBlock;
-      if (act) {
-#pragma unroll
-        for (int g = 0; g < kHeads; ++g) {
-          const float sc = t < valid ? __uint_as_float(r[g]) * kScale : -INFINITY;
-          m[g] = fmaxf(m[g], sc);
-          S.scores[g][u * kBlock + t] = sc;
-        }
-      }
-    }
-    // chunk maximum of each head: over the 16 lanes, then over the four warps
-#pragma unroll
-    for (int g = 0; g < kHeads; ++g) {
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < kHeads; ++g) S.red[q][g] = m[g];
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
-    float mb[kHeads];
-#pragma unroll
-    for (int g = 0; g < kHeads; ++g) {
-      m[g] = fmaxf(fmaxf(S.red[0][g], S.red[1][g]), fmaxf(S.red[2][g], S.red[3][g]));
-      mb[g] = m[g] * kLog2e;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");  // S.red is reused for the sums
-    float l[kHeads];
-#pragma unroll
-    for (int g = 0; g < kHeads; ++g) l[g] = 0.f;
-    for (int v = 0; v < n && ok; ++v) {
-      const int pb = v & 1;
-      if (v >= 2) {
-        ok = __all_sync(0xffffffffu, tc_wait(&S.pempty[pb], ((v >> 1) - 1) & 1, a.status, abort));
-        if (!ok) break;
-      }
-      if (act) {
-        float p[kHeads];
-#pragma unroll
-        for (int g = 0; g < kHeads; ++g) {
-          const float sc = S.scores[g][v * kBlock + t];
-          p[g] = (g < G && m[g] != -INFINITY) ? exp2f(fmaf(sc, kLog2e, -mb[g])) : 0.f;
-          l[g] += p[g];
-        }
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          hi[i] = pack2<T>(f2(p[2 * i], p[2 * i + 1]));
-          const float2 hv = unpack2<T>(hi[i]);
-          lo[i] = pack2<T>(f2(p[2 * i] - hv.x, p[2 * i + 1] - hv.y));
-        }
-        uint16_t *pt = S.ptile[pb] + (t >> 3) * 64 + (t & 7) * 8;
-        *reinterpret_cast<uint4 *>(pt) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4 *>(pt + 512) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.pfull[pb]);
-    }
-#pragma unroll
-    for (int g = 0; g < kHeads; ++g) {
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < kHeads; ++g) S.red[q][g] = l[g];
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
-    if (ok && q == 0 && lane < G) {
-      float lm = 0.f, ls = 0.f;
-#pragma unroll
-      for (int g = 0; g < kHeads; ++g) {
-        if (g == lane) {
-          lm = m[g];
-          ls = (S.red[0][g] + S.red[1][g]) + (S.red[2][g] + S.red[3][g]);
-        }
-      }
-      const int64_t prow = (b * a.hq + h * G + lane) * a.max_chunks + chunk;
-      a.part_ml[prow * 2] = lm;
-      a.part_ml[prow * 2 + 1] = ls;
-    }
-  } else if (warp == kProducerWarp) {
-    // ---------------- producer: TMA ring and restore coefficients (sealed chunks)
-    if (!is_raw) {
-      const float fac = static_cast<float>(1 << (23 - code_pos<BITS>(lane)));
-      int issued = 0, landed = 0;
-      auto issue = [&](int u) {
-        const int s = u % kStages;
-        const bool isv = u >= n;
-        const int i = blk0 + (isv ? u - n : u);
-        const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
-        const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
-        Stage<BITS> &sg = S.stage[s];
-        if (lane == 0) {
-          mbar_expect_tx(&S.full[s], CB + kBlock * 2 + 2 * kDim * 2);
-          bulk_g2s(sg.codes, (isv ? a.vc : a.kc) + bi * CB, CB, &S.full[s]);
-          bulk_g2s(sg.norm, (isv ? a.vn : a.kn) + bi * kBlock, kBlock * 2, &S.full[s]);
-          bulk_g2s(sg.mn, (isv ? a.vm : a.km) + bi * kDim, kDim * 2, &S.full[s]);
-          bulk_g2s(sg.sc, (isv ? a.vs : a.ks) + bi * kDim, kDim * 2, &S.full[s]);
-        }
-        ++issued;
-      };
-      for (int u = 0; u < units && u < kStages; ++u) issue(u);
-      for (int u = 0; u < units; ++u) {
-        const int s = u % kStages;
-        if (!__all_sync(0xffffffffu, tc_wait(&S.full[s], (u / kStages) & 1, a.status, abort))) break;
-        ++landed;
-        Stage<BITS> &sg = S.stage[s];
-        bool bad = false;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = lane + 32 * i, ci = meta_index(c);
-          const float m = half_bits_to_f(sg.mn[c]), sc = half_bits_to_f(sg.sc[c]);
-          const float bb = sc * fac;
-          sg.fa[ci] = m - bb;
-          sg.fb[ci] = bb;
-          bad |= !isfinite(m) || !isfinite(sc);
-        }
-        bad |= !isfinite(half_bits_to_f(sg.norm[lane])) || !isfinite(half_bits_to_f(sg.norm[lane + 32]));
+    __syncthreads();  // no thread may poll a barrier before thread 0 has initialised it
+    const float fac = static_cast<float>(1 << (23 - code_pos<BITS>(tid & 31)));
+    for (int li = 0; li < nloc; ++li) {
+      const int s = li % kStages;
+      const bool ok = mbar_wait_bounded(&S.full[s], (li / kStages) & 1, a.status);
+      const Stage<BITS> &sg = S.stage[s];
+      MetaF &mf = S.meta[li & 1];
+      if (ok) {  // fp32 metadata of this block, one channel per thread
+        const int ci = meta_index(tid);
+        const float km = half_bits_to_f(sg.km[tid]), ks = half_bits_to_f(sg.ks[tid]);
+        const float vm = half_bits_to_f(sg.vm[tid]), vs = half_bits_to_f(sg.vs[tid]);
+        const float kb_ = ks * fac, vb_ = vs * fac;
+        mf.ka[ci] = km - kb_;
+        mf.kb[ci] = kb_;
+        mf.va[ci] = vm - vb_;
+        mf.vb[ci] = vb_;
+        bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
+        if (tid < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[tid])) || !isfinite(half_bits_to_f(sg.vn[tid]));
         if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.ready[s]);
-        const int nx = u - 1 + kStages;
-        if (u >= 1 && nx < units) {
-          if (!__all_sync(0xffffffffu, tc_wait(&S.empty[(u - 1) % kStages], ((u - 1) / kStages) & 1, a.status, abort)))
-            break;
-          issue(nx);
+      }
+      if (__syncthreads_or(!ok)) {
+        // A staged copy never landed: give the later copies a bounded chance to
+        // finish, then leave; the timeout status tells the host.
+        if (tid == 0)
+          for (int k = li + 1; k < nloc && k < li + kStages; ++k)
+            mbar_wait_bounded(&S.full[k % kStages], (k / kStages) & 1, a.status);
+        return;
+      }
+      // every warp has finished block li-1: its stage takes block li-1+kStages
+      if (tid == 0 && li >= 1 && li - 1 + kStages < nloc) issue(blk0 + li - 1 + kStages, (li - 1) % kStages);
+      // ---- V rows t0, t1: restore, renormalise, round to the bridge dtype (the value
+      // restore_group stores) into this warp's V tile
+      {
+        uint32_t u0[16], u1[16];
+        restore_two_rows<BITS, T>(sg.vc, mf.va, mf.vb, mi, t0, t1, tig, half_bits_to_f(sg.vn[t0]),
+                                  half_bits_to_f(sg.vn[t1]), u0, u1);
+        store_row32(&v16[g][cbase], u0);
+        store_row32(&v16[g + 8][cbase], u1);
+      }
+      // ---- K rows t0, t1: the same restore, then the scores of both rows
+      float sraw[4];
+      {
+        uint32_t k0[16], k1[16];
+        restore_two_rows<BITS, T>(sg.kc, mf.ka, mf.kb, mi, t0, t1, tig, half_bits_to_f(sg.kn[t0]),
+                                  half_bits_to_f(sg.kn[t1]), k0, k1);
+        // four independent accumulation chains per row (two slices each) shorten the
+        // dependent MMA sequence; their sum is the score
+        float s0[4][4], s1[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s0[c][i] = s1[c][i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          mma16816<T>(s0[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k0[2 * j], k0[2 * j + 1]);
+          mma16816<T>(s1[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k1[2 * j], k1[2 * j + 1]);
+        }
+        sraw[0] = (s0[0][0] + s0[1][0]) + (s0[2][0] + s0[3][0]);
+        sraw[1] = (s0[0][1] + s0[1][1]) + (s0[2][1] + s0[3][1]);
+        sraw[2] = (s1[0][0] + s1[1][0]) + (s1[2][0] + s1[3][0]);
+        sraw[3] = (s1[0][1] + s1[1][1]) + (s1[2][1] + s1[3][1]);
+      }
+      __syncwarp();
+      warp_softmax_pv<T>(ws, sraw, v16, all_valid, G, lane, st);
+      __syncwarp();
+    }
+  } else {
+    // ---- native rows (tail, appended token, or materialised K/V), per warp 16 rows of each 64-row tile
+    const T *ktb = static_cast<const T *>(a.kt) + (b * a.tss + h * a.tsh) * kDim;
+    const T *vtb = static_cast<const T *>(a.vt) + (b * a.tss + h * a.tsh) * kDim;
+    const T *kn_row = a.knew ? static_cast<const T *>(a.knew) + (b * a.h + h) * kDim : nullptr;
+    const T *vn_row = a.vnew ? static_cast<const T *>(a.vnew) + (b * a.h + h) * kDim : nullptr;
+    const int raw0 = (chunk - n_sealed_chunks) * raw_per_chunk;
+    const int raw1 = min(tail_total, raw0 + raw_per_chunk);
+    const bool can_store = tl < a.tsh;
+    if (a.knew && !can_store && tl >= raw0 && tl < raw1 && tid == 0) st |= NSNKV_ST_CAPACITY;
+    const int ntiles = (raw1 - raw0 + kBlock - 1) / kBlock;
+    for (int tile = 0; tile < ntiles; ++tile) {
+      const int j0 = raw0 + tile * kBlock + t0, j1 = raw0 + tile * kBlock + t1;
+      const bool v0 = j0 < raw1, v1 = j1 < raw1;
+      auto row_ptr = [&](const T *base, const T *fresh_row, int j) -> const T * {
+        return (fresh_row && j == tl) ? fresh_row : base + static_cast<int64_t>(j) * kDim;
+      };
+      uint32_t ka[16], kb[16], va[16], vb[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ka[i] = kb[i] = va[i] = vb[i] = 0u;
+      if (v0) {
+        load_row32<T>(row_ptr(ktb, kn_row, j0), cbase, ka);
+        load_row32<T>(row_ptr(vtb, vn_row, j0), cbase, va);
+        st |= check_row32<T>(ka) | check_row32<T>(va);
+      }
+      if (v1) {
+        load_row32<T>(row_ptr(ktb, kn_row, j1), cbase, kb);
+        load_row32<T>(row_ptr(vtb, vn_row, j1), cbase, vb);
+        st |= check_row32<T>(kb) | check_row32<T>(vb);
+      }
+      if (kn_row && can_store) {
+        // the appended token is written into the tail buffers at index tl
+        if (v0 && j0 == tl) {
+          store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(ktb) + static_cast<int64_t>(j0) * kDim) + cbase, ka);
+          store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(vtb) + static_cast<int64_t>(j0) * kDim) + cbase, va);
+        }
+        if (v1 && j1 == tl) {
+          store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(ktb) + static_cast<int64_t>(j1) * kDim) + cbase, kb);
+          store_row32(reinterpret_cast<uint16_t *>(const_cast<T *>(vtb) + static_cast<int64_t>(j1) * kDim) + cbase, vb);
         }
       }
-      // copies still in flight after an abort: a bounded wait each before the CTA leaves
-      for (int u = landed; u < issued; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1, a.status);
+      store_row32(&v16[g][cbase], va);
+      store_row32(&v16[g + 8][cbase], vb);
+      // validity of tokens 2tig, 2tig+1, 8+2tig, 9+2tig of this warp's 16 rows
+      const int jb = raw0 + tile * kBlock + 16 * warp;
+      const bool valid[4] = {jb + 2 * tig < raw1, jb + 2 * tig + 1 < raw1, jb + 8 + 2 * tig < raw1,
+                             jb + 9 + 2 * tig < raw1};
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      qk_rows<T>(aq, ka, s0);
+      qk_rows<T>(aq, kb, s1);
+      const float sraw[4] = {s0[0], s0[1], s1[0], s1[1]};
+      __syncwarp();
+      warp_softmax_pv<T>(ws, sraw, v16, valid, G, lane, st);
+      __syncwarp();
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMA issue (one thread)
-    if (lane == 0) {
-      constexpr uint32_t kIdQK = umma_idesc<T>(kBlock, kHeads, 0, 0);
-      constexpr uint32_t kIdPV = umma_idesc<T>(128, 16, 1, 1);
-      const uint32_t qa = smem_addr(S.qtile);
-      for (int u = 0; u < units; ++u) {
-        const int buf = u & 1;
-        if (!tc_wait(&S.tfull[buf], (u >> 1) & 1, a.status, abort)) break;
-        tc_fence_after();
-        const uint32_t ta = smem_addr(S.tile[buf]);
-        if (u < n) {
-          if (u >= 2) {
-            if (!tc_wait(&S.d1empty[buf], ((u >> 1) - 1) & 1, a.status, abort)) break;
-            tc_fence_after();
-          }
-#pragma unroll
-          for (int k = 0; k < kDim / 16; ++k)
-            umma_f16(tmem + 8u * buf, umma_desc(ta + 256u * k, 128u, 2048u), umma_desc(qa + 256u * k, 128u, 1024u),
-                     kIdQK, k);
-          umma_commit(&S.tempty[buf]);
-          umma_commit(&S.d1full[buf]);
-        } else {
-          const int v = u - n, pb = v & 1;
-          if (!tc_wait(&S.pfull[pb], (v >> 1) & 1, a.status, abort)) break;
-          tc_fence_after();
-          const uint32_t pa = smem_addr(S.ptile[pb]);
-#pragma unroll
-          for (int k = 0; k < kBlock / 16; ++k)
-            umma_f16(tmem + 16u, umma_desc(ta + 256u * k, 128u, 1024u), umma_desc(pa + 256u * k, 128u, 1024u), kIdPV,
-                     (v > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&S.tempty[buf]);
-          umma_commit(&S.pempty[pb]);
-          if (v == n - 1) umma_commit(&S.d2full);
-        }
-      }
-      // every MMA issued has completed before TMEM is released
-      umma_commit(&S.done);
-      mbar_wait_bounded(&S.done, 0, a.status);
-    }
-    __syncwarp();
   }
 
-  if (st) set_status(a.status, st);
-  tc_fence_before();
+  // ---- combine the four warps' partials and write this chunk's partial
   __syncthreads();
-  tc_fence_after();
-  if (warp == kMmaWarp)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  MergeSmem &M = S.u.merge;
+  if (tig == 0) {
+    M.m[warp][g] = ws.m;
+    M.l[warp][g] = ws.l;
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int c = 16 * mt + g;
+    M.acc[warp][2 * tig][c] = ws.acc[mt][0];
+    M.acc[warp][2 * tig + 1][c] = ws.acc[mt][1];
+    M.acc[warp][2 * tig][c + 8] = ws.acc[mt][2];
+    M.acc[warp][2 * tig + 1][c + 8] = ws.acc[mt][3];
+  }
+  __syncthreads();
+  constexpr float kLog2e = 1.4426950408889634f;
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
+    float o = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
+      o += wt * M.acc[w][n][c];
+      l += wt * M.l[w][n];
+    }
+    const int64_t row = (b * a.hq + h * G + n) * a.max_chunks + chunk;
+    a.part_o[row * kDim + c] = o;
+    if (c == 0) {
+      a.part_ml[row * 2] = mx;
+      a.part_ml[row * 2 + 1] = l;
+    }
+  }
+  if (st) set_status(a.status, st);
 }
 
 // Combine the chunk partials of one (sequence, query head).
@@ -731,7 +647,7 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   int64_t per_unit = (target + units - 1) / units;  // desired chunks per (seq, head)
   int64_t ch = (work + per_unit - 1) / per_unit;
   if (ch < 4) ch = 4;
-  if (ch > kChunk) ch = kChunk;
+  if (ch > 16) ch = 16;
   return static_cast<int>(ch);
 }
 
