@@ -46,6 +46,15 @@ def peaks():
     return HBM_FALLBACK, "fallback"
 
 
+def traffic_for(bytes_attn):
+    """DRAM bytes per attention launch: the ncu capture's traffic/algorithmic ratio times this launch's bytes."""
+    p = ROOT / "profiles" / "attn_partial_cfg2_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d["traffic_bytes_per_launch"] / d["algorithmic_bytes_that_launch"] * bytes_attn
+
+
 # ------------------------------------------------------------------ clocks sampling
 class ClockSampler:
     """nvidia-smi clocks/throttle sampling during the timed region (every 200 ms)."""
@@ -462,7 +471,9 @@ def main():
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
             "roofline": {"bound": "hbm", "kernel": "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn),
+                         "traffic_note": "ncu dram read+write of attn_partial at one full-size bench launch "
+                                         "(profiles/attn_partial_cfg2.md), scaled to this launch's algorithmic bytes",
                          "bytes_per_launch": bytes_attn},
             "e2e": e2e,
             "gpu_launches": 4 * args.steps,
