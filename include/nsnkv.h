@@ -203,6 +203,14 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
 int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *lse, int dtype,
                        void *out, float *out_f32, float *lse_out, int32_t *status, void *stream);
 
+/*
+ * The same combine over packed per-shard records, the form one all-gather returns:
+ * record s starts at records + s * record_stride (floats) and holds o [rows][128]
+ * followed by lse [rows].  record_stride >= rows * 129.
+ */
+int nsnkv_merge_shard_records(int n_shards, int64_t rows, const float *records, int64_t record_stride, int dtype,
+                              void *out, float *out_f32, float *lse_out, int32_t *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -615,20 +615,22 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G
 }
 
 // Combine per-shard (o, lse) rows: used after an all-gather in the split-KV path.
+// Shard s's rows start at o + s * o_stride and lse_in + s * lse_stride.
 template <typename T>
 __global__ void __launch_bounds__(128) merge_shards_kernel(int n_shards, int64_t rows, const float *o,
-                                                            const float *lse_in, T *out, float *out_f32,
+                                                            int64_t o_stride, const float *lse_in,
+                                                            int64_t lse_stride, T *out, float *out_f32,
                                                             float *lse_out, int32_t *status) {
   const int64_t r = blockIdx.x;
   const int c = threadIdx.x;
   float M = -INFINITY;
-  for (int s = 0; s < n_shards; ++s) M = fmaxf(M, lse_in[s * rows + r]);
+  for (int s = 0; s < n_shards; ++s) M = fmaxf(M, lse_in[s * lse_stride + r]);
   float L = 0.f, acc = 0.f;
   for (int s = 0; s < n_shards; ++s) {
-    const float l = lse_in[s * rows + r];
+    const float l = lse_in[s * lse_stride + r];
     const float w = l == -INFINITY ? 0.f : expf(l - M);
     L += w;
-    acc += w * o[(s * rows + r) * kDim + c];
+    acc += w * o[s * o_stride + r * kDim + c];
   }
   const float y = __fdiv_rn(acc, L);
   const T yt = Elem<T>::from_f(y);
@@ -765,20 +767,35 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
-int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *lse, int dtype, void *out,
-                       float *out_f32, float *lse_out, int32_t *status, void *stream) {
-  if (n_shards <= 0 || rows <= 0 || rows > 0x7FFFFFFF || !o || !lse || !out || !status) return NSNKV_ERR_ARG;
+static int merge_shards_launch(int n_shards, int64_t rows, const float *o, int64_t o_stride, const float *lse,
+                               int64_t lse_stride, int dtype, void *out, float *out_f32, float *lse_out,
+                               int32_t *status, void *stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
   if (dtype == NSNKV_F16)
-    merge_shards_kernel<__half><<<static_cast<unsigned>(rows), kDim, 0, st>>>(n_shards, rows, o, lse,
-                                                                            static_cast<__half *>(out), out_f32,
-                                                                            lse_out, status);
+    merge_shards_kernel<__half><<<grid, kDim, 0, st>>>(n_shards, rows, o, o_stride, lse, lse_stride,
+                                                       static_cast<__half *>(out), out_f32, lse_out, status);
   else if (dtype == NSNKV_BF16)
-    merge_shards_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), kDim, 0, st>>>(
-        n_shards, rows, o, lse, static_cast<__nv_bfloat16 *>(out), out_f32, lse_out, status);
+    merge_shards_kernel<__nv_bfloat16><<<grid, kDim, 0, st>>>(n_shards, rows, o, o_stride, lse, lse_stride,
+                                                              static_cast<__nv_bfloat16 *>(out), out_f32, lse_out,
+                                                              status);
   else
     return NSNKV_ERR_ARG;
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *lse, int dtype, void *out,
+                       float *out_f32, float *lse_out, int32_t *status, void *stream) {
+  if (n_shards <= 0 || rows <= 0 || rows > 0x7FFFFFFF || !o || !lse || !out || !status) return NSNKV_ERR_ARG;
+  return merge_shards_launch(n_shards, rows, o, rows * kDim, lse, rows, dtype, out, out_f32, lse_out, status, stream);
+}
+
+int nsnkv_merge_shard_records(int n_shards, int64_t rows, const float *records, int64_t record_stride, int dtype,
+                              void *out, float *out_f32, float *lse_out, int32_t *status, void *stream) {
+  if (n_shards <= 0 || rows <= 0 || rows > 0x7FFFFFFF || !records || !out || !status) return NSNKV_ERR_ARG;
+  if (record_stride < rows * (kDim + 1)) return NSNKV_ERR_ARG;
+  return merge_shards_launch(n_shards, rows, records, record_stride, records + rows * kDim, record_stride, dtype, out,
+                             out_f32, lse_out, status, stream);
 }
 
 }  // extern "C"

@@ -2,10 +2,11 @@
 
 For one long sequence (cfg4: 2047 INT5 blocks + 64-token tail, GQA 64:8), rank r
 of N holds a contiguous range of sealed blocks (the last rank also holds the
-native tail).  Each rank runs the fused attention over its range and keeps the
-fp32 context and the log-sum-exp of its scores per query head; the (o, lse)
-rows of all ranks are all-gathered (NCCL over NVLink / NVSwitch, about 33 KB per
-rank at cfg4) and combined by ``nsnkv_merge_shards``:
+native tail).  Each rank runs the fused attention over its range, writing the
+fp32 context and the log-sum-exp of its scores per query head straight into one
+send record [o (hq x 128) | lse (hq)]; one all-gather (NCCL over NVLink /
+NVSwitch, about 33 KB per rank at cfg4) collects the records and
+``nsnkv_merge_shard_records`` combines them in place:
 
     L = log sum_r exp(lse_r),  out = sum_r exp(lse_r - L) * o_r.
 
@@ -59,6 +60,31 @@ def merge_shards(O: torch.Tensor, S: torch.Tensor, dtype=torch.float16, out=None
     return out, status
 
 
+def gather_records(rec: torch.Tensor, group=None, out=None):
+    """All-gather one flat fp32 record per rank -> [N * len(rec)] (one collective)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if out is None:
+        out = torch.empty((world * rec.numel(),), dtype=rec.dtype, device=rec.device)
+    dist.all_gather_into_tensor(out, rec, group=group)
+    return out
+
+
+def merge_records(records: torch.Tensor, n_shards: int, rows: int, dtype=torch.float16, out=None, status=None):
+    """Combine gathered records (each [o rows x 128 | lse rows]) with nsnkv_merge_shard_records."""
+    L.require_cuda()
+    dev = records.device
+    if out is None:
+        out = torch.empty((rows, 128), dtype=dtype, device=dev)
+    if status is None:
+        status = L.status_tensor(dev)
+    L.check(L.load().nsnkv_merge_shard_records(n_shards, rows, L.ptr(records), records.numel() // n_shards,
+                                               L.DTYPE_CODE[dtype], L.ptr(out), None, None, L.ptr(status),
+                                               L.stream_handle(dev)),
+            "nsnkv_merge_shard_records")
+    return out, status
+
+
 class ShardedSequence:
     """One rank's share of a long sequence: its block range of K/V (reference group
     layout [1, h, n_r, ...]) plus, on the last rank, the native tail."""
@@ -70,14 +96,20 @@ class ShardedSequence:
         self.n = 0 if k_group is None else k_group["codes"].shape[2]
         self.t = 0 if k_tail is None else k_tail.shape[2]
         dev = (k_group["codes"] if k_group is not None else k_tail).device
-        self.o = torch.empty((hq, 128), dtype=torch.float32, device=dev)
-        self.lse = torch.empty((hq,), dtype=torch.float32, device=dev)
+        # send record: o [hq, 128] then lse [hq], written in place by the attention kernel
+        self.rec = torch.empty((hq * 129,), dtype=torch.float32, device=dev)
+        self.o = self.rec[:hq * 128].view(hq, 128)
+        self.lse = self.rec[hq * 128:]
+        self.recv = None
+        self.lout = torch.empty((1, hq, 128), dtype=(k_tail.dtype if k_tail is not None else torch.float16),
+                                device=dev)
         self.status = L.status_tensor(dev)
 
     def local(self, q, out=None):
         """Fused attention over this rank's share -> fp32 (o, lse) per query head."""
         if out is None:
-            out = torch.empty((1, self.hq, 128), dtype=q.dtype, device=q.device)
+            out = self.lout if self.lout.dtype == q.dtype else torch.empty((1, self.hq, 128), dtype=q.dtype,
+                                                                           device=q.device)
         decode_attention(q.reshape(1, self.hq, 128), group_pool(self.kg, self.h) if self.n else None,
                          group_pool(self.vg, self.h) if self.n else None, h=self.h, bits=self.bits,
                          blk_stride_head=self.n, blk_stride_page=1, n_blocks=self.n, max_blocks=self.n,
@@ -97,9 +129,12 @@ class ShardedSequence:
             res = torch.empty((self.hq, 128), dtype=q.dtype, device=q.device) if out is None else out
             self.local(q, out=res.view(1, self.hq, 128))
             return res
-        o, lse = self.local(q)
-        O, S = gather_partials(o, lse, group)
-        res, _ = merge_shards(O, S, dtype=q.dtype, out=out, status=self.status)
+        self.local(q)
+        world = dist.get_world_size(group)
+        if self.recv is None or self.recv.numel() != world * self.rec.numel():
+            self.recv = torch.empty((world * self.rec.numel(),), dtype=torch.float32, device=self.rec.device)
+        gather_records(self.rec, group, out=self.recv)
+        res, _ = merge_records(self.recv, world, self.hq, dtype=q.dtype, out=out, status=self.status)
         return res
 
     def check(self):

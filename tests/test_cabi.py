@@ -23,7 +23,7 @@ def header_functions():
 def test_header_declares_entry_points():
     decls = header_functions()
     for name in ("nsnkv_encode_blocks", "nsnkv_restore", "nsnkv_pack", "nsnkv_unpack", "nsnkv_decode_attn",
-                 "nsnkv_seal_full_tails", "nsnkv_merge_shards"):
+                 "nsnkv_seal_full_tails", "nsnkv_merge_shards", "nsnkv_merge_shard_records"):
         assert name in decls
 
 

@@ -179,6 +179,12 @@ def test_split_kv_merge_equals_one_pass():
         sh.check()
     out, status = merge_shards(torch.stack(Os), torch.stack(Ss), dtype=torch.float16)
     assert int(status.item()) == 0
+    # the packed-record form (what one all-gather returns) merges to the same bits
+    from nsn_b200.splitkv import merge_records
+    records = torch.cat([torch.cat([o.reshape(-1), s_.reshape(-1)]) for o, s_ in zip(Os, Ss)])
+    out_r, status_r = merge_records(records, world, hq, dtype=torch.float16)
+    assert int(status_r.item()) == 0
+    assert torch.equal(out_r.view(torch.int16), out.view(torch.int16))
     ok, err = O.within_tolerance(out.float().cpu().numpy(), one.cpu().numpy(), *O.TOLERANCE["float16"])
     assert ok, err
     # and against the oracle
