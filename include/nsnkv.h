@@ -211,6 +211,24 @@ int nsnkv_merge_shards(int n_shards, int64_t rows, const float *o, const float *
 int nsnkv_merge_shard_records(int n_shards, int64_t rows, const float *records, int64_t record_stride, int dtype,
                               void *out, float *out_f32, float *lse_out, int32_t *status, void *stream);
 
+/*
+ * Int3AsymNsepPchanCache (src/nsn/cache.py:134-313, from_fp16 / to_fp16): x is
+ * [rows][tokens][dim] (dim % 8 == 0, 8 <= dim <= 256, rows <= 65535) in x_dtype.
+ * Outputs: packed [rows][tokens][3*dim/8] (3-bit indices, 8 per 3 bytes, LSB first:
+ * src/nsn/pack.py:85-128), norm fp16 [rows][tokens], d_min / d_step fp16 [rows][dim].
+ * norm_order: 0 when the caller's channel axis is contiguous (torch's 8-lane norm),
+ * 1 when it is strided (sequential sum), as for nsnkv_encode_blocks.
+ * scratch: device memory of nsnkv_int3asym_scratch_bytes(rows, tokens, dim) bytes.
+ * Status: NSNKV_ST_INPUT_NONFINITE for a non-finite input (the reference does not check).
+ */
+int64_t nsnkv_int3asym_scratch_bytes(int64_t rows, int64_t tokens, int dim);
+int nsnkv_int3asym_encode(const void *x, int x_dtype, int64_t rows, int64_t tokens, int dim, int norm_order,
+                          uint8_t *packed, uint16_t *norm, uint16_t *d_min, uint16_t *d_step, void *scratch,
+                          int64_t scratch_bytes, int32_t *status, void *stream);
+/* to_fp16: out fp16 [rows][tokens][dim] from the fields above. */
+int nsnkv_int3asym_decode(const uint8_t *packed, const uint16_t *norm, const uint16_t *d_min, const uint16_t *d_step,
+                          int64_t rows, int64_t tokens, int dim, uint16_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

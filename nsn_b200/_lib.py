@@ -61,6 +61,9 @@ SIGNATURES = [
                                       P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
+    ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),
+    ("nsnkv_int3asym_encode", c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, P, P, P, P, c_int64, P, P]),
+    ("nsnkv_int3asym_decode", c_int, [P, P, P, P, c_int64, c_int64, c_int, P, P]),
 ]
 
 _lib = None

@@ -57,11 +57,16 @@ class NumericalFailure(RuntimeError):
 
 # ---------------------------------------------------------------- norms
 def row_sumsq_lanes8(a: np.ndarray) -> np.ndarray:
-    """Sum of squares over the last axis (128) in PyTorch's contiguous-row order."""
+    """Sum of squares over the last axis in PyTorch's contiguous-row order.
+
+    The axis length is a multiple of 8 (128 on the block path; the library container
+    also takes 32, 64 and 256, where torch 2.11's CPU order was measured to be the same).
+    """
     a = np.asarray(a, np.float32)
-    assert a.shape[-1] == DIM
+    D = a.shape[-1]
+    assert D % 8 == 0
     acc = a[..., 0:8] * a[..., 0:8]
-    for i in range(8, DIM, 8):
+    for i in range(8, D, 8):
         blk = a[..., i:i + 8]
         acc = acc + blk * blk
     s = acc[..., 0].copy()
@@ -286,3 +291,30 @@ def within_tolerance(got, want, rtol=2e-3, atol=1e-3):
     want = np.asarray(want, np.float64)
     err = np.abs(got - want)
     return bool(np.all(err <= atol + rtol * np.abs(want))), float(err.max()) if err.size else 0.0
+
+
+# ---------------------------------------------------------------- library INT3 container
+def int3asym_encode(x):
+    """Restates Int3AsymNsepPchanCache.from_fp16 (src/nsn/cache.py:183-212).
+
+    x: float32 array [..., T, D] (fp16/bf16 widened exactly).  Returns
+    (idx uint8 [..., T, D], norm f16 [..., T, 1], d_min f16 [..., 1, D],
+    d_step f16 [..., 1, D]); the packed bytes are pack_codes(idx, 3) per token row.
+    """
+    a = np.asarray(x, np.float32)
+    n = np.maximum(row_norm(a), np.float32(1e-12))[..., None]
+    d = (a / n).astype(np.float32)
+    d_min = d.min(axis=-2, keepdims=True)  # numpy keeps the later of equal values, like torch
+    d_max = d.max(axis=-2, keepdims=True)
+    step = (np.maximum(d_max - d_min, np.float32(1e-12)) / np.float32(7)).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        idx = np.clip(np.rint((d - d_min) / step), 0, 7).astype(np.uint8)
+    return idx, n.astype(np.float16), d_min.astype(np.float16), step.astype(np.float16)
+
+
+def int3asym_decode(idx, norm16, d_min16, d_step16):
+    """Restates Int3AsymNsepPchanCache.to_fp16 (src/nsn/cache.py:214-221) -> fp16 [..., T, D]."""
+    dq = (idx.astype(np.float32) * d_step16.astype(np.float32)).astype(np.float32) + d_min16.astype(np.float32)
+    dq = dq.astype(np.float32)
+    den = np.maximum(np.sqrt(row_sumsq_lanes8(dq)).astype(np.float32), np.float32(1e-8))[..., None]
+    return (norm16.astype(np.float32) * (dq / den).astype(np.float32)).astype(np.float32).astype(np.float16)

@@ -357,12 +357,55 @@ def gen_cache():
         w.LAYERS, w.HEADS = old
 
 
+# ------------------------------------------------------------------ library INT3 container (src/nsn)
+def gen_int3asym():
+    sys.path.insert(0, str(REF / "src"))
+    from nsn.cache import Int3AsymNsepPchanCache
+    from nsn.pack import pack_int3_unsigned
+    g2 = torch.Generator().manual_seed(PILOT_SEED + 21)
+    cases = []
+
+    def case(name, x):
+        c = Int3AsymNsepPchanCache.from_fp16(x)
+        y = c.to_fp16()
+        put(f"asym_{name}_x", tensor_bits(x))
+        put(f"asym_{name}_packed", c.packed_d.numpy())
+        put(f"asym_{name}_norm", tensor_bits(c.norm))
+        put(f"asym_{name}_dmin", tensor_bits(c.d_min))
+        put(f"asym_{name}_dstep", tensor_bits(c.d_step))
+        put(f"asym_{name}_y", tensor_bits(y))
+        cases.append(dict(name=name, shape=list(x.shape), dtype=str(x.dtype).replace("torch.", ""),
+                          channel_stride=int(x.stride(-1)), size_bytes=int(c.size_bytes())))
+
+    x = torch.randn(1, 2, 70, 128, generator=g2) * torch.exp(torch.randn(1, 2, 70, 1, generator=g2))
+    x[..., 5] *= 8
+    case("fp16_128", x.half())
+    case("fp32_64", torch.randn(2, 1, 33, 64, generator=g2))
+    case("fp16_256", (torch.randn(1, 1, 130, 256, generator=g2) * 3).half())
+    case("bf16_128", torch.randn(1, 1, 65, 128, generator=g2).to(torch.bfloat16))
+    case("fp16_128_strided", torch.randn(1, 2, 128, 40, generator=g2).half().transpose(-1, -2))
+    x = torch.randn(1, 1, 48, 128, generator=g2)
+    x[..., ::7, :] = 0
+    x[..., 3] = 0.5
+    case("zero_tokens_const_channel", x.half())
+    x = torch.rand(1, 1, 64, 128, generator=g2) + 0.1
+    zero = torch.rand(1, 1, 64, 128, generator=g2) < 0.1
+    neg = torch.rand(1, 1, 64, 128, generator=g2) < 0.5
+    x = torch.where(zero, torch.where(neg, torch.tensor(-0.0), torch.tensor(0.0)), x)
+    case("signed_zero_min", x.half())
+    codes = torch.randint(0, 8, (3, 5, 64), generator=g2, dtype=torch.int8)
+    put("asym_pack_codes", codes.numpy())
+    put("asym_pack_bytes", pack_int3_unsigned(codes).numpy())
+    index["int3asym"] = dict(source="src/nsn/cache.py:134-313; src/nsn/pack.py:85-163", cases=cases)
+
+
 def main():
     gen_pack()
     gen_encode()
     gen_group()
     gen_attention()
     gen_cache()
+    gen_int3asym()
     np.savez_compressed(HERE / "golden.npz", **arrays)
     index["hashed"] = HASHED
     index["torch"] = torch.__version__

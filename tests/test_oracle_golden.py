@@ -130,3 +130,43 @@ def test_bridge_attention_oracle(name):
     assert ok, (name, err)
     ok, err = O.within_tolerance(out, fin, rtol=1e-5, atol=1e-5)
     assert ok, (name, err)
+
+
+# ---------------------------------------------------------------- library INT3 container
+def _asym_input(case):
+    """float32 values in the input's logical order (a transposed input was recorded through its view)."""
+    return G.bits_to_float32(G.get(f"asym_{case['name']}_x"), case["dtype"]).reshape(case["shape"])
+
+
+@pytest.mark.parametrize("case", G.index()["int3asym"]["cases"], ids=lambda c: c["name"])
+def test_oracle_int3asym_matches_reference(case):
+    name = case["name"]
+    x = _asym_input(case)
+    strided = case["channel_stride"] != 1
+    idx, n16, m16, s16 = O.int3asym_encode(x) if not strided else _asym_encode_strided(x)
+    packed = np.frombuffer(O.pack_codes(idx, 3), np.uint8).reshape(G.get(f"asym_{name}_packed").shape)
+    assert np.array_equal(packed, G.get(f"asym_{name}_packed"))
+    assert np.array_equal(n16.view(np.uint16).reshape(-1), G.get(f"asym_{name}_norm").reshape(-1))
+    assert np.array_equal(m16.view(np.uint16).reshape(-1), G.get(f"asym_{name}_dmin").reshape(-1))
+    assert np.array_equal(s16.view(np.uint16).reshape(-1), G.get(f"asym_{name}_dstep").reshape(-1))
+    y = O.int3asym_decode(idx, n16, m16, s16)
+    assert np.array_equal(y.view(np.uint16).reshape(-1), G.get(f"asym_{name}_y").reshape(-1))
+
+
+def _asym_encode_strided(x):
+    """The oracle's encode with the sequential norm order of a channel-strided input."""
+    a = np.asarray(x, np.float32)
+    n = np.maximum(O.row_norm(a, strided=True), np.float32(1e-12))[..., None]
+    d = (a / n).astype(np.float32)
+    d_min = d.min(axis=-2, keepdims=True)
+    d_max = d.max(axis=-2, keepdims=True)
+    step = (np.maximum(d_max - d_min, np.float32(1e-12)) / np.float32(7)).astype(np.float32)
+    idx = np.clip(np.rint((d - d_min) / step), 0, 7).astype(np.uint8)
+    return idx, n.astype(np.float16), d_min.astype(np.float16), step.astype(np.float16)
+
+
+def test_oracle_int3_unsigned_packing_matches_reference():
+    codes = G.get("asym_pack_codes").astype(np.uint8)
+    want = G.get("asym_pack_bytes")
+    got = np.frombuffer(O.pack_codes(codes, 3), np.uint8).reshape(want.shape)
+    assert np.array_equal(got, want)
