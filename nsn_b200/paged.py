@@ -24,11 +24,89 @@ Layout (head-major pools so one sequence's blocks of one head are contiguous):
 """
 from __future__ import annotations
 
+import struct
+
 import torch
 
 from . import _lib as L
+from . import checks
 from . import primitives as w
 from .kernel import decode_attention
+
+# ------------------------------------------------------------ sequence container format
+# A sealed sequence as bytes, for moving it between caches or processes:
+#   preamble  '<8sHHBBHII': magic, format version 1, kv heads h, bits, tail dtype
+#             (0 fp16, 1 bf16), reserved 0, sealed blocks n, tail tokens t      (24 bytes)
+#   K blocks  for head j, block i: the block's 12-byte '<QHBB' header (64*i, 64, bits, 0;
+#             loop_kv_nb06_codec.py:32), codes (64*128*bits/8 bytes), norm (64 fp16),
+#             min (128 fp16), scale (128 fp16)
+#   V blocks  the same
+#   tails     K [h, t, 128] then V [h, t, 128] in the tail dtype
+# Everything after the preamble is what planned_bytes (loop_kv_nb06_primitives.py:72-81)
+# counts for K and V.
+SEQ_MAGIC = b"NSNKVSEQ"
+_PREAMBLE = struct.Struct("<8sHHBBHII")
+_TAIL_CODE = {torch.float16: 0, torch.bfloat16: 1}
+
+
+def sequence_to_bytes(kg, kt, vg, vt) -> bytes:
+    """Serialise a sequence given in the reference's layout (groups + tails [1, h, t, 128])."""
+    h, t = kt.shape[1], kt.shape[2]
+    n = 0 if kg is None else kg["codes"].shape[2]
+    bits = 3 if kg is None else kg["codes"].shape[-1] * 8 // (w.BLOCK * w.DIM)
+    w.require(kt.dtype in _TAIL_CODE and vt.shape == kt.shape and vt.dtype == kt.dtype, "Tail layout")
+    parts = [_PREAMBLE.pack(SEQ_MAGIC, 1, h, bits, _TAIL_CODE[kt.dtype], 0, n, t)]
+    for g in (kg, vg):
+        if n == 0:
+            continue
+        w.require(g["codes"].shape[2] == n and checks.headers_ok(g), "Block headers")
+        hdr = g["headers"].cpu().numpy().reshape(h, n, 12)
+        codes = g["codes"].cpu().numpy().reshape(h, n, -1)
+        metas = [m.cpu().contiguous().view(torch.int16).numpy().reshape(h, n, -1) for m in g["metas"]]
+        for j in range(h):
+            for i in range(n):
+                parts += [hdr[j, i].tobytes(), codes[j, i].tobytes()] + [m[j, i].tobytes() for m in metas]
+    for tail in (kt, vt):
+        parts.append(tail.cpu().contiguous().view(torch.int16).numpy().tobytes())
+    return b"".join(parts)
+
+
+def sequence_from_bytes(blob: bytes, device="cpu"):
+    """Parse sequence_to_bytes output back into (kg, kt, vg, vt) on `device`; headers are verified."""
+    import numpy as np
+    w.require(len(blob) >= _PREAMBLE.size, "Sequence container")
+    magic, version, h, bits, tcode, reserved, n, t = _PREAMBLE.unpack_from(blob, 0)
+    w.require(magic == SEQ_MAGIC and version == 1 and bits in (3, 4, 5) and tcode in (0, 1) and reserved == 0,
+              "Sequence container")
+    cb = w.code_bytes(bits)
+    per_block = 12 + cb + 2 * (w.BLOCK + 2 * w.DIM)
+    want = _PREAMBLE.size + 2 * h * n * per_block + 2 * h * t * w.DIM * 2
+    w.require(len(blob) == want, "Sequence container length")
+    buf = np.frombuffer(blob, np.uint8, offset=_PREAMBLE.size)
+    dtype = torch.float16 if tcode == 0 else torch.bfloat16
+    groups, off = [], 0
+    for _ in range(2):
+        if n == 0:
+            groups.append(None)
+            continue
+        blk = buf[off:off + h * n * per_block].reshape(h, n, per_block)
+        off += h * n * per_block
+        f16 = lambda a, b_, shape: torch.from_numpy(blk[:, :, a:b_].copy().view(np.int16)).view(torch.float16) \
+            .reshape(shape).to(device)
+        g = dict(headers=torch.from_numpy(blk[:, :, :12].copy()).reshape(1, h, n, 12).to(device),
+                 codes=torch.from_numpy(blk[:, :, 12:12 + cb].copy()).reshape(1, h, n, cb).to(device),
+                 metas=(f16(12 + cb, 12 + cb + 2 * w.BLOCK, (1, h, n, w.BLOCK, 1)),
+                        f16(12 + cb + 2 * w.BLOCK, 12 + cb + 2 * w.BLOCK + 2 * w.DIM, (1, h, n, 1, w.DIM)),
+                        f16(12 + cb + 2 * w.BLOCK + 2 * w.DIM, per_block, (1, h, n, 1, w.DIM))))
+        w.require(checks.headers_ok(g), "Block headers")
+        groups.append(g)
+    tails = []
+    for _ in range(2):
+        nbytes = h * t * w.DIM * 2
+        tails.append(torch.from_numpy(buf[off:off + nbytes].copy().view(np.int16)).view(dtype)
+                     .reshape(1, h, t, w.DIM).to(device))
+        off += nbytes
+    return groups[0], tails[0], groups[1], tails[1]
 
 
 class PagedKVCache:
@@ -78,6 +156,75 @@ class PagedKVCache:
                 tail[b, :, :t].copy_(src[:, nb * w.BLOCK:])
         self.n_blocks[b] = nb
         self.tail_len[b] = t
+
+    # ------------------------------------------------------------ exchange with the reference layout
+    def export_groups(self, b: int):
+        """Sequence b as the reference's data: (k_group, k_tail, v_group, v_tail).
+
+        Groups are what encode_group(x, 0) returns for the same tokens
+        (loop_kv_nb06_codec.py:28-34): codes [1, h, n, CB], metas (norm [1, h, n, 64, 1],
+        min / scale [1, h, n, 1, 128]) and '<QHBB' headers [1, h, n, 12]; None when nothing
+        is sealed.  Tails are [1, h, t, 128] in the cache dtype.
+        """
+        nb, t = int(self.n_blocks[b]), int(self.tail_len[b])
+        pages = self.block_table[b, :nb].long()
+        h = self.h
+
+        def group(pool):
+            if nb == 0:
+                return None
+            return dict(codes=pool["codes"][:, pages].unsqueeze(0).contiguous(),
+                        metas=(pool["norm"][:, pages].reshape(1, h, nb, w.BLOCK, 1).contiguous(),
+                               pool["min"][:, pages].reshape(1, h, nb, 1, w.DIM).contiguous(),
+                               pool["scale"][:, pages].reshape(1, h, nb, 1, w.DIM).contiguous()),
+                        headers=checks.expected_headers(nb, h, self.bits, 0, self.device).contiguous())
+
+        return (group(self.k_pool), self.k_tail[b, :, :t].unsqueeze(0).contiguous(), group(self.v_pool),
+                self.v_tail[b, :, :t].unsqueeze(0).contiguous())
+
+    def import_groups(self, b: int, kg, kt, vg, vt):
+        """Load sequence b from the reference's layout; headers are verified.
+
+        A tail of 64 tokens or more (the reference's PackedCache keeps 64..127) is sealed
+        into further blocks, so the cache's seal-at-64 invariant holds afterwards.
+        """
+        h = self.h
+        n = 0 if kg is None else kg["codes"].shape[2]
+        w.require((kg is None) == (vg is None) and kt.shape == vt.shape and tuple(kt.shape[:2]) == (1, h)
+                  and kt.shape[-1] == w.DIM, "import layout")
+        for g in (kg, vg):
+            if g is not None:
+                w.require(tuple(g["codes"].shape) == (1, h, n, w.code_bytes(self.bits)) and checks.headers_ok(g),
+                          "import blocks")
+        t = kt.shape[2]
+        extra, rest = t // w.BLOCK, t % w.BLOCK
+        w.require(n + extra <= self.max_blocks, "import exceeds max_blocks")
+        pages = self.block_table[b, :n].long()
+        for g, pool in ((kg, self.k_pool), (vg, self.v_pool)):
+            if g is None:
+                continue
+            pool["codes"][:, pages] = g["codes"][0].to(self.device)
+            pool["norm"][:, pages] = g["metas"][0].reshape(h, n, w.BLOCK).to(self.device)
+            pool["min"][:, pages] = g["metas"][1].reshape(h, n, w.DIM).to(self.device)
+            pool["scale"][:, pages] = g["metas"][2].reshape(h, n, w.DIM).to(self.device)
+        for src, pool, tail in ((kt, self.k_pool, self.k_tail), (vt, self.v_pool, self.v_tail)):
+            src = src[0].to(self.device, self.dtype)
+            if extra:
+                x = src[:, :extra * w.BLOCK].reshape(h, extra, w.BLOCK, w.DIM)
+                w.encode_blocks(x, self.bits, out=pool, out_row_stride=self.pages,
+                                out_offset=b * self.max_blocks + n, check=False)
+            tail[b, :, :rest].copy_(src[:, extra * w.BLOCK:])
+        self.n_blocks[b] = n + extra
+        self.tail_len[b] = rest
+
+    def to_bytes(self, b: int) -> bytes:
+        """Sequence b in the sequence container format (see sequence_to_bytes)."""
+        return sequence_to_bytes(*self.export_groups(b))
+
+    def load_bytes(self, b: int, blob: bytes):
+        """Load sequence b from sequence container bytes."""
+        kg, kt, vg, vt = sequence_from_bytes(blob, self.device)
+        self.import_groups(b, kg, kt, vg, vt)
 
     def lengths(self):
         return (self.n_blocks.long() * w.BLOCK + self.tail_len.long()).cpu()

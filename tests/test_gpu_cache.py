@@ -196,3 +196,55 @@ def test_split_kv_merge_equals_one_pass():
     want, _ = O.bridge_attention(q.float().cpu().numpy(), fulls[0], fulls[1])
     ok, err = O.within_tolerance(out.float().cpu().numpy(), want[0], *O.TOLERANCE["float16"])
     assert ok, err
+
+
+def test_paged_export_import_and_bytes_round_trip():
+    """A live paged cache's sequence: exported to the reference layout it attends like the
+    cache (bridge arm on the exported data), and through the byte container it loads
+    into a second cache with identical pages and identical attention outputs.  Reference-
+    layout data with a tail of 64+ tokens is resealed on import."""
+    from nsn_b200 import codec, kernel, workloads
+    from nsn_b200.paged import PagedKVCache
+    rng = np.random.default_rng(31)
+    h, hq, lens = 2, 8, [150, 64, 97]
+    cache = PagedKVCache(len(lens), h, max_blocks=6, bits=3, dtype=torch.float16, hq=hq)
+    for b, L in enumerate(lens):
+        cache.prefill(b, torch.from_numpy(workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5)).cuda(),
+                      torch.from_numpy(workloads.np_kv(rng, (h, L, 128), (), 0.5)).cuda())
+    for s in range(40):
+        kn = torch.from_numpy(workloads.np_kv(rng, (len(lens), h, 1, 128), (), 0.5)[:, :, 0]).cuda()
+        vn = torch.from_numpy(workloads.np_kv(rng, (len(lens), h, 1, 128), (), 0.5)[:, :, 0]).cuda()
+        q = torch.from_numpy((rng.standard_normal((len(lens), hq, 128)) / np.sqrt(128)).astype(np.float16)).cuda()
+        cache.step(q, kn, vn)
+    cache.check()
+    q = torch.from_numpy((rng.standard_normal((len(lens), hq, 128)) / np.sqrt(128)).astype(np.float16)).cuda()
+    out = cache.attend(q).clone()
+    cache.check()
+    other = PagedKVCache(len(lens), h, max_blocks=6, bits=3, dtype=torch.float16, hq=hq)
+    for b in range(len(lens)):
+        kg, kt, vg, vt = cache.export_groups(b)
+        want = kernel.pipeline("TORCH_SDPA", (kg, kt, q[b].reshape(1, hq, 1, 128), vg, vt)).float().reshape(hq, 128)
+        ok, err = O.within_tolerance(out[b].float().cpu().numpy(), want.cpu().numpy(), *O.TOLERANCE["float16"])
+        assert ok, (b, err)
+        other.load_bytes(b, cache.to_bytes(b))
+    assert torch.equal(other.n_blocks, cache.n_blocks) and torch.equal(other.tail_len, cache.tail_len)
+    for b in range(len(lens)):
+        nb, t = int(cache.n_blocks[b]), int(cache.tail_len[b])
+        pages = cache.block_table[b, :nb].long()
+        for pa, pb in ((cache.k_pool, other.k_pool), (cache.v_pool, other.v_pool)):
+            for key in ("codes", "norm", "min", "scale"):
+                assert torch.equal(pa[key][:, pages], pb[key][:, pages]), (b, key)
+        assert torch.equal(cache.k_tail[b, :, :t], other.k_tail[b, :, :t])
+    out2 = other.attend(q)
+    other.check()
+    assert torch.equal(out2.view(torch.int16), out.view(torch.int16))
+    # reference layout with a 70-token tail (the reference policy keeps 64..127): resealed on import
+    x = torch.from_numpy(workloads.np_kv(rng, (1, h, 3 * 64 + 70, 128), (), 0.5)).cuda()
+    g = codec.encode_group(x[:, :, :192].reshape(1, h, 3, 64, 128), 0)
+    third = PagedKVCache(1, h, max_blocks=6, bits=3, dtype=torch.float16, hq=hq)
+    third.import_groups(0, g, x[:, :, 192:].contiguous(), g, x[:, :, 192:].contiguous())
+    assert int(third.n_blocks[0]) == 4 and int(third.tail_len[0]) == 6
+    g4 = codec.encode_group(x[:, :, :256].reshape(1, h, 4, 64, 128), 0)
+    kg, kt, _, _ = third.export_groups(0)
+    assert torch.equal(kg["codes"], g4["codes"]) and torch.equal(kg["headers"], g4["headers"])
+    assert torch.equal(kt, x[:, :, 256:])

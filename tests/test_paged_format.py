@@ -1,0 +1,72 @@
+"""Sequence container format of the paged cache, on CPU.
+
+A sequence in the reference's layout (packed groups with '<QHBB' headers plus native
+tails, built here with the oracle's encoder) survives sequence_to_bytes /
+sequence_from_bytes unchanged.  Its size after the preamble is what the reference's
+planned_bytes counts for K and V.  Corrupted headers and truncated input are rejected.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nsn_oracle as O
+
+
+def _reference_sequence(h=2, n=3, t=17, bits=3, seed=5):
+    from nsn_b200 import checks
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(2):
+        x = rng.standard_normal((1, h, n * 64 + t, 128)).astype(np.float16)
+        q, nn, m, s, st = O.nsn_encode(x[:, :, :n * 64].astype(np.float32).reshape(1, h, n, 64, 128), bits)
+        codes = np.frombuffer(O.pack_codes(q, bits), np.uint8).reshape(1, h, n, -1).copy()
+        g = dict(codes=torch.from_numpy(codes),
+                 metas=tuple(torch.from_numpy(a.copy()) for a in (nn, m, s)),
+                 headers=checks.expected_headers(n, h, bits, 0, "cpu").contiguous())
+        out += [g, torch.from_numpy(x[:, :, n * 64:].copy())]
+    return out[0], out[1], out[2], out[3]
+
+
+def _same(a, b):
+    return a.dtype == b.dtype and tuple(a.shape) == tuple(b.shape) and torch.equal(a.view(torch.uint8) if a.dtype == torch.uint8 else a.view(torch.int16), b.view(torch.uint8) if b.dtype == torch.uint8 else b.view(torch.int16))
+
+
+@pytest.mark.parametrize("bits", [3, 5])
+def test_sequence_container_round_trip_and_size(bits):
+    from nsn_b200 import primitives as w
+    from nsn_b200.paged import sequence_from_bytes, sequence_to_bytes
+    h, n, t = 2, 3, 17
+    kg, kt, vg, vt = _reference_sequence(h, n, t, bits)
+    blob = sequence_to_bytes(kg, kt, vg, vt)
+    planned = w.planned_bytes((1, h, n * 64 + t, 128), n * 64, bits)
+    assert len(blob) == 24 + 2 * sum(planned.values())
+    kg2, kt2, vg2, vt2 = sequence_from_bytes(blob)
+    for a, b in ((kg, kg2), (vg, vg2)):
+        assert _same(a["codes"], b["codes"]) and _same(a["headers"], b["headers"])
+        for x, y in zip(a["metas"], b["metas"]):
+            assert _same(x, y)
+    assert _same(kt, kt2) and _same(vt, vt2)
+
+
+def test_sequence_container_without_sealed_blocks():
+    from nsn_b200.paged import sequence_from_bytes, sequence_to_bytes
+    kt = torch.randn(1, 2, 9, 128).half()
+    vt = torch.randn(1, 2, 9, 128).half()
+    kg, kt2, vg, vt2 = sequence_from_bytes(sequence_to_bytes(None, kt, None, vt))
+    assert kg is None and vg is None and torch.equal(kt2, kt) and torch.equal(vt2, vt)
+
+
+def test_sequence_container_rejects_corruption():
+    from nsn_b200 import primitives as w
+    from nsn_b200.paged import sequence_from_bytes, sequence_to_bytes
+    blob = bytearray(sequence_to_bytes(*_reference_sequence()))
+    with pytest.raises(w.ContractError):
+        sequence_from_bytes(bytes(blob[:-1]))
+    bad = bytearray(blob)
+    bad[24 + 8] = 63  # first block header's token count
+    with pytest.raises(w.ContractError):
+        sequence_from_bytes(bytes(bad))
+    bad = bytearray(blob)
+    bad[:8] = b"NOTNSNKV"
+    with pytest.raises(w.ContractError):
+        sequence_from_bytes(bytes(bad))
