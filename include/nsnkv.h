@@ -229,6 +229,20 @@ int nsnkv_int3asym_encode(const void *x, int x_dtype, int64_t rows, int64_t toke
 int nsnkv_int3asym_decode(const uint8_t *packed, const uint16_t *norm, const uint16_t *d_min, const uint16_t *d_step,
                           int64_t rows, int64_t tokens, int dim, uint16_t *out, void *stream);
 
+/*
+ * Batched GQA decode scores over a per-channel quantised K cache, the K1c layout
+ * (experiments/kernels/phase_k1c_triton_fused_kernel.py:172-250, triton_decode_scores):
+ *   recipe 0 FP16: code is K itself, fp16 [batch][tokens][n_kv*head_dim];
+ *   recipe 1 KIVI / 2 NSN: code uint8 [batch][tokens][n_kv*head_dim], k_min / k_step fp16
+ *   [batch][n_kv*head_dim]; NSN also eff_norm fp16 [batch][n_kv][tokens].
+ * q fp16 [batch][n_q][head_dim]; scores fp32 [batch][n_q][tokens] =
+ *   (1/sqrt(head_dim)) * eff_norm * sum_d q * (code * step + min).
+ * Contiguous layouts; head_dim % 16 == 0, <= 256; n_q / n_kv <= 8; code 16-byte aligned.
+ */
+int nsnkv_k1c_scores(int recipe, int64_t batch, int n_q, int n_kv, int64_t tokens, int head_dim, const void *q,
+                     const void *code, const uint16_t *k_min, const uint16_t *k_step, const uint16_t *eff_norm,
+                     float *scores, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,7 @@ SIGNATURES = [
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),
     ("nsnkv_int3asym_encode", c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, P, P, P, P, c_int64, P, P]),
     ("nsnkv_int3asym_decode", c_int, [P, P, P, P, c_int64, c_int64, c_int, P, P]),
+    ("nsnkv_k1c_scores", c_int, [c_int, c_int64, c_int, c_int, c_int64, c_int, P, P, P, P, P, P, P]),
 ]
 
 _lib = None

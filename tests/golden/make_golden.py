@@ -399,6 +399,30 @@ def gen_int3asym():
     index["int3asym"] = dict(source="src/nsn/cache.py:134-313; src/nsn/pack.py:85-163", cases=cases)
 
 
+# ------------------------------------------------------------------ K1c batched decode scores
+def gen_k1c():
+    sys.path.insert(0, str(REF / "experiments/kernels"))
+    import phase_k1c_triton_fused_kernel as k1c
+    models = {"gemma": k1c.GRID_MODELS[0], "qwen": k1c.GRID_MODELS[1]}
+    cells = []
+    for mname, model in models.items():
+        for recipe, bits in (("nsn", 5), ("kivi", 5), ("nsn", 4), ("kivi", 4), ("fp16", 16)):
+            B, T = 2, 97
+            q, ref_store, tstore, n_q, n_kv, hd = k1c.make_triton_store(model, B, T, bits, recipe, "cpu")
+            ref32 = k1c._torch_decode_scores(q.float(), {k: (v.float() if torch.is_tensor(v) else v)
+                                                        for k, v in ref_store.items()}, recipe, n_q, n_kv, hd)
+            key = f"k1c_{mname}_{recipe}{bits}"
+            arrays_sha = {}
+            for f in ("code", "min", "step", "eff_norm"):
+                if f in tstore:
+                    arrays_sha[f] = sha(tensor_bits(tstore[f]).tobytes())
+            put(key + "_scores", ref32.numpy(), force=True)
+            cells.append(dict(key=key, model=mname, recipe=recipe, bits=bits, B=B, T=T, q_sha256=sha(tensor_bits(q).tobytes()),
+                              store_sha256=arrays_sha))
+    index["k1c"] = dict(source="experiments/kernels/phase_k1c_triton_fused_kernel.py:63-250", gate_tol=k1c.GATE_TOL,
+                        cells=cells)
+
+
 def main():
     gen_pack()
     gen_encode()
@@ -406,6 +430,7 @@ def main():
     gen_attention()
     gen_cache()
     gen_int3asym()
+    gen_k1c()
     np.savez_compressed(HERE / "golden.npz", **arrays)
     index["hashed"] = HASHED
     index["torch"] = torch.__version__

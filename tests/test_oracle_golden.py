@@ -170,3 +170,20 @@ def test_oracle_int3_unsigned_packing_matches_reference():
     want = G.get("asym_pack_bytes")
     got = np.frombuffer(O.pack_codes(codes, 3), np.uint8).reshape(want.shape)
     assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------- K1c batched decode scores
+@pytest.mark.parametrize("cell", G.index()["k1c"]["cells"], ids=lambda c: c["key"])
+def test_oracle_k1c_store_and_scores_match_reference(cell):
+    import hashlib
+    import torch
+    from oracle import k1c
+    model = k1c.MODELS[cell["model"]]
+    q, tstore, ref32 = k1c.make_store(model, cell["B"], cell["T"], cell["bits"], cell["recipe"])
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().tobytes() if t.dtype != torch.uint8 else t.numpy().tobytes()
+    assert hashlib.sha256(bits(q)).hexdigest() == cell["q_sha256"]
+    for f, h in cell["store_sha256"].items():
+        assert hashlib.sha256(bits(tstore[f])).hexdigest() == h, f
+    got = k1c.gate_scores(q, ref32, cell["recipe"], model).numpy()
+    want = G.get(cell["key"] + "_scores")
+    assert np.abs(got - want).max() <= 1e-6 * np.abs(want).max()
