@@ -336,6 +336,78 @@ def run_cfg4(args, rank, world, local, dist):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ cfg3: looped model, teacher-forced decode
+def run_cfg3(args, rank, world, local, dist):
+    """cfg3: a 24-layer looped decoder (hidden 2048, 16 MHA heads x 128, SwiGLU 5632, RoPE
+    theta 1e4, vocab 32000, 4 loops sharing weights: 96 (loop, layer) INT3 KV slots),
+    random-init fp16 weights.  4 sequences of 2048 random prompt ids, then 256
+    teacher-forced decode steps each; sequences are sharded over ranks (at most 4).
+    Timed: the decode steps (prefill outside the events), per arm."""
+    from transformers import LlamaConfig
+    from nsn_b200 import adapter
+    device = torch.device("cuda", local)
+    cfg = LlamaConfig(vocab_size=32000, hidden_size=2048, intermediate_size=5632, num_hidden_layers=24,
+                      num_attention_heads=16, num_key_value_heads=16, head_dim=128, max_position_embeddings=4096,
+                      rope_theta=10000.0, attn_implementation="sdpa")
+    torch.manual_seed(3)
+    model = adapter.LoopedDecoder(cfg, loops=4).to(device).half().eval()
+    restore = adapter.install(model)
+    n_seq, prompt_len, steps = 4, 2048, args.cfg3_steps
+    mine = [i for i in range(n_seq) if i % world == rank]
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (n_seq, prompt_len + steps), generator=gen)
+    Cache = adapter.make_cache()
+    results = {}
+    for arm, checks in (("GQA_FUSED", "step"), ("GQA_FUSED", "call"), ("TORCH_SDPA", "call")):
+        total_ms, kv_packed, kv_fp16 = 0.0, 0, 0
+        for i in mine:
+            cache = Cache(arm, 4, checks)
+            x = ids[i:i + 1].to(device)
+            model(x[:, :prompt_len], cache, 0)
+            cache.post_prefill()
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for t in range(steps):
+                model(x[:, prompt_len + t:prompt_len + t + 1], cache, prompt_len + t)
+                cache.post_decode()
+            e1.record()
+            torch.cuda.synchronize(device)
+            total_ms += e0.elapsed_time(e1)
+            nbytes = lambda t: t.numel() * t.element_size()
+            kv_packed = sum(nbytes(x) for x in cache.key_cache + cache.value_cache if x is not None)
+            kv_packed += sum(nbytes(g["codes"]) + nbytes(g["headers"]) + sum(nbytes(m) for m in g["metas"])
+                             for g in cache.packed.values())
+            kv_fp16 = 96 * 2 * 16 * (prompt_len + steps) * 128 * 2
+            del cache
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        results[(arm, checks)] = dict(ms=t.item(), kv_bytes_per_seq=kv_packed, kv_fp16_bytes_per_seq=kv_fp16)
+    restore()
+    if rank == 0:
+        tok = n_seq * steps
+        fused = results[("GQA_FUSED", "step")]
+        line = {"metric": "decode tokens/s (looped model, cfg3)", "value": tok / (fused["ms"] / 1000.0),
+                "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": 0,
+                "ms_per_step": fused["ms"] / (steps * max(1, -(-n_seq // world))), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random-init weights, "
+                "random token ids)",
+                "config": {"workload": "cfg3-looped-24x4: hidden 2048, 16 MHA heads x 128, SwiGLU 5632, vocab 32000, "
+                                       "4 loops (96 INT3 KV slots), 4 seqs x 2048 prompt + teacher-forced decode",
+                           "global_batch": n_seq, "parallelism": f"seq-shard{world}",
+                           "kv_bytes_per_seq_packed": fused["kv_bytes_per_seq"],
+                           "kv_bytes_per_seq_fp16": fused["kv_fp16_bytes_per_seq"]},
+                "checks": "device status read once per decode step (post_decode)",
+                "fused_per_call_checks": {"value": tok / (results[("GQA_FUSED", "call")]["ms"] / 1000.0),
+                                          "unit": "tokens/s",
+                                          "note": "the reference pipeline's checks (host sync) on every call"},
+                "bridge_arm": {"arm": "TORCH_SDPA (reference bridge: restore_group + repeat_kv + SDPA, "
+                                      "per-call checks)",
+                               "value": tok / (results[("TORCH_SDPA", "call")]["ms"] / 1000.0), "unit": "tokens/s"}}
+        print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ main GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -345,8 +417,9 @@ def main():
     ap.add_argument("--impl", default="nsn", choices=["nsn", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
-                    help="2: batched decode (the default bench line); 4: split-KV long context + encode")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: batched decode (the default bench line); 3: looped model; 4: split-KV long context + encode")
+    ap.add_argument("--cfg3-steps", type=int, default=256, help="teacher-forced decode steps per sequence (cfg3)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -367,9 +440,9 @@ def main():
             dist.destroy_process_group()
         return
 
-    if args.config == 4:
+    if args.config in (3, 4):
         torch.cuda.set_device(local)
-        run_cfg4(args, rank, world, local, dist)
+        (run_cfg3 if args.config == 3 else run_cfg4)(args, rank, world, local, dist)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

@@ -65,10 +65,15 @@ def make_cache(base=ListCacheBase):
     parent = make_packed_cache(base)
 
     class ConnectionCache(parent):
-        def __init__(self, arm, loops=1):
+        def __init__(self, arm, loops=1, checks="call"):
             w.require(arm in ARMS, "Unknown model arm")
+            w.require(checks in ("call", "step"), "Check granularity")
             super().__init__(loops, None if arm in ("OFFICIAL", "NATIVE") else 3)
             self.arm = arm
+            # "call": every attention call runs the reference pipeline's checks (host syncs);
+            # "step": fused calls OR their device status into one word that post_decode reads
+            self.checks = checks
+            self.status = None
             self._defer = False
             self.connections = Counter()
             self.skipped_k = Counter()
@@ -80,6 +85,14 @@ def make_cache(base=ListCacheBase):
                 (self.skipped_k if kv == "K" else self.skipped_v)[slot] += 1
                 return None
             return super().materialize(slot, kv)
+
+        def post_decode(self):
+            if self.checks == "step" and self.status is not None:
+                st = int(self.status.item())
+                if st:
+                    self.status.zero_()
+                    K._raise_status(st)
+            super().post_decode()
 
         def append_for_attention(self, key, value, slot, kwargs):
             w.require(not self._defer and self.restore_observer is None, "Recursive/decorated restore")
@@ -119,7 +132,14 @@ def decode(attn, module, hidden_states, position_embeddings, cache, loop_idx=0, 
     cache.append_for_attention(k, v, slot, {"sin": sin, "cos": cos, "cache_position": cache_position})
     data = (cache.packed.get((slot, "K")), cache.key_cache[slot], q.contiguous(), cache.packed.get((slot, "V")),
             cache.value_cache[slot])
-    out = K.pipeline("GQA_FUSED" if cache.arm == "GQA_FUSED" else "TORCH_SDPA", data)
+    if cache.checks == "step" and cache.arm == "GQA_FUSED":
+        from . import checks
+        checks.structural(*data)
+        if cache.status is None:
+            cache.status = torch.zeros(1, dtype=torch.int32, device=q.device)
+        out = K.launch(*data, check=False, status=cache.status)[0]
+    else:
+        out = K.pipeline("GQA_FUSED" if cache.arm == "GQA_FUSED" else "TORCH_SDPA", data)
     cache.connections[slot] += 1
     if cache.capture is not None:
         cache.capture(slot, data, out)

@@ -111,11 +111,13 @@ def restore_v(g, tail):
     return y.reshape(1, h, n * 64 + tail.shape[2], 128)
 
 
-def launch(g, kt, q, vg, vt, trace=False, check=True):
+def launch(g, kt, q, vg, vt, trace=False, check=True, status=None):
     """Fused attention over packed K/V groups plus native tails.
 
     Returns (out [1,1,hq,128] in q.dtype, context fp32 [1,hq,1,128], score, v);
     score/v are the diagnostic fp32 scores [1,hq,T] and restored V when trace.
+    With ``check=False`` the device status is left in ``status`` (ORed into it when
+    given) for the caller to read later.
     """
     h = kt.shape[1]
     hq = q.shape[1]
@@ -127,7 +129,8 @@ def launch(g, kt, q, vg, vt, trace=False, check=True):
         q.reshape(1, hq, 128), group_pool(g, h) if g is not None else None,
         group_pool(vg, h) if vg is not None else None, h=h, bits=bits, blk_stride_head=n, blk_stride_page=1,
         n_blocks=n, max_blocks=n, k_tail=kt if t else None, v_tail=vt if t else None,
-        tail_stride_seq=h * t, tail_stride_head=t, tail_len=t, max_tail=t, out_f32=ctx.reshape(1, hq, 128))
+        tail_stride_seq=h * t, tail_stride_head=t, tail_len=t, max_tail=t, out_f32=ctx.reshape(1, hq, 128),
+        status=status)
     if check:
         _raise_status(int(status.item()))
     out = out.reshape(1, 1, hq, 128)

@@ -67,6 +67,8 @@ def test_looped_decoder_fused_matches_bridge():
         logits_fused = model.generate_teacher_forced(prompt, forced, fused)
         bridge = Cache("TORCH_SDPA", loops)
         logits_bridge = model.generate_teacher_forced(prompt, forced, bridge)
+        stepwise = Cache("GQA_FUSED", loops, checks="step")
+        logits_step = model.generate_teacher_forced(prompt, forced, stepwise)
     finally:
         restore()
     slots = cfg.num_hidden_layers * loops
@@ -85,7 +87,9 @@ def test_looped_decoder_fused_matches_bridge():
         want = K.pipeline("TORCH_SDPA", data)
         ok, err = O.within_tolerance(out.float().cpu().numpy(), want.float().cpu().numpy(), *O.TOLERANCE["float16"])
         assert ok, (slot, err)
-    # the two runs differ only in the attention arithmetic
+    # reading the device status once per step changes nothing but the host syncs
+    assert torch.equal(logits_step, logits_fused)
+    # the fused and bridge runs differ only in the attention arithmetic
     assert torch.isfinite(logits_fused).all()
     scale = logits_bridge.float().abs().max().item()
     assert (logits_fused.float() - logits_bridge.float()).abs().max().item() <= 2e-2 * scale
