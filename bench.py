@@ -465,7 +465,8 @@ def main():
     def attn_bytes():
         nb = cache.n_blocks.long()
         tl = cache.tail_len.long() + 1  # + the appended token
-        per_block = 3072 + 64 * 2 + 128 * 4
+        # codes + min/scale + per-token factors (fp32 renorm factors on the sealed INT3 kernel, fp16 norms otherwise)
+        per_block = 3072 + 64 * (4 if cache.uses_alpha_path() else 2) + 128 * 4
         return int((2 * 8 * (nb * per_block + tl * 256)).sum() + 2 * n_seq * 32 * 256 + n_seq * 8 * 2 * 256)
 
     for i in range(args.warmup):
@@ -557,14 +558,19 @@ def main():
                        "l2": "flushed (256 MiB write) before every timed step, outside the events",
                        "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
-            "roofline": {"bound": "hbm", "kernel": "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("nsnkv_decode_attn_alpha (attn_sealed3_kernel + attn_partial_kernel on the tails "
+                                    "+ attn_merge_kernel)") if cache.uses_alpha_path() else
+                                   "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn),
                          "traffic_note": "ncu dram read+write of attn_partial at one full-size bench launch "
                                          "(profiles/attn_partial_cfg2.md), scaled to this launch's algorithmic bytes",
                          "bytes_per_launch": bytes_attn},
             "e2e": e2e,
-            "gpu_launches": 4 * args.steps,
+            # attend: sealed kernel + tail kernel + merge (2 without the renorm path); seal: encode +
+            # renorm + counters (2 without it)
+            "gpu_launches": (6 if cache.uses_alpha_path() else 4) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

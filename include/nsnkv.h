@@ -138,6 +138,42 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
                       void *out, float *out_f32, float *lse,
                       void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
 
+/*
+ * nsnkv_decode_attn over blocks that also carry per-token renorm factors:
+ *   k_alpha / v_alpha  fp32 [64] per block, indexed like k_norm / v_norm, holding
+ *                      alpha_t = n_t / max(||d_t||, 1e-12) (0 when n_t == 0) with
+ *                      d = min + scale * code: the factor nsn_decode applies to a row
+ *                      (loop_kv_nb06_primitives.py:57-66); nsnkv_block_renorm and
+ *                      nsnkv_seal_full_tails_alpha write it.
+ * INT3 fp16 caches with hq / h <= 4 then run the sealed blocks on the tensor cores
+ * without restoring any K or V value (the codes are the MMA operands); the norms are
+ * not read.  Other shapes take the nsnkv_decode_attn path.  The result matches
+ * nsnkv_decode_attn within fp32 accumulation error, not bit for bit: this path
+ * skips the bridge's rounding of the restored rows to fp16.  Same workspace.
+ */
+int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
+                            const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
+                            const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
+                            const uint16_t *v_min, const uint16_t *v_scale,
+                            const float *k_alpha, const float *v_alpha,
+                            int64_t blk_stride_head, int64_t blk_stride_page,
+                            const int32_t *block_table, int64_t table_stride,
+                            const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                            void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                            const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail,
+                            const void *k_new, const void *v_new,
+                            void *out, float *out_f32, float *lse,
+                            void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+
+/*
+ * Per-token renorm factors of sealed blocks (see nsnkv_decode_attn_alpha), for the
+ * blocks nsnkv_encode_blocks lays out: block (row r, i) of rows x blocks_per_row has
+ * index r*row_stride + offset + i in codes / norm / min / scale / alpha.
+ */
+int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
+                       const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
+                       void *stream);
+
 /* Workspace bytes nsnkv_decode_attn needs for these sizes. */
 int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t max_blocks, int32_t max_tail);
 
@@ -193,6 +229,16 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
                           uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
                           int64_t blk_stride_head, int64_t blk_stride_page,
                           int32_t *status, void *stream);
+
+/* nsnkv_seal_full_tails that also writes the sealed blocks' renorm factors (k_alpha / v_alpha, fp32 [64] per block). */
+int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
+                                void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                                int32_t *tail_len, int32_t *n_blocks, int pending_append,
+                                const int32_t *block_table, int64_t table_stride,
+                                uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
+                                uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
+                                float *k_alpha, float *v_alpha, int64_t blk_stride_head, int64_t blk_stride_page,
+                                int32_t *status, void *stream);
 
 /*
  * Combine per-shard attention partials (one row per shard) into the final

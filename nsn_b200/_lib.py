@@ -50,6 +50,14 @@ SIGNATURES = [
                                   P, c_int32, c_int32,
                                   P, P, P, P, P, P, c_int64, P, P]),
     ("nsnkv_decode_attn_workspace_bytes", c_int64, [c_int64, c_int, c_int, c_int32, c_int32]),
+    ("nsnkv_decode_attn_alpha", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
+                                        P, P, P, P, P, P, P, P, P, P,
+                                        c_int64, c_int64, P, c_int64,
+                                        P, c_int32, c_int32,
+                                        P, P, c_int64, c_int64,
+                                        P, c_int32, c_int32,
+                                        P, P, P, P, P, P, c_int64, P, P]),
+    ("nsnkv_block_renorm", c_int, [c_int, c_int64, c_int64, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_decode_attn_noalloc", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
                                           P, P, P, P, P, P, P, P,
                                           c_int64, c_int64, P, c_int64,
@@ -59,6 +67,8 @@ SIGNATURES = [
                                           P, P, P, P, P, P, P]),
     ("nsnkv_seal_full_tails", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P, c_int64,
                                       P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
+    ("nsnkv_seal_full_tails_alpha", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P,
+                                            c_int64, P, P, P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),

@@ -35,6 +35,7 @@ struct AttnArgs {
   const uint16_t *kn, *km, *ks;
   const uint8_t *vc;
   const uint16_t *vn, *vm, *vs;
+  const float *ka, *va;  // per-token renorm factors (sealed INT3 path), or null
   int64_t sh, sp;
   const int32_t *table;
   int64_t table_stride;
@@ -47,6 +48,7 @@ struct AttnArgs {
   const void *knew, *vnew;
   int32_t chunk_blocks;
   int32_t max_chunks;
+  int32_t raw_only;  // 1: CTA x takes the x-th native-row chunk (sealed chunks run in attn_sealed3_kernel)
   float *part_o;   // [batch][hq][max_chunks][128]
   float *part_ml;  // [batch][hq][max_chunks][2]
   int32_t *status;
@@ -368,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3, cbase = 32 * tig, mi = meta_index(cbase);
   const int t0 = 16 * warp + g, t1 = t0 + 8;
-  const int chunk = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int G = a.hq / a.h;
 
@@ -378,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
   const int n_sealed_chunks = (nb + a.chunk_blocks - 1) / a.chunk_blocks;
   const int raw_per_chunk = a.chunk_blocks * kBlock;
   const int n_chunks = n_sealed_chunks + (tail_total + raw_per_chunk - 1) / raw_per_chunk;
+  const int chunk = a.raw_only ? n_sealed_chunks + static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
   if (chunk >= n_chunks) return;
   const bool is_raw = chunk >= n_sealed_chunks;
 
@@ -640,6 +643,419 @@ __global__ void __launch_bounds__(128) merge_shards_kernel(int n_shards, int64_t
   if (!isfinite(Elem<T>::to_f(yt))) set_status(status, NSNKV_ST_OUTPUT_NONFINITE);
 }
 
+// ----------------------------------------------------------------- sealed INT3 blocks on the tensor cores
+// attn_sealed3_kernel: the sealed chunks of INT3 fp16 caches with G <= 4 query heads per
+// kv head, when per-token renorm factors alpha_t = n_t / max(||d_t||, eps) are stored
+// beside the blocks (computed once at seal time by nsnkv_block_renorm).  With
+// d = min + scale * code, a token's restored row is alpha_t * d, so
+//   q . k_t = alpha_t * (sum_c q_c scale_c code_tc + sum_c q_c min_c)
+//   sum_t p_t v_t = sum_t p_t alpha_t (min_c + scale_c code_tc)
+// and both contractions take the 3-bit codes themselves as mma.sync operands.  One
+// AND drops a code into the mantissa of an fp16 subnormal (value code * 2^(pos-24)),
+// two codes per register; the per-channel scale goes into the other operand
+// (K side: q * scale split exactly into fp16 hi + lo columns) or into an fp32
+// epilogue per block (V side).  Each warp owns whole blocks: block li of the chunk
+// goes to warp li % 4, which streams it through its own two-stage TMA ring and runs
+//   K  4 m-tiles (16 tokens) x 9 k-steps of mma.m16n8k16: A = code pairs of a token,
+//      B = [q_h * scale hi | lo] for the warp lane's head h = tig,
+//   softmax over the block's 64 tokens for that head (running max / sum per warp),
+//   V  8 m-tiles (16 channel slots) x 4 k-steps: A = code pairs of one channel in two
+//      tokens, B = p * alpha split into hi | lo (movmatrix turns the score layout into
+//      the B fragments), then acc += scale_c * D + min_c * sum_t p_t alpha_t.
+// No restored K or V value is formed anywhere.
+namespace s3 {
+
+constexpr int kRing = 2;  // TMA stages per warp
+constexpr int kRec = 60;  // words of a lane's constant record: stride 4 * odd -> conflict-free 128-bit loads
+constexpr int kCB = 3072;  // INT3 code bytes per block
+
+struct SStage {
+  uint8_t kc[kCB];
+  uint8_t vc[kCB];
+  uint16_t km[kDim], ks[kDim], vm[kDim], vs[kDim];
+  float ka[kBlock], va[kBlock];
+};
+static_assert(sizeof(SStage) == 7680, "stage layout");
+
+struct SSmem {
+  union {
+    SStage stage[kWarps][kRing];
+    MergeSmem merge;  // after the last block of every warp
+  } u;
+  uint32_t rec[32][kRec];  // per lane: [0,18) qa, [20,38) qz, [40,56) Delta A fragments
+  uint64_t full[kWarps][kRing];
+  float qmax[kWarps];
+};
+
+// K side.  A lane group (tig) covers channels 32*tig + j, j = 0..31 of a token row: 96
+// bits in three words w0..w2, code j at bits 3j..3j+2.  Source words X0..X5 are the
+// group's bits starting at 0, 8, 32, 40, 64, 72; register r takes one code from the low
+// 16 bits of X_src (start in [0, 8)) and one from the high 16 bits (start in [16, 24)),
+// each staying below bit 10 of its half.  Columns: src, j_lo, pos_lo, j_hi, pos_hi
+// (-1: the half stays zero).  18 registers = 9 k-steps of 16 channel slots.
+__host__ __device__ constexpr int ktab(int r, int f) {
+  constexpr int t[18][5] = {{0, 0, 0, 6, 2},    {0, 1, 3, 7, 5},    {0, 2, 6, -1, 0},  {1, 3, 1, 8, 0},
+                            {1, 4, 4, 9, 3},    {1, 5, 7, 10, 6},   {2, 11, 1, 16, 0}, {2, 12, 4, 17, 3},
+                            {2, 13, 7, 18, 6},  {3, 14, 2, 19, 1},  {3, 15, 5, 20, 4}, {3, -1, 0, 21, 7},
+                            {4, 22, 2, 27, 1},  {4, 23, 5, 28, 4},  {4, -1, 0, 29, 7}, {5, 24, 0, 30, 2},
+                            {5, 25, 3, 31, 5},  {5, 26, 6, -1, 0}};
+  return t[r][f];
+}
+__host__ __device__ constexpr uint32_t kmask(int r) {
+  return (ktab(r, 1) >= 0 ? 7u << ktab(r, 2) : 0u) | (ktab(r, 3) >= 0 ? 7u << (16 + ktab(r, 4)) : 0u);
+}
+// PRMT selector gathering the scales of register r's two channels from natural pairs.
+__host__ __device__ constexpr uint32_t ksel(int r) {
+  return (ktab(r, 1) >= 0 && (ktab(r, 1) & 1) ? 0x32u : 0x10u) |
+         ((ktab(r, 3) >= 0 && (ktab(r, 3) & 1) ? 0x76u : 0x54u) << 8);
+}
+
+// V side.  Lane g covers channels 16g + i, i = 0..15: the 48-bit field F at bit 48g of
+// a token row, code i at F bits 3i.  L = F bytes 0..3, H = F bytes 2..5; window k
+// (0..5) is the 16-bit slice of F starting at byte k, taken from L (k < 3) or H, and
+// a register holds channel i of two tokens: the window of each token in one half,
+// then an AND at the code's position inside the window.
+__host__ __device__ constexpr int vwin(int i) { return (3 * i) >> 3; }
+__host__ __device__ constexpr int vpos(int i) { return 3 * i - 8 * vwin(i); }
+__host__ __device__ constexpr uint32_t vsel(int k) {
+  return k == 0 ? 0x5410u : (k == 1 || k == 3) ? 0x6521u : (k == 2 || k == 4) ? 0x7632u : 0x7733u;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// An fp32 weight as fp16 hi (low half) and fp16 lo = RN(w - hi) (high half).
+__device__ __forceinline__ uint32_t split_hilo(float w) {
+  const float hf = __half2float(__float2half_rn(w));
+  __half2 p = __floats2half2_rn(w, w - hf);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
+
+}  // namespace s3
+
+__global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArgs a) {
+  using namespace s3;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  SSmem &S = *reinterpret_cast<SSmem *>(smem_raw);
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  const int chunk = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = a.hq / a.h;
+  const int nb = a.nblk ? a.nblk[b] : a.nblk_const;
+  const int blk0 = chunk * a.chunk_blocks;
+  if (blk0 >= nb) return;
+  const int nloc = min(nb - blk0, a.chunk_blocks);
+  const __half *qb = static_cast<const __half *>(a.q) + (b * a.hq + static_cast<int64_t>(h) * G) * kDim;
+
+  // ---- q exponent: every |q| * 2^(7 - kq) stays below 2^15, so q * 2^(7 - pos - kq) is a finite fp16
+  float qm = 0.f;
+  for (int e = tid; e < G * kDim; e += kThreads) qm = fmaxf(qm, fabsf(__half2float(qb[e])));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, o));
+  if (lane == 0) S.qmax[warp] = qm;
+  if (lane == 0) {
+    mbar_init(&S.full[warp][0], 1);
+    mbar_init(&S.full[warp][1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  qm = fmaxf(fmaxf(S.qmax[0], S.qmax[1]), fmaxf(S.qmax[2], S.qmax[3]));
+  int qe = 0;
+  frexpf(qm, &qe);
+  const int kq = qe > 8 ? qe - 8 : 0;
+
+  // ---- per-lane constants (the same in every warp): warp 0 writes them
+  if (warp == 0) {
+    uint32_t *rec = S.rec[lane];
+    const int hb = g >> 1, pb = g & 1;
+#pragma unroll
+    for (int r = 0; r < 18; ++r) {
+      float lo = 0.f, hi = 0.f;
+      if (hb < G) {
+        if (ktab(r, 1) >= 0) lo = ldexpf(__half2float(qb[hb * kDim + 32 * tig + ktab(r, 1)]), 7 - ktab(r, 2) - kq);
+        if (ktab(r, 3) >= 0) hi = ldexpf(__half2float(qb[hb * kDim + 32 * tig + ktab(r, 3)]), 7 - ktab(r, 4) - kq);
+      }
+      __half2 s2 = __floats2half2_rn(lo, hi);
+      const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
+      rec[r] = pb ? su ^ 0x80008000u : su;  // hi lanes: q; lo lanes: -q
+      rec[20 + r] = pb ? su : 0u;           // lo lanes: q; hi lanes: 0
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a0 = 0u, a2 = 0u;
+      if (g < G) {
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qb + g * kDim + 32 * tig + 4 * ks);
+        a0 = qw[0];
+        a2 = qw[1];
+      }
+      rec[40 + 2 * ks] = a0;
+      rec[41 + 2 * ks] = a2;
+    }
+  }
+  __syncthreads();
+
+  const int njw = nloc > warp ? (nloc - 1 - warp) / kWarps + 1 : 0;  // this warp's blocks
+  auto issue = [&](int j) {
+    const int i = blk0 + warp + kWarps * j;
+    const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
+    const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
+    SStage &sg = S.u.stage[warp][j & 1];
+    uint64_t *bar = &S.full[warp][j & 1];
+    mbar_expect_tx(bar, sizeof(SStage));
+    bulk_g2s(sg.kc, a.kc + bi * kCB, kCB, bar);
+    bulk_g2s(sg.vc, a.vc + bi * kCB, kCB, bar);
+    bulk_g2s(sg.km, a.km + bi * kDim, kDim * 2, bar);
+    bulk_g2s(sg.ks, a.ks + bi * kDim, kDim * 2, bar);
+    bulk_g2s(sg.vm, a.vm + bi * kDim, kDim * 2, bar);
+    bulk_g2s(sg.vs, a.vs + bi * kDim, kDim * 2, bar);
+    bulk_g2s(sg.ka, a.ka + bi * kBlock, kBlock * 4, bar);
+    bulk_g2s(sg.va, a.va + bi * kBlock, kBlock * 4, bar);
+  };
+  if (lane == 0)
+    for (int j = 0; j < kRing && j < njw; ++j) issue(j);
+  __syncwarp();
+
+  const float c1 = ldexpf(kScale, 17 + kq), c2 = kScale;
+  const int vword = (3 * g - (g & 1)) >> 1;  // first word holding this lane's V field
+  const uint32_t selL = (g & 1) ? 0x5432u : 0x3210u, selH = (g & 1) ? 0x7654u : 0x5432u;
+  const uint32_t *rec = S.rec[lane];
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  int st = 0;
+  int jfail = -1;
+
+  for (int j = 0; j < njw; ++j) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&S.full[warp][j & 1], (j >> 1) & 1, a.status))) {
+      jfail = j;
+      break;
+    }
+    const SStage &sg = S.u.stage[warp][j & 1];
+
+    // ---- K weights of this block: W[r] = hi (even g) or lo (odd g) of q * scale * 2^(7-pos-kq)
+    uint32_t W[18];
+    {
+      uint32_t nat[16];
+      const uint4 *ksv = reinterpret_cast<const uint4 *>(sg.ks + 32 * tig);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = ksv[i];
+        nat[4 * i] = v.x;
+        nat[4 * i + 1] = v.y;
+        nat[4 * i + 2] = v.z;
+        nat[4 * i + 3] = v.w;
+      }
+      uint32_t qa[20], qz[20];
+      const uint4 *rq = reinterpret_cast<const uint4 *>(rec);
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const uint4 x = rq[i], y = rq[5 + i];
+        qa[4 * i] = x.x, qa[4 * i + 1] = x.y, qa[4 * i + 2] = x.z, qa[4 * i + 3] = x.w;
+        qz[4 * i] = y.x, qz[4 * i + 1] = y.y, qz[4 * i + 2] = y.z, qz[4 * i + 3] = y.w;
+      }
+#pragma unroll
+      for (int r = 0; r < 18; ++r) {
+        const uint32_t lo_src = ktab(r, 1) >= 0 ? nat[ktab(r, 1) >> 1] : 0u;
+        const uint32_t hi_src = ktab(r, 3) >= 0 ? nat[ktab(r, 3) >> 1] : 0u;
+        const uint32_t b2 = prmt(lo_src, hi_src, ksel(r));
+        W[r] = hfma2u(qz[r], b2, hmul2u(qa[r], b2));
+      }
+    }
+    // ---- Delta_h = sum_c q_hc min_c on the tensor cores (rows = heads, every column alike)
+    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint4 *kmv = reinterpret_cast<const uint4 *>(sg.km + 32 * tig);
+      const uint4 *rqd = reinterpret_cast<const uint4 *>(rec + 40);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 mv = kmv[i], qv = rqd[i];
+        mma16816<__half>(dd, qv.x, 0u, qv.y, 0u, mv.x, mv.y);
+        mma16816<__half>(dd, qv.z, 0u, qv.w, 0u, mv.z, mv.w);
+      }
+    }
+    const float dlt = __shfl_sync(0xffffffffu, dd[0], 4 * tig) * c2;
+
+    // ---- K: scores of tokens 16m+g and 16m+g+8 for head tig
+    float sc[4][4];
+    {
+      const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
+      uint32_t X0[4][6], X1[4][6];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
+        const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
+        X0[m][0] = u0, X0[m][1] = __funnelshift_r(u0, u1, 8), X0[m][2] = u1;
+        X0[m][3] = __funnelshift_r(u1, u2, 8), X0[m][4] = u2, X0[m][5] = u2 >> 8;
+        X1[m][0] = v0, X1[m][1] = __funnelshift_r(v0, v1, 8), X1[m][2] = v1;
+        X1[m][3] = __funnelshift_r(v1, v2, 8), X1[m][4] = v2, X1[m][5] = v2 >> 8;
+        sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 9; ++k)
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int r0 = 2 * k, r1 = 2 * k + 1;
+          mma16816<__half>(sc[m], X0[m][ktab(r0, 0)] & kmask(r0), X1[m][ktab(r0, 0)] & kmask(r0),
+                           X0[m][ktab(r1, 0)] & kmask(r1), X1[m][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+        }
+    }
+    float s[4][2];
+    float bm = -INFINITY;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      s[m][0] = sg.ka[16 * m + g] * fmaf(sc[m][0] + sc[m][1], c1, dlt);
+      s[m][1] = sg.ka[16 * m + g + 8] * fmaf(sc[m][2] + sc[m][3], c1, dlt);
+      bm = fmaxf(bm, fmaxf(s[m][0], s[m][1]));
+      if (tig < G && !(isfinite(s[m][0]) && isfinite(s[m][1]))) st |= NSNKV_ST_OUTPUT_NONFINITE;
+    }
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+    const float m_new = fmaxf(m_run, bm);
+    const float r = m_run == -INFINITY ? 0.f : exp2f((m_run - m_new) * kLog2e);
+    const float mb = m_new * kLog2e;
+    float psum = 0.f, wsum = 0.f;
+    uint32_t PB[4][2];
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float p = exp2f(fmaf(s[m][i], kLog2e, -mb));
+        const float pv = p * sg.va[16 * m + g + 8 * i];
+        psum += p;
+        wsum += pv;
+        PB[m][i] = movtrans(split_hilo(pv));
+      }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+    }
+    l_run = l_run * r + psum;
+    m_run = m_new;
+    if (!__all_sync(0xffffffffu, r == 1.f)) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i][0] *= r, acc[i][1] *= r, acc[i][2] *= r, acc[i][3] *= r;
+    }
+
+    // ---- V: D[mt] (channel slots 16g+2mt | 16g+2mt+1, head tig hi | lo) over the 64 tokens
+    float D[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
+    {
+      const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + vword;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int ta = 16 * ks + 2 * tig;
+        uint32_t L[4], H[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = ta + (u & 1) + 8 * (u >> 1);  // ta, ta+1, ta+8, ta+9
+          const uint32_t w0 = vw[12 * t], w1 = vw[12 * t + 1];
+          L[u] = prmt(w0, w1, selL);
+          H[u] = prmt(w0, w1, selH);
+        }
+        uint32_t P[2][6];
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int x = 2 * pr, y = 2 * pr + 1;
+          P[pr][0] = prmt(L[x], L[y], vsel(0));
+          P[pr][1] = prmt(L[x], L[y], vsel(1));
+          P[pr][2] = prmt(L[x], L[y], vsel(2));
+          P[pr][3] = prmt(H[x], H[y], vsel(3));
+          P[pr][4] = prmt(H[x], H[y], vsel(4));
+          P[pr][5] = prmt(H[x], H[y], vsel(5));
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          constexpr uint32_t one = 0x00070007u;
+          const int i0 = 2 * mt, i1 = 2 * mt + 1;
+          mma16816<__half>(D[mt], P[0][vwin(i0)] & (one << vpos(i0)), P[0][vwin(i1)] & (one << vpos(i1)),
+                           P[1][vwin(i0)] & (one << vpos(i0)), P[1][vwin(i1)] & (one << vpos(i1)), PB[ks][0],
+                           PB[ks][1]);
+        }
+      }
+    }
+    // ---- epilogue: acc' += scale_c * D + min_c * 2^(pos_c - 24) * sum_t p_t alpha_t
+    {
+      const uint4 *vsv = reinterpret_cast<const uint4 *>(sg.vs + 16 * g);
+      const uint4 *vmv = reinterpret_cast<const uint4 *>(sg.vm + 16 * g);
+      const uint4 s0 = vsv[0], s1 = vsv[1], n0 = vmv[0], n1 = vmv[1];
+      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+      float wp[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) wp[p] = wsum * ldexpf(1.f, p - 24);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const float2 bs = Elem<__half>::to_f2(sw[mt]), ms = Elem<__half>::to_f2(nw[mt]);
+        acc[mt][0] = fmaf(bs.x, D[mt][0], fmaf(ms.x, wp[vpos(2 * mt)], acc[mt][0]));
+        acc[mt][1] = fmaf(bs.x, D[mt][1], acc[mt][1]);
+        acc[mt][2] = fmaf(bs.y, D[mt][2], fmaf(ms.y, wp[vpos(2 * mt + 1)], acc[mt][2]));
+        acc[mt][3] = fmaf(bs.y, D[mt][3], acc[mt][3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && j + kRing < njw) issue(j + kRing);
+  }
+  if (jfail >= 0 && lane == 0)  // give the copies still in flight a bounded chance to land
+    for (int jj = jfail + 1; jj < njw && jj < jfail + kRing; ++jj)
+      mbar_wait_bounded(&S.full[warp][jj & 1], (jj >> 1) & 1, a.status);
+
+  // ---- combine the four warps and write this chunk's partial
+  __syncthreads();
+  MergeSmem &M = S.u.merge;
+  if (tig < G) {
+    if (g == 0) {
+      M.m[warp][tig] = m_run;
+      M.l[warp][tig] = l_run;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int c = 16 * g + 2 * mt;
+      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * ldexpf(1.f, 24 - vpos(2 * mt));
+      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * ldexpf(1.f, 24 - vpos(2 * mt + 1));
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
+    float o = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
+      o += wt * M.acc[w][n][c];
+      l += wt * M.l[w][n];
+    }
+    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
+    a.part_o[row * kDim + c] = o;
+    if (c == 0) {
+      a.part_ml[row * 2] = mx;
+      a.part_ml[row * 2 + 1] = l;
+    }
+  }
+  if (st) set_status(a.status, st);
+}
+
 // ----------------------------------------------------------------- host side
 static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t max_tail) {
   // Aim for >= 4 CTAs per SM (148 SMs) while keeping the partials small.
@@ -648,6 +1064,7 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
   int64_t per_unit = (target + units - 1) / units;  // desired chunks per (seq, head)
   int64_t ch = (work + per_unit - 1) / per_unit;
+  ch = (ch + 3) / 4 * 4;  // whole rounds of the sealed kernel's four warps
   if (ch < 4) ch = 4;
   if (ch > 16) ch = 16;
   return static_cast<int>(ch);
@@ -693,15 +1110,19 @@ int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t 
   return batch * hq * mc * (kDim + 2) * static_cast<int64_t>(sizeof(float));
 }
 
-int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const void *q, const uint8_t *k_codes,
-                      const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale, const uint8_t *v_codes,
-                      const uint16_t *v_norm, const uint16_t *v_min, const uint16_t *v_scale, int64_t blk_stride_head,
-                      int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
-                      const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail, void *v_tail,
-                      int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
-                      int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new, void *out,
-                      float *out_f32, float *lse, void *workspace, int64_t workspace_bytes, int32_t *status,
-                      void *stream) {
+}  // extern "C"
+
+namespace nsnkv {
+static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, const void *q, const uint8_t *k_codes,
+                            const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
+                            const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min,
+                            const uint16_t *v_scale, const float *k_alpha, const float *v_alpha,
+                            int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
+                            int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                            void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                            const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new,
+                            const void *v_new, void *out, float *out_f32, float *lse, void *workspace,
+                            int64_t workspace_bytes, int32_t *status, void *stream) {
   if (batch <= 0 || hq <= 0 || h <= 0 || hq % h != 0 || max_blocks < 0 || max_tail < 0) return NSNKV_ERR_ARG;
   if (bits < 3 || bits > 5 || (dtype != NSNKV_F16 && dtype != NSNKV_BF16)) return NSNKV_ERR_ARG;
   if (!q || !out || !status || !workspace || !aligned16(q) || !aligned16(out)) return NSNKV_ERR_ARG;
@@ -755,9 +1176,28 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
   a.status = status;
   const int G = hq / h;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dim3 grid(a.max_chunks, h, static_cast<unsigned>(batch));
-  int rc = dtype == NSNKV_F16 ? dispatch_bits<__half>(bits, G, a, grid, st)
-                              : dispatch_bits<__nv_bfloat16>(bits, G, a, grid, st);
+  int rc = NSNKV_OK;
+  if (k_alpha && v_alpha && bits == 3 && dtype == NSNKV_F16 && G <= 4 && max_blocks > 0) {
+    // sealed chunks on the tensor-core kernel, native-row chunks on attn_partial_kernel
+    if (!aligned16(k_alpha) || !aligned16(v_alpha)) return NSNKV_ERR_ARG;
+    a.ka = k_alpha;
+    a.va = v_alpha;
+    const size_t smem = sizeof(s3::SSmem);
+    if (cudaFuncSetAttribute(attn_sealed3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return NSNKV_ERR_CUDA;
+    const int sealed_chunks = (max_blocks + a.chunk_blocks - 1) / a.chunk_blocks;
+    attn_sealed3_kernel<<<dim3(sealed_chunks, h, static_cast<unsigned>(batch)), kThreads, smem, st>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
+    if (any_tail) {
+      a.raw_only = 1;
+      const int raw_chunks = a.max_chunks - sealed_chunks;
+      rc = launch_attn<3, __half>(a, dim3(raw_chunks, h, static_cast<unsigned>(batch)), st);
+    }
+  } else {
+    dim3 grid(a.max_chunks, h, static_cast<unsigned>(batch));
+    rc = dtype == NSNKV_F16 ? dispatch_bits<__half>(bits, G, a, grid, st)
+                            : dispatch_bits<__nv_bfloat16>(bits, G, a, grid, st);
+  }
   if (rc != NSNKV_OK) return rc;
   dim3 mgrid(hq, static_cast<unsigned>(batch));
   if (dtype == NSNKV_F16)
@@ -765,6 +1205,44 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
   else
     attn_merge_kernel<__nv_bfloat16><<<mgrid, kDim, 0, st>>>(a, G, static_cast<__nv_bfloat16 *>(out), out_f32, lse);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+}  // namespace nsnkv
+
+extern "C" {
+
+int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const void *q, const uint8_t *k_codes,
+                      const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale, const uint8_t *v_codes,
+                      const uint16_t *v_norm, const uint16_t *v_min, const uint16_t *v_scale, int64_t blk_stride_head,
+                      int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
+                      const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail, void *v_tail,
+                      int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
+                      int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new, void *out,
+                      float *out_f32, float *lse, void *workspace, int64_t workspace_bytes, int32_t *status,
+                      void *stream) {
+  return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
+                          v_scale, nullptr, nullptr, blk_stride_head, blk_stride_page, block_table, table_stride,
+                          n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
+                          tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
+                          workspace_bytes, status, stream);
+}
+
+int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
+                            const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
+                            const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
+                            const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
+                            const float *v_alpha, int64_t blk_stride_head, int64_t blk_stride_page,
+                            const int32_t *block_table, int64_t table_stride, const int32_t *n_blocks,
+                            int32_t n_blocks_const, int32_t max_blocks, void *k_tail, void *v_tail,
+                            int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
+                            int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new,
+                            void *out, float *out_f32, float *lse, void *workspace, int64_t workspace_bytes,
+                            int32_t *status, void *stream) {
+  if (max_blocks > 0 && (!k_alpha || !v_alpha)) return NSNKV_ERR_ARG;
+  return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
+                          v_scale, k_alpha, v_alpha, blk_stride_head, blk_stride_page, block_table, table_stride,
+                          n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
+                          tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
+                          workspace_bytes, status, stream);
 }
 
 static int merge_shards_launch(int n_shards, int64_t rows, const float *o, int64_t o_stride, const float *lse,

@@ -589,6 +589,69 @@ __global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_
   }
 }
 
+// ----------------------------------------------------------------- per-token renorm factors
+// alpha_t = n_t / max(||d_t||, eps), and 0 when n_t == 0, with d = min + scale * code in
+// fp32: the factor nsn_decode applies to a row (loop_kv_nb06_primitives.py:57-66,
+// y = n * d / max(||d||, eps)).  Decode attention over a cache that stores it beside
+// each block does not recompute ||d|| on every step.  One 256-thread CTA per block:
+// thread (t = tid / 4, quarter) sums 32 channels of token t.
+template <int BITS>
+__device__ void renorm_block(const uint8_t *codes, const uint16_t *norm, const uint16_t *mn, const uint16_t *sc,
+                             float *alpha) {
+  const int t = threadIdx.x >> 2, part = threadIdx.x & 3;
+  constexpr int total = code_bytes(BITS);
+  float ss = 0.f;
+  for (int c = 32 * part; c < 32 * part + 32; ++c) {
+    const int bit = (t * kDim + c) * BITS;
+    const int byte = bit >> 3, sh = bit & 7;
+    uint32_t w = codes[byte];
+    if (sh + BITS > 8 && byte + 1 < total) w |= static_cast<uint32_t>(codes[byte + 1]) << 8;
+    const float x = static_cast<float>((w >> sh) & ((1u << BITS) - 1u));
+    const float d = __fadd_rn(half_bits_to_f(mn[c]), __fmul_rn(half_bits_to_f(sc[c]), x));
+    ss = __fmaf_rn(d, d, ss);
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  if (part == 0) {
+    const float n = half_bits_to_f(norm[t]);
+    alpha[t] = n == 0.f ? 0.f : __fdiv_rn(n, fmaxf(__fsqrt_rn(ss), kEps));
+  }
+}
+
+// Blocks laid out as nsnkv_encode_blocks writes them: block (row r, i) at r * row_stride + offset + i.
+template <int BITS>
+__global__ void __launch_bounds__(256) renorm_blocks_kernel(const uint8_t *codes, const uint16_t *norm,
+                                                            const uint16_t *mn, const uint16_t *sc,
+                                                            int64_t blocks_per_row, int64_t row_stride,
+                                                            int64_t offset, float *alpha) {
+  const int64_t r = blockIdx.x / blocks_per_row, i = blockIdx.x % blocks_per_row;
+  const int64_t blk = r * row_stride + offset + i;
+  renorm_block<BITS>(codes + blk * code_bytes(BITS), norm + blk * kBlock, mn + blk * kDim, sc + blk * kDim,
+                     alpha + blk * kBlock);
+}
+
+// The blocks seal_kernel writes in the same step (same predicate and page).
+template <int BITS>
+__global__ void __launch_bounds__(256) renorm_seal_kernel(const int32_t *tail_len, const int32_t *n_blocks,
+                                                          int pending, const int32_t *table, int64_t table_stride,
+                                                          const uint8_t *k_codes, const uint16_t *k_norm,
+                                                          const uint16_t *k_min, const uint16_t *k_scale,
+                                                          const uint8_t *v_codes, const uint16_t *v_norm,
+                                                          const uint16_t *v_min, const uint16_t *v_scale,
+                                                          float *k_alpha, float *v_alpha, int64_t sh, int64_t sp) {
+  const int h = blockIdx.x, kv = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  if (tail_len[b] + pending < kBlock) return;
+  const int32_t page = table[b * table_stride + n_blocks[b]];
+  const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
+  if (kv == 0)
+    renorm_block<BITS>(k_codes + blk * code_bytes(BITS), k_norm + blk * kBlock, k_min + blk * kDim,
+                       k_scale + blk * kDim, k_alpha + blk * kBlock);
+  else
+    renorm_block<BITS>(v_codes + blk * code_bytes(BITS), v_norm + blk * kBlock, v_min + blk * kDim,
+                       v_scale + blk * kDim, v_alpha + blk * kBlock);
+}
+
 // ----------------------------------------------------------------- host dispatch
 template <typename T>
 static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits, int norm_order, uint8_t *codes,
@@ -678,7 +741,8 @@ template <typename T>
 static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tail, int64_t tss, int64_t tsh,
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
-                       uint16_t *vm, uint16_t *vs, int64_t sh, int64_t sp, int32_t *status, cudaStream_t st) {
+                       uint16_t *vm, uint16_t *vs, float *ka, float *va, int64_t sh, int64_t sp, int32_t *status,
+                       cudaStream_t st) {
   const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
@@ -689,6 +753,9 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     k<<<grid, 256, smem, st>>>(static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss, tsh,   \
                                tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, sh, \
                                sp, status);                                                                \
+    if (ka)                                                                                                \
+      renorm_seal_kernel<B><<<grid, 256, 0, st>>>(tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, \
+                                                  vn, vm, vs, ka, va, sh, sp);                             \
     break;                                                                                                 \
   }
   switch (bits) {
@@ -783,33 +850,81 @@ int nsnkv_unpack(const uint8_t *payload, int64_t count, int bits, uint8_t *out, 
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
-int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
-                          int64_t tail_stride_seq, int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks,
-                          int pending_append, const int32_t *block_table, int64_t table_stride, uint8_t *k_codes,
-                          uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm,
-                          uint16_t *v_min, uint16_t *v_scale, int64_t blk_stride_head, int64_t blk_stride_page,
-                          int32_t *status, void *stream) {
+static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail, int64_t tail_stride_seq,
+                     int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks, int pending_append,
+                     const int32_t *block_table, int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm,
+                     uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
+                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_stride_head,
+                     int64_t blk_stride_page, int32_t *status, void *stream) {
   if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
   if (batch == 0) return NSNKV_OK;
   if (!k_tail || !v_tail || !tail_len || !n_blocks || !block_table || !k_codes || !v_codes || !status)
     return NSNKV_ERR_ARG;
   if (!aligned16(k_tail) || !aligned16(v_tail) || !aligned16(k_codes) || !aligned16(v_codes)) return NSNKV_ERR_ARG;
+  if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
   if (tail_stride_head < kBlock || tail_stride_seq < tail_stride_head * h) return NSNKV_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case NSNKV_F16:
       return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
                                  n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
-                                 k_scale, v_codes, v_norm, v_min, v_scale, blk_stride_head, blk_stride_page, status,
-                                 st);
+                                 k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, blk_stride_head,
+                                 blk_stride_page, status, st);
     case NSNKV_BF16:
       return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                                         tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
-                                        k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, blk_stride_head,
-                                        blk_stride_page, status, st);
+                                        k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha,
+                                        blk_stride_head, blk_stride_page, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
+}
+
+int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
+                          int64_t tail_stride_seq, int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks,
+                          int pending_append, const int32_t *block_table, int64_t table_stride, uint8_t *k_codes,
+                          uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm,
+                          uint16_t *v_min, uint16_t *v_scale, int64_t blk_stride_head, int64_t blk_stride_page,
+                          int32_t *status, void *stream) {
+  return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
+                   pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
+                   v_min, v_scale, nullptr, nullptr, blk_stride_head, blk_stride_page, status, stream);
+}
+
+int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
+                                int64_t tail_stride_seq, int64_t tail_stride_head, int32_t *tail_len,
+                                int32_t *n_blocks, int pending_append, const int32_t *block_table,
+                                int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min,
+                                uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
+                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_stride_head,
+                                int64_t blk_stride_page, int32_t *status, void *stream) {
+  if (!k_alpha || !v_alpha) return NSNKV_ERR_ARG;
+  return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
+                   pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
+                   v_min, v_scale, k_alpha, v_alpha, blk_stride_head, blk_stride_page, status, stream);
+}
+
+int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
+                       const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
+                       void *stream) {
+  if (bits < 3 || bits > 5 || rows < 0 || blocks_per_row < 0 || offset < 0) return NSNKV_ERR_ARG;
+  if (rows == 0 || blocks_per_row == 0) return NSNKV_OK;
+  if (!codes || !norm || !min || !scale || !alpha || row_stride < blocks_per_row + offset) return NSNKV_ERR_ARG;
+  if (rows * blocks_per_row > 0x7fffffffLL) return NSNKV_ERR_TOO_LARGE;
+  const unsigned grid = static_cast<unsigned>(rows * blocks_per_row);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (bits) {
+    case 3:
+      renorm_blocks_kernel<3><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      break;
+    case 4:
+      renorm_blocks_kernel<4><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      break;
+    default:
+      renorm_blocks_kernel<5><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      break;
+  }
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
 }  // extern "C"

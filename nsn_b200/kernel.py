@@ -47,10 +47,11 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
                      k_tail=None, v_tail=None, tail_stride_seq=0, tail_stride_head=0, tail_len=0, max_tail=0,
                      block_table=None, k_new=None, v_new=None, out=None, out_f32=None, lse=None, status=None,
                      ws=None):
-    """Direct binding of nsnkv_decode_attn.
+    """Direct binding of nsnkv_decode_attn (nsnkv_decode_attn_alpha when both pools carry "alpha").
 
-    q [B, hq, 128]; k_pool/v_pool dicts of codes/norm/min/scale tensors (or None
-    when max_blocks == 0); n_blocks/tail_len either ints (same for every
+    q [B, hq, 128]; k_pool/v_pool dicts of codes/norm/min/scale tensors, plus the
+    per-token renorm factors "alpha" (fp32, 64 per block) when the cache keeps them
+    (or None when max_blocks == 0); n_blocks/tail_len either ints (same for every
     sequence) or int32 CUDA tensors [B].  Returns (out, status).
     """
     L.require_cuda()
@@ -68,17 +69,22 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     tl_t = tail_len if isinstance(tail_len, torch.Tensor) else None
     kp = k_pool or {}
     vp = v_pool or {}
-    rc = lib.nsnkv_decode_attn(
-        B, hq, h, bits, L.DTYPE_CODE[q.dtype], L.ptr(q),
-        L.ptr(kp.get("codes")), L.ptr(kp.get("norm")), L.ptr(kp.get("min")), L.ptr(kp.get("scale")),
-        L.ptr(vp.get("codes")), L.ptr(vp.get("norm")), L.ptr(vp.get("min")), L.ptr(vp.get("scale")),
+    blocks = (L.ptr(kp.get("codes")), L.ptr(kp.get("norm")), L.ptr(kp.get("min")), L.ptr(kp.get("scale")),
+              L.ptr(vp.get("codes")), L.ptr(vp.get("norm")), L.ptr(vp.get("min")), L.ptr(vp.get("scale")))
+    if kp.get("alpha") is not None and vp.get("alpha") is not None:
+        entry, name = lib.nsnkv_decode_attn_alpha, "nsnkv_decode_attn_alpha"
+        blocks = blocks + (L.ptr(kp["alpha"]), L.ptr(vp["alpha"]))
+    else:
+        entry, name = lib.nsnkv_decode_attn, "nsnkv_decode_attn"
+    rc = entry(
+        B, hq, h, bits, L.DTYPE_CODE[q.dtype], L.ptr(q), *blocks,
         blk_stride_head, blk_stride_page, L.ptr(block_table), block_table.shape[-1] if block_table is not None else 0,
         L.ptr(nb_t), 0 if nb_t is not None else int(n_blocks), int(max_blocks),
         L.ptr(k_tail), L.ptr(v_tail), tail_stride_seq, tail_stride_head,
         L.ptr(tl_t), 0 if tl_t is not None else int(tail_len), int(max_tail),
         L.ptr(k_new), L.ptr(v_new), L.ptr(out), L.ptr(out_f32), L.ptr(lse),
         L.ptr(ws), ws.numel(), L.ptr(status), L.stream_handle(dev))
-    L.check(rc, "nsnkv_decode_attn")
+    L.check(rc, name)
     return out, status
 
 

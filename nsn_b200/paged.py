@@ -17,7 +17,10 @@ between steps (the benchmark specification's batched policy; the reference's
 per-slot PackedCache keeps 64..127, see nsn_b200.packed).
 
 Layout (head-major pools so one sequence's blocks of one head are contiguous):
-  codes [h, pages, code_bytes] uint8, norm [h, pages, 64], min/scale [h, pages, 128] fp16
+  codes [h, pages, code_bytes] uint8, norm [h, pages, 64], min/scale [h, pages, 128] fp16,
+  alpha [h, pages, 64] fp32: per-token renorm factors n / max(||d||, eps), written
+  whenever a block is (sealed, prefilled or imported) so attention does not recompute
+  ||d|| per step; derived data, not part of the reference's format or of the exports
   block (sequence b, head j, block i) = pool row j, page block_table[b, i]
   block_table [batch, max_blocks] int32 (sequence b owns pages b*max_blocks ..)
   n_blocks, tail_len [batch] int32 (device), k_tail/v_tail [batch, h, 64, 128].
@@ -126,7 +129,8 @@ class PagedKVCache:
             return dict(codes=torch.zeros((h, self.pages, cb), dtype=torch.uint8, device=dev),
                         norm=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float16, device=dev),
                         min=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
-                        scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev))
+                        scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
+                        alpha=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float32, device=dev))
 
         self.k_pool, self.v_pool = pool(), pool()
         self.block_table = torch.arange(self.pages, dtype=torch.int32, device=dev).reshape(batch, max_blocks)
@@ -207,6 +211,7 @@ class PagedKVCache:
             pool["norm"][:, pages] = g["metas"][0].reshape(h, n, w.BLOCK).to(self.device)
             pool["min"][:, pages] = g["metas"][1].reshape(h, n, w.DIM).to(self.device)
             pool["scale"][:, pages] = g["metas"][2].reshape(h, n, w.DIM).to(self.device)
+            w.block_renorm(pool, self.bits, h, n, self.pages, b * self.max_blocks)
         for src, pool, tail in ((kt, self.k_pool, self.k_tail), (vt, self.v_pool, self.v_tail)):
             src = src[0].to(self.device, self.dtype)
             if extra:
@@ -241,15 +246,15 @@ class PagedKVCache:
 
     def seal(self, pending_append: int = 1):
         lib = L.load()
-        rc = lib.nsnkv_seal_full_tails(
+        rc = lib.nsnkv_seal_full_tails_alpha(
             self.batch, self.h, self.bits, L.DTYPE_CODE[self.dtype], L.ptr(self.k_tail), L.ptr(self.v_tail),
             self.h * w.BLOCK, w.BLOCK, L.ptr(self.tail_len), L.ptr(self.n_blocks), pending_append,
             L.ptr(self.block_table), self.max_blocks,
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
-            L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), self.pages, 1, L.ptr(self.status),
-            L.stream_handle(self.device))
-        L.check(rc, "nsnkv_seal_full_tails")
+            L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
+            L.ptr(self.v_pool["alpha"]), self.pages, 1, L.ptr(self.status), L.stream_handle(self.device))
+        L.check(rc, "nsnkv_seal_full_tails_alpha")
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, out=None):
         """One decode step: append (k_new, v_new) [batch, h, 128], attend with q, seal full tails."""
@@ -270,9 +275,17 @@ class PagedKVCache:
         per_block = w.code_bytes(self.bits) + w.BLOCK * 2 + w.DIM * 4 + 12
         return 2 * self.h * (nb * per_block + t * w.DIM * 2)
 
+    def uses_alpha_path(self):
+        """True when attend() runs the sealed blocks through the renorm-factor kernel."""
+        return self.bits == 3 and self.dtype == torch.float16 and self.hq // self.h <= 4
+
     def read_bytes_per_step(self):
-        """Algorithmic bytes one attend() reads: sealed blocks (codes + metadata) and tails, q and out."""
+        """Algorithmic bytes one attend() reads: sealed blocks (codes + metadata) and tails, q and out.
+
+        The renorm-factor kernel reads codes, min, scale and the fp32 factors of each
+        block; the restore kernel reads codes, min, scale and the fp16 norms."""
         nb = int(self.n_blocks.sum())
         t = int(self.tail_len.sum())
-        per_block = w.code_bytes(self.bits) + w.BLOCK * 2 + w.DIM * 4
+        per_tok = 4 if self.uses_alpha_path() else 2
+        per_block = w.code_bytes(self.bits) + w.BLOCK * per_tok + w.DIM * 4
         return 2 * self.h * (nb * per_block + t * w.DIM * 2) + 2 * self.batch * self.hq * w.DIM * 2

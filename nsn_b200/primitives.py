@@ -153,6 +153,8 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
             L.ptr(xc), L.DTYPE_CODE[x.dtype], rows, bpr, bits, order, L.ptr(codes), L.ptr(q), L.ptr(n), L.ptr(m),
             L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, L.ptr(status), L.stream_handle(dev)),
             "nsnkv_encode_blocks")
+        if out is not None and out.get("alpha") is not None and codes is not None:
+            block_renorm(out, bits, rows, bpr, stride, offset)
     if check:
         st = int(status.item())
         _status_to_error(st, "Nonfinite input to NSN")
@@ -160,6 +162,22 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
         res["status"] = status
     res.update(codes=codes, q=q, metas=(n, m, s), headers=hdr)
     return res
+
+
+def block_renorm(pool, bits: int, rows: int, blocks_per_row: int, row_stride: int, offset: int = 0):
+    """Fill pool["alpha"] (fp32, 64 per block) for blocks (r, i) at r*row_stride + offset + i.
+
+    alpha_t = n_t / max(||d_t||, 1e-12) with d = min + scale * code, 0 when n_t == 0:
+    the per-token factor of nsn_decode (loop_kv_nb06_primitives.py:57-66) that
+    nsnkv_decode_attn_alpha reads instead of recomputing ||d||.
+    """
+    require(all(pool[k].is_cuda for k in ("codes", "norm", "min", "scale", "alpha")), "renorm pools on CUDA")
+    require(pool["alpha"].dtype == torch.float32, "renorm alpha dtype")
+    if rows and blocks_per_row:
+        L.check(L.load().nsnkv_block_renorm(
+            bits, rows, blocks_per_row, L.ptr(pool["codes"]), L.ptr(pool["norm"]), L.ptr(pool["min"]),
+            L.ptr(pool["scale"]), row_stride, offset, L.ptr(pool["alpha"]), L.stream_handle(pool["codes"].device)),
+            "nsnkv_block_renorm")
 
 
 def nsn_encode(x: torch.Tensor, bits: int):

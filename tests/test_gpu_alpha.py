@@ -1,0 +1,207 @@
+"""GPU tests of the renorm-factor path (nsnkv_block_renorm, nsnkv_seal_full_tails_alpha,
+nsnkv_decode_attn_alpha).
+
+* alpha = n / max(||min + scale * code||, 1e-12) per token against the oracle's decode.
+* Attention through the paged cache (sealed blocks on attn_sealed3_kernel, tails on
+  attn_partial_kernel) against fp64 attention over the exact fp32 restore of the
+  same blocks (nsn_decode without the final cast), with a tight bar, and against the
+  reference bridge (rows rounded to fp16) with the parity bar.
+* GQA groups 1..4, q magnitudes that need the exponent shift, zero-norm tokens,
+  constant blocks, chunk sizes that leave warps idle, appended tokens and seals.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nsn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TIGHT = (1e-4, 2e-5)  # (rtol, atol) against the exact fp32 restore: fp32 accumulation only
+
+
+def exact_restore(q8, n16, m16, s16):
+    """nsn_decode (loop_kv_nb06_primitives.py:57-66) in fp64, without the cast to fp16."""
+    d = m16.astype(np.float64) + s16.astype(np.float64) * q8.astype(np.float64)
+    den = np.maximum(np.sqrt((d * d).sum(-1, keepdims=True)), 1e-12)
+    n = n16.astype(np.float64)
+    return np.where(n == 0, 0.0, n * d / den)
+
+
+def attention64(q, k, v):
+    """q [hq,128], k/v [h,T,128] fp64 -> [hq,128] (repeat_kv grouping, scale 1/sqrt(128))."""
+    h = k.shape[0]
+    rep = q.shape[0] // h
+    out = np.empty((q.shape[0], 128))
+    for j in range(q.shape[0]):
+        s = k[j // rep] @ q[j] / np.sqrt(128.0)
+        p = np.exp(s - s.max())
+        out[j] = (p[:, None] * v[j // rep]).sum(0) / p.sum()
+    return out
+
+
+def history_oracle(hk, hv, nb, rows="exact"):
+    """Full K/V [h,T,128] in fp64: nb sealed blocks restored (exactly, or as the bridge's fp16 rows) + the tail."""
+    parts_k, parts_v = [], []
+    for src, parts in ((hk, parts_k), (hv, parts_v)):
+        h = src.shape[0]
+        if nb:
+            x = src[None, :, :nb * 64].astype(np.float32).reshape(1, h, nb, 64, 128)
+            q8, n, m, s, st = O.nsn_encode(x, 3)
+            assert st == 0
+            if rows == "exact":
+                y = exact_restore(q8, n, m, s)
+            else:
+                y = np.asarray(O.nsn_decode(q8, n, m, s, "float16"), np.float64)
+            parts.append(y.reshape(h, nb * 64, 128))
+        parts.append(src[:, nb * 64:].astype(np.float64))
+    return np.concatenate(parts_k, 1), np.concatenate(parts_v, 1)
+
+
+def make_cache(rng, lens, h, hq, max_blocks, q_scale=1.0):
+    from nsn_b200 import workloads
+    from nsn_b200.paged import PagedKVCache
+    hk = [workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5) for L in lens]
+    hv = [workloads.np_kv(rng, (h, L, 128), (), 0.5) for L in lens]
+    cache = PagedKVCache(len(lens), h, max_blocks=max_blocks, bits=3, dtype=torch.float16, hq=hq)
+    for b in range(len(lens)):
+        cache.prefill(b, torch.from_numpy(hk[b]).cuda(), torch.from_numpy(hv[b]).cuda())
+    q = (rng.standard_normal((len(lens), hq, 128)) * q_scale / np.sqrt(128)).astype(np.float16)
+    return cache, hk, hv, q
+
+
+@pytest.mark.parametrize("bits", [3, 4, 5])
+def test_block_renorm_matches_oracle(bits):
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(bits)
+    x = workloads.np_kv(rng, (3, 5, 64, 128), workloads.K_OUTLIERS_4, 0.5)
+    x[0, 1, 7] = 0.0  # a zero-norm token
+    x[1, 2] = 0.25    # a constant block (all codes 0, scale 0)
+    xt = torch.from_numpy(x).cuda()
+    pool = dict(codes=torch.zeros((3, 7, w.code_bytes(bits)), dtype=torch.uint8, device="cuda"),
+                norm=torch.zeros((3, 7, 64), dtype=torch.float16, device="cuda"),
+                min=torch.zeros((3, 7, 128), dtype=torch.float16, device="cuda"),
+                scale=torch.zeros((3, 7, 128), dtype=torch.float16, device="cuda"),
+                alpha=torch.full((3, 7, 64), -1.0, dtype=torch.float32, device="cuda"))
+    w.encode_blocks(xt, bits, out=pool, out_row_stride=7, out_offset=1, check=False)
+    q8, n, m, s, st = O.nsn_encode(x.astype(np.float32), bits)
+    d = m.astype(np.float64) + s.astype(np.float64) * q8.astype(np.float64)
+    den = np.maximum(np.sqrt((d * d).sum(-1)), 1e-12)
+    n64 = n[..., 0].astype(np.float64)
+    want = np.where(n64 == 0, 0.0, n64 / den)
+    got = pool["alpha"].cpu().numpy()
+    assert np.all(got[:, 0] == -1.0) and np.all(got[:, 6] == -1.0), "wrote outside the encoded blocks"
+    np.testing.assert_allclose(got[:, 1:6], want, rtol=2e-6, atol=0)
+    assert np.all(got[0, 2, 7] == 0.0)
+
+
+@pytest.mark.parametrize("h,hq", [(2, 8), (2, 6), (4, 8), (3, 3)])
+def test_alpha_path_tight_against_exact_restore(h, hq):
+    rng = np.random.default_rng(100 + hq)
+    lens = [64, 1, 130, 64 * 9 + 17, 64 * 21, 64 * 5 + 63]
+    cache, hk, hv, q = make_cache(rng, lens, h, hq, max_blocks=22)
+    assert cache.uses_alpha_path()
+    out32 = torch.empty((len(lens), hq, 128), dtype=torch.float32, device="cuda")
+    out = cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
+    cache.check()
+    got32, got16 = out32.cpu().numpy(), out.float().cpu().numpy()
+    for b, L in enumerate(lens):
+        nb = L // 64
+        k, v = history_oracle(hk[b], hv[b], nb, "exact")
+        want = attention64(q[b].astype(np.float64), k, v)
+        ok, err = O.within_tolerance(got32[b], want, *TIGHT)
+        assert ok, (b, L, err)
+        kb, vb = history_oracle(hk[b], hv[b], nb, "bridge")
+        ok, err = O.within_tolerance(got16[b], attention64(q[b].astype(np.float64), kb, vb), *O.TOLERANCE["float16"])
+        assert ok, (b, L, err)
+
+
+@pytest.mark.parametrize("q_scale", [1e-3, 300.0, 4000.0])
+def test_alpha_path_q_magnitudes(q_scale):
+    """q far from unit scale: tiny values and values whose q * 2^7 leaves the fp16 range.
+
+    fp32 carries a logit s to about 2^-24 |s|, so an exact fp32 computation already
+    moves the output by ~1e-7 |s| per unit of value spread; the bar adds 1e-6 * max |s|
+    (q x 300 gives logits near 10^3)."""
+    rng = np.random.default_rng(7)
+    lens = [64 * 12 + 5, 64 * 4]
+    cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=13, q_scale=q_scale)
+    out32 = torch.empty((len(lens), 8, 128), dtype=torch.float32, device="cuda")
+    cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
+    cache.check()
+    for b, L in enumerate(lens):
+        k, v = history_oracle(hk[b], hv[b], L // 64, "exact")
+        q64 = q[b].astype(np.float64)
+        want = attention64(q64, k, v)
+        logit = np.abs(np.einsum("jd,jtd->jt", q64, np.repeat(k, 4, 0))).max() / np.sqrt(128.0)
+        ok, err = O.within_tolerance(out32[b].cpu().numpy(), want, TIGHT[0], TIGHT[1] + 1e-6 * logit)
+        assert ok, (q_scale, b, err, logit)
+
+
+def test_alpha_path_zero_and_constant_blocks():
+    from nsn_b200 import workloads
+    from nsn_b200.paged import PagedKVCache
+    rng = np.random.default_rng(3)
+    h, hq, L = 2, 8, 64 * 6 + 9
+    hk = workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5)
+    hv = workloads.np_kv(rng, (h, L, 128), (), 0.5)
+    hk[:, 64:128] = 0.0          # a zero K block: every norm 0
+    hv[0, 128:192] = 0.5         # a constant V block: scale 0
+    hk[1, 200:203] = 0.0         # zero-norm tokens inside a block
+    hv[1, 300] = 0.0
+    cache = PagedKVCache(1, h, max_blocks=8, bits=3, dtype=torch.float16, hq=hq)
+    cache.prefill(0, torch.from_numpy(hk).cuda(), torch.from_numpy(hv).cuda())
+    q = (rng.standard_normal((1, hq, 128)) / np.sqrt(128)).astype(np.float16)
+    out32 = torch.empty((1, hq, 128), dtype=torch.float32, device="cuda")
+    cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
+    cache.check()
+    k, v = history_oracle(hk, hv, L // 64, "exact")
+    ok, err = O.within_tolerance(out32[0].cpu().numpy(), attention64(q[0].astype(np.float64), k, v), *TIGHT)
+    assert ok, err
+
+
+def test_alpha_path_agrees_with_restore_path():
+    """The same cache attended through nsnkv_decode_attn (norms, bridge rounding) and the renorm-factor kernel."""
+    from nsn_b200.kernel import decode_attention
+    from nsn_b200 import primitives as w
+    rng = np.random.default_rng(11)
+    lens = [64 * 30 + 3, 64 * 7, 64 * 16 + 40]
+    cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=31)
+    qt = torch.from_numpy(q).cuda()
+    fast = cache.attend(qt).float().cpu().numpy()
+    pools = [{k: p[k] for k in ("codes", "norm", "min", "scale")} for p in (cache.k_pool, cache.v_pool)]
+    slow, st = decode_attention(
+        qt, pools[0], pools[1], h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1,
+        n_blocks=cache.n_blocks, max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
+        tail_stride_seq=cache.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=cache.tail_len, max_tail=w.BLOCK - 1,
+        block_table=cache.block_table)
+    assert int(st.item()) == 0
+    ok, err = O.within_tolerance(fast, slow.float().cpu().numpy(), *O.TOLERANCE["float16"])
+    assert ok, err
+
+
+def test_seal_writes_renorm_factors():
+    """After decode steps that seal pages, every sealed page's alpha equals nsnkv_block_renorm's."""
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(5)
+    lens = [60, 120, 64]
+    cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=4)
+    for s in range(70):
+        qq = (rng.standard_normal((3, 8, 128)) / np.sqrt(128)).astype(np.float16)
+        kn = workloads.np_kv(rng, (3, 2, 1, 128), workloads.K_OUTLIERS_4, 0.5)[:, :, 0]
+        vn = workloads.np_kv(rng, (3, 2, 1, 128), (), 0.5)[:, :, 0]
+        cache.step(torch.from_numpy(qq).cuda(), torch.from_numpy(kn).cuda(), torch.from_numpy(vn).cuda())
+    cache.check()
+    nb = cache.n_blocks.cpu().tolist()
+    assert nb == [(L + 70) // 64 for L in lens]
+    for pool in (cache.k_pool, cache.v_pool):
+        sealed = pool["alpha"].clone()
+        pool["alpha"].fill_(-1.0)
+        for b in range(3):
+            w.block_renorm(pool, 3, cache.h, nb[b], cache.pages, b * cache.max_blocks)
+        torch.cuda.synchronize()
+        for b in range(3):
+            pages = cache.block_table[b, :nb[b]].long()
+            assert torch.equal(sealed[:, pages], pool["alpha"][:, pages]), b
