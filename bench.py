@@ -568,8 +568,8 @@ def main():
                                          "(profiles/attn_partial_cfg2.md), scaled to this launch's algorithmic bytes",
                          "bytes_per_launch": bytes_attn},
             "e2e": e2e,
-            # attend: sealed kernel + tail kernel + merge (2 without the renorm path); seal: encode +
-            # renorm + counters (2 without it)
+            # attend: sealed kernel + tail kernel + merge (restore kernel + merge without the renorm
+            # path); seal: encode + renorm + counters (encode + counters without it)
             "gpu_launches": (6 if cache.uses_alpha_path() else 4) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,

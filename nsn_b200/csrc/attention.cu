@@ -665,7 +665,7 @@ __global__ void __launch_bounds__(128) merge_shards_kernel(int n_shards, int64_t
 // No restored K or V value is formed anywhere.
 namespace s3 {
 
-constexpr int kRing = 2;  // TMA stages per warp
+constexpr int kRing = 6;  // TMA stages per CTA: block li of a chunk lives in stage li % kRing
 constexpr int kRec = 60;  // words of a lane's constant record: stride 4 * odd -> conflict-free 128-bit loads
 constexpr int kCB = 3072;  // INT3 code bytes per block
 
@@ -679,12 +679,16 @@ static_assert(sizeof(SStage) == 7680, "stage layout");
 
 struct SSmem {
   union {
-    SStage stage[kWarps][kRing];
+    SStage stage[kRing];
     MergeSmem merge;  // after the last block of every warp
   } u;
   uint32_t rec[32][kRec];  // per lane: [0,18) qa, [20,38) qz, [40,56) Delta A fragments
-  uint64_t full[kWarps][kRing];
-  float qmax[kWarps];
+  // Block B completes on full[B % kRing][(B / kRing) & 1], parity (B / (2 kRing)) & 1.  Two
+  // barriers per stage: warp B % 4 consumed block B - 2 kRing (the same barrier's previous
+  // phase) before it waits for B, so a parity wait never meets a barrier two phases behind.
+  uint64_t full[kRing][2];
+  int32_t nissued[kRing][2];  // copies started per barrier (read only after a failed wait)
+  int32_t failed;
 };
 
 // K side.  A lane group (tig) covers channels 32*tig + j, j = 0..31 of a token row: 96
@@ -747,7 +751,7 @@ __device__ __forceinline__ uint32_t split_hilo(float w) {
 
 }  // namespace s3
 
-__global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArgs a) {
   using namespace s3;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SSmem &S = *reinterpret_cast<SSmem *>(smem_raw);
@@ -762,60 +766,16 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
   const int nloc = min(nb - blk0, a.chunk_blocks);
   const __half *qb = static_cast<const __half *>(a.q) + (b * a.hq + static_cast<int64_t>(h) * G) * kDim;
 
-  // ---- q exponent: every |q| * 2^(7 - kq) stays below 2^15, so q * 2^(7 - pos - kq) is a finite fp16
-  float qm = 0.f;
-  for (int e = tid; e < G * kDim; e += kThreads) qm = fmaxf(qm, fabsf(__half2float(qb[e])));
-#pragma unroll
-  for (int o = 16; o; o >>= 1) qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, o));
-  if (lane == 0) S.qmax[warp] = qm;
-  if (lane == 0) {
-    mbar_init(&S.full[warp][0], 1);
-    mbar_init(&S.full[warp][1], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  qm = fmaxf(fmaxf(S.qmax[0], S.qmax[1]), fmaxf(S.qmax[2], S.qmax[3]));
-  int qe = 0;
-  frexpf(qm, &qe);
-  const int kq = qe > 8 ? qe - 8 : 0;
-
-  // ---- per-lane constants (the same in every warp): warp 0 writes them
-  if (warp == 0) {
-    uint32_t *rec = S.rec[lane];
-    const int hb = g >> 1, pb = g & 1;
-#pragma unroll
-    for (int r = 0; r < 18; ++r) {
-      float lo = 0.f, hi = 0.f;
-      if (hb < G) {
-        if (ktab(r, 1) >= 0) lo = ldexpf(__half2float(qb[hb * kDim + 32 * tig + ktab(r, 1)]), 7 - ktab(r, 2) - kq);
-        if (ktab(r, 3) >= 0) hi = ldexpf(__half2float(qb[hb * kDim + 32 * tig + ktab(r, 3)]), 7 - ktab(r, 4) - kq);
-      }
-      __half2 s2 = __floats2half2_rn(lo, hi);
-      const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
-      rec[r] = pb ? su ^ 0x80008000u : su;  // hi lanes: q; lo lanes: -q
-      rec[20 + r] = pb ? su : 0u;           // lo lanes: q; hi lanes: 0
-    }
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t a0 = 0u, a2 = 0u;
-      if (g < G) {
-        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qb + g * kDim + 32 * tig + 4 * ks);
-        a0 = qw[0];
-        a2 = qw[1];
-      }
-      rec[40 + 2 * ks] = a0;
-      rec[41 + 2 * ks] = a2;
-    }
-  }
-  __syncthreads();
-
-  const int njw = nloc > warp ? (nloc - 1 - warp) / kWarps + 1 : 0;  // this warp's blocks
-  auto issue = [&](int j) {
-    const int i = blk0 + warp + kWarps * j;
+  // Block li of the chunk goes to warp li % 4 and stage li % kRing; the warp that
+  // finishes block li starts the copy of block li + kRing into the stage it frees, so a
+  // stage is only ever refilled by its last reader.
+  auto issue = [&](int li) {
+    const int i = blk0 + li;
     const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
     const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
-    SStage &sg = S.u.stage[warp][j & 1];
-    uint64_t *bar = &S.full[warp][j & 1];
+    SStage &sg = S.u.stage[li % kRing];
+    uint64_t *bar = &S.full[li % kRing][(li / kRing) & 1];
+    S.nissued[li % kRing][(li / kRing) & 1] += 1;
     mbar_expect_tx(bar, sizeof(SStage));
     bulk_g2s(sg.kc, a.kc + bi * kCB, kCB, bar);
     bulk_g2s(sg.vc, a.vc + bi * kCB, kCB, bar);
@@ -826,11 +786,74 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
     bulk_g2s(sg.ka, a.ka + bi * kBlock, kBlock * 4, bar);
     bulk_g2s(sg.va, a.va + bi * kBlock, kBlock * 4, bar);
   };
-  if (lane == 0)
-    for (int j = 0; j < kRing && j < njw; ++j) issue(j);
-  __syncwarp();
+  // thread 0 initialises the ring and starts the first copies before anything else
+  if (tid == 0) {
+    S.failed = 0;
+#pragma unroll
+    for (int s = 0; s < kRing; ++s)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        mbar_init(&S.full[s][x], 1);
+        S.nissued[s][x] = 0;
+      }
+    fence_mbar_init();
+    for (int li = 0; li < kRing && li < nloc; ++li) issue(li);
+  }
 
-  const float c1 = ldexpf(kScale, 17 + kq), c2 = kScale;
+  // ---- per-head q exponent kq_h: |q_h| < 2^(8 + kq_h), so q * 2^(7 - pos - kq_h) is a finite fp16
+  // (each MMA column is one head, so the shift may differ per head); every warp computes all four
+  int kqh[4];
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) {
+    float mx = 0.f;
+    if (hh < G) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(qb + hh * kDim + 4 * lane);
+      const float2 x0 = Elem<__half>::to_f2(u.x), x1 = Elem<__half>::to_f2(u.y);
+      mx = fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x1.x), fabsf(x1.y)));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int e = ((__float_as_int(mx) >> 23) & 0xff) - 126;  // mx < 2^e (frexp exponent)
+    kqh[hh] = e > 8 ? e - 8 : 0;
+  }
+  auto pick = [&](int hh) { return hh == 0 ? kqh[0] : hh == 1 ? kqh[1] : hh == 2 ? kqh[2] : kqh[3]; };
+  auto pow2 = [](int e) { return __int_as_float((127 + e) << 23); };  // 2^e, -126 <= e <= 127
+
+  // ---- per-lane constant records (the same in every warp), each warp writing a quarter
+  {
+    uint32_t *rec = S.rec[lane];
+    const int hb = g >> 1, pb = g & 1;
+    const int kb = pick(hb);
+#pragma unroll
+    for (int r = 0; r < 18; ++r) {
+      if ((r & 3) != warp) continue;
+      float lo = 0.f, hi = 0.f;
+      if (hb < G) {
+        if (ktab(r, 1) >= 0) lo = __half2float(qb[hb * kDim + 32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
+        if (ktab(r, 3) >= 0) hi = __half2float(qb[hb * kDim + 32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
+      }
+      __half2 s2 = __floats2half2_rn(lo, hi);
+      const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
+      rec[r] = pb ? su ^ 0x80008000u : su;  // hi lanes: q; lo lanes: -q
+      rec[20 + r] = pb ? su : 0u;           // lo lanes: q; hi lanes: 0
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      if (((ks + 2) & 3) != warp) continue;
+      uint32_t a0 = 0u, a2 = 0u;
+      if (g < G) {
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qb + g * kDim + 32 * tig + 4 * ks);
+        a0 = qw[0];
+        a2 = qw[1];
+      }
+      rec[40 + 2 * ks] = a0;
+      rec[41 + 2 * ks] = a2;
+    }
+  }
+  __syncthreads();  // records written; the ring initialised before any wait
+  const int kq = pick(tig);
+
+  const float c1 = kScale * pow2(17 + kq), c2 = kScale;
   const int vword = (3 * g - (g & 1)) >> 1;  // first word holding this lane's V field
   const uint32_t selL = (g & 1) ? 0x5432u : 0x3210u, selH = (g & 1) ? 0x7654u : 0x5432u;
   const uint32_t *rec = S.rec[lane];
@@ -839,14 +862,14 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   int st = 0;
-  int jfail = -1;
 
-  for (int j = 0; j < njw; ++j) {
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&S.full[warp][j & 1], (j >> 1) & 1, a.status))) {
-      jfail = j;
+  for (int li = warp; li < nloc; li += kWarps) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&S.full[li % kRing][(li / kRing) & 1], (li / (2 * kRing)) & 1,
+                                                   a.status))) {
+      if (lane == 0) S.failed = 1;
       break;
     }
-    const SStage &sg = S.u.stage[warp][j & 1];
+    const SStage &sg = S.u.stage[li % kRing];
 
     // ---- K weights of this block: W[r] = hi (even g) or lo (odd g) of q * scale * 2^(7-pos-kq)
     uint32_t W[18];
@@ -891,29 +914,33 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
     }
     const float dlt = __shfl_sync(0xffffffffu, dd[0], 4 * tig) * c2;
 
-    // ---- K: scores of tokens 16m+g and 16m+g+8 for head tig
+    // ---- K: scores of tokens 16m+g and 16m+g+8 for head tig (two m-tiles at a time)
     float sc[4][4];
     {
       const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
-      uint32_t X0[4][6], X1[4][6];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
-        const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
-        X0[m][0] = u0, X0[m][1] = __funnelshift_r(u0, u1, 8), X0[m][2] = u1;
-        X0[m][3] = __funnelshift_r(u1, u2, 8), X0[m][4] = u2, X0[m][5] = u2 >> 8;
-        X1[m][0] = v0, X1[m][1] = __funnelshift_r(v0, v1, 8), X1[m][2] = v1;
-        X1[m][3] = __funnelshift_r(v1, v2, 8), X1[m][4] = v2, X1[m][5] = v2 >> 8;
-        sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
-      }
+      for (int half = 0; half < 2; ++half) {
+        uint32_t X0[2][6], X1[2][6];
 #pragma unroll
-      for (int k = 0; k < 9; ++k)
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int r0 = 2 * k, r1 = 2 * k + 1;
-          mma16816<__half>(sc[m], X0[m][ktab(r0, 0)] & kmask(r0), X1[m][ktab(r0, 0)] & kmask(r0),
-                           X0[m][ktab(r1, 0)] & kmask(r1), X1[m][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+        for (int mm = 0; mm < 2; ++mm) {
+          const int m = 2 * half + mm;
+          const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
+          const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
+          X0[mm][0] = u0, X0[mm][1] = __funnelshift_r(u0, u1, 8), X0[mm][2] = u1;
+          X0[mm][3] = __funnelshift_r(u1, u2, 8), X0[mm][4] = u2, X0[mm][5] = u2 >> 8;
+          X1[mm][0] = v0, X1[mm][1] = __funnelshift_r(v0, v1, 8), X1[mm][2] = v1;
+          X1[mm][3] = __funnelshift_r(v1, v2, 8), X1[mm][4] = v2, X1[mm][5] = v2 >> 8;
+          sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
         }
+#pragma unroll
+        for (int k = 0; k < 9; ++k)
+#pragma unroll
+          for (int mm = 0; mm < 2; ++mm) {
+            const int r0 = 2 * k, r1 = 2 * k + 1;
+            mma16816<__half>(sc[2 * half + mm], X0[mm][ktab(r0, 0)] & kmask(r0), X1[mm][ktab(r0, 0)] & kmask(r0),
+                             X0[mm][ktab(r1, 0)] & kmask(r1), X1[mm][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+          }
+      }
     }
     float s[4][2];
     float bm = -INFINITY;
@@ -943,11 +970,8 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
         PB[m][i] = movtrans(split_hilo(pv));
       }
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      psum += __shfl_xor_sync(0xffffffffu, psum, o);
-      wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
-    }
-    l_run = l_run * r + psum;
+    for (int o = 4; o < 32; o <<= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+    l_run = l_run * r + psum;  // this lane's tokens only: the head's sum is formed at the end
     m_run = m_new;
     if (!__all_sync(0xffffffffu, r == 1.f)) {
 #pragma unroll
@@ -1001,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
       const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
       float wp[8];
 #pragma unroll
-      for (int p = 0; p < 8; ++p) wp[p] = wsum * ldexpf(1.f, p - 24);
+      for (int p = 0; p < 8; ++p) wp[p] = wsum * pow2(p - 24);
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         const float2 bs = Elem<__half>::to_f2(sw[mt]), ms = Elem<__half>::to_f2(nw[mt]);
@@ -1012,13 +1036,17 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
       }
     }
     __syncwarp();
-    if (lane == 0 && j + kRing < njw) issue(j + kRing);
+    if (lane == 0 && li + kRing < nloc) issue(li + kRing);
   }
-  if (jfail >= 0 && lane == 0)  // give the copies still in flight a bounded chance to land
-    for (int jj = jfail + 1; jj < njw && jj < jfail + kRing; ++jj)
-      mbar_wait_bounded(&S.full[warp][jj & 1], (jj >> 1) & 1, a.status);
+  __syncthreads();
+  if (S.failed && tid == 0)  // a copy never landed: give every started copy a bounded chance to finish
+    for (int s = 0; s < kRing; ++s)
+      for (int x = 0; x < 2; ++x)
+        if (S.nissued[s][x] > 0) mbar_wait_bounded(&S.full[s][x], (S.nissued[s][x] - 1) & 1, a.status);
 
   // ---- combine the four warps and write this chunk's partial
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
   __syncthreads();
   MergeSmem &M = S.u.merge;
   if (tig < G) {
@@ -1029,8 +1057,8 @@ __global__ void __launch_bounds__(kThreads, 3) attn_sealed3_kernel(const AttnArg
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int c = 16 * g + 2 * mt;
-      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * ldexpf(1.f, 24 - vpos(2 * mt));
-      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * ldexpf(1.f, 24 - vpos(2 * mt + 1));
+      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * pow2(24 - vpos(2 * mt));
+      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * pow2(24 - vpos(2 * mt + 1));
     }
   }
   __syncthreads();
@@ -1067,6 +1095,19 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   ch = (ch + 3) / 4 * 4;  // whole rounds of the sealed kernel's four warps
   if (ch < 4) ch = 4;
   if (ch > 16) ch = 16;
+  return static_cast<int>(ch);
+}
+
+// The sealed INT3 kernel's chunks: the same target, up to 32 blocks.
+static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail) {
+  const int64_t units = batch * h;
+  const int64_t target = 148 * 12;
+  const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
+  const int64_t per_unit = (target + units - 1) / units;
+  int64_t ch = (work + per_unit - 1) / per_unit;
+  ch = (ch + 3) / 4 * 4;
+  if (ch < 4) ch = 4;
+  if (ch > 32) ch = 32;
   return static_cast<int>(ch);
 }
 
@@ -1185,13 +1226,18 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
     const size_t smem = sizeof(s3::SSmem);
     if (cudaFuncSetAttribute(attn_sealed3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return NSNKV_ERR_CUDA;
+    // whole chunks of up to 32 blocks (8 per warp) amortise the per-CTA set-up; fewer chunks
+    // than nsnkv_decode_attn_workspace_bytes() sized for, so the same workspace holds them
+    a.chunk_blocks = s3_chunk_blocks(batch, h, max_blocks, max_tail);
+    a.max_chunks = max_chunks_for(max_blocks, max_tail, a.chunk_blocks);
+    a.part_ml = a.part_o + batch * hq * static_cast<int64_t>(a.max_chunks) * kDim;
+    // sealed chunks here, native-row chunks on attn_partial_kernel, then the merge kernel
     const int sealed_chunks = (max_blocks + a.chunk_blocks - 1) / a.chunk_blocks;
     attn_sealed3_kernel<<<dim3(sealed_chunks, h, static_cast<unsigned>(batch)), kThreads, smem, st>>>(a);
     if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
     if (any_tail) {
       a.raw_only = 1;
-      const int raw_chunks = a.max_chunks - sealed_chunks;
-      rc = launch_attn<3, __half>(a, dim3(raw_chunks, h, static_cast<unsigned>(batch)), st);
+      rc = launch_attn<3, __half>(a, dim3(a.max_chunks - sealed_chunks, h, static_cast<unsigned>(batch)), st);
     }
   } else {
     dim3 grid(a.max_chunks, h, static_cast<unsigned>(batch));
