@@ -114,23 +114,31 @@ def sequence_from_bytes(blob: bytes, device="cpu"):
 
 class PagedKVCache:
     def __init__(self, batch: int, h: int, max_blocks: int, bits: int = 3, dtype=torch.float16, device="cuda",
-                 hq: int | None = None):
+                 hq: int | None = None, bridge_rounding: bool = False):
+        """``bridge_rounding=True`` attends through the restore kernel, which rounds every
+        restored K/V row to the cache dtype exactly as the reference bridge
+        (restore_group + SDPA) does.  The default keeps per-token renorm factors and, for
+        INT3 fp16 caches with hq / h <= 4, attends over the codes directly on the tensor
+        cores: the exact fp32 restore, with no rounding of restored rows."""
         w.require(batch > 0 and h > 0 and max_blocks > 0 and bits in (3, 4, 5), "paged cache shape")
         w.require(dtype in (torch.float16, torch.bfloat16), "paged cache dtype")
         L.require_cuda()
         self.batch, self.h, self.max_blocks, self.bits, self.dtype = batch, h, max_blocks, bits, dtype
         self.hq = hq or h
+        self.bridge_rounding = bridge_rounding
         self.device = torch.device(device)
         self.pages = batch * max_blocks
         cb = w.code_bytes(bits)
         dev = self.device
 
         def pool():
-            return dict(codes=torch.zeros((h, self.pages, cb), dtype=torch.uint8, device=dev),
-                        norm=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float16, device=dev),
-                        min=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
-                        scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
-                        alpha=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float32, device=dev))
+            p = dict(codes=torch.zeros((h, self.pages, cb), dtype=torch.uint8, device=dev),
+                     norm=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float16, device=dev),
+                     min=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
+                     scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev))
+            if not bridge_rounding:
+                p["alpha"] = torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float32, device=dev)
+            return p
 
         self.k_pool, self.v_pool = pool(), pool()
         self.block_table = torch.arange(self.pages, dtype=torch.int32, device=dev).reshape(batch, max_blocks)
@@ -211,7 +219,8 @@ class PagedKVCache:
             pool["norm"][:, pages] = g["metas"][0].reshape(h, n, w.BLOCK).to(self.device)
             pool["min"][:, pages] = g["metas"][1].reshape(h, n, w.DIM).to(self.device)
             pool["scale"][:, pages] = g["metas"][2].reshape(h, n, w.DIM).to(self.device)
-            w.block_renorm(pool, self.bits, h, n, self.pages, b * self.max_blocks)
+            if "alpha" in pool:
+                w.block_renorm(pool, self.bits, h, n, self.pages, b * self.max_blocks)
         for src, pool, tail in ((kt, self.k_pool, self.k_tail), (vt, self.v_pool, self.v_tail)):
             src = src[0].to(self.device, self.dtype)
             if extra:
@@ -246,6 +255,17 @@ class PagedKVCache:
 
     def seal(self, pending_append: int = 1):
         lib = L.load()
+        if self.bridge_rounding:
+            rc = lib.nsnkv_seal_full_tails(
+                self.batch, self.h, self.bits, L.DTYPE_CODE[self.dtype], L.ptr(self.k_tail), L.ptr(self.v_tail),
+                self.h * w.BLOCK, w.BLOCK, L.ptr(self.tail_len), L.ptr(self.n_blocks), pending_append,
+                L.ptr(self.block_table), self.max_blocks,
+                L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
+                L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
+                L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), self.pages, 1, L.ptr(self.status),
+                L.stream_handle(self.device))
+            L.check(rc, "nsnkv_seal_full_tails")
+            return
         rc = lib.nsnkv_seal_full_tails_alpha(
             self.batch, self.h, self.bits, L.DTYPE_CODE[self.dtype], L.ptr(self.k_tail), L.ptr(self.v_tail),
             self.h * w.BLOCK, w.BLOCK, L.ptr(self.tail_len), L.ptr(self.n_blocks), pending_append,
@@ -277,7 +297,8 @@ class PagedKVCache:
 
     def uses_alpha_path(self):
         """True when attend() runs the sealed blocks through the renorm-factor kernel."""
-        return self.bits == 3 and self.dtype == torch.float16 and self.hq // self.h <= 4
+        return (not self.bridge_rounding and self.bits == 3 and self.dtype == torch.float16
+                and self.hq // self.h <= 4)
 
     def read_bytes_per_step(self):
         """Algorithmic bytes one attend() reads: sealed blocks (codes + metadata) and tails, q and out.

@@ -20,6 +20,18 @@ pytestmark = pytest.mark.gpu
 TIGHT = (1e-4, 2e-5)  # (rtol, atol) against the exact fp32 restore: fp32 accumulation only
 
 
+def mma_bar(q, k, v):
+    """Extra absolute bar for the tensor-core dot products over codes.
+
+    The codes enter mma.sync as fp16 subnormals, for which the tensor core keeps about
+    2^-18.5 of sum |products| per k-group (a B200 probe; normal fp16 operands keep 2^-23).
+    A logit therefore carries up to ~2^-16 * sum_c |q_c k_c| / sqrt(128), and the output
+    moves by at most that times max |v|.  With 1/sqrt(128)-scaled queries this is ~1e-5."""
+    rep = q.shape[0] // k.shape[0]
+    sabs = np.einsum("jd,jtd->jt", np.abs(q), np.abs(np.repeat(k, rep, 0))).max() / np.sqrt(128.0)
+    return 2.0 ** -16 * sabs * np.abs(v).max()
+
+
 def exact_restore(q8, n16, m16, s16):
     """nsn_decode (loop_kv_nb06_primitives.py:57-66) in fp64, without the cast to fp16."""
     d = m16.astype(np.float64) + s16.astype(np.float64) * q8.astype(np.float64)
@@ -58,12 +70,13 @@ def history_oracle(hk, hv, nb, rows="exact"):
     return np.concatenate(parts_k, 1), np.concatenate(parts_v, 1)
 
 
-def make_cache(rng, lens, h, hq, max_blocks, q_scale=1.0):
+def make_cache(rng, lens, h, hq, max_blocks, q_scale=1.0, bridge_rounding=False):
     from nsn_b200 import workloads
     from nsn_b200.paged import PagedKVCache
     hk = [workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5) for L in lens]
     hv = [workloads.np_kv(rng, (h, L, 128), (), 0.5) for L in lens]
-    cache = PagedKVCache(len(lens), h, max_blocks=max_blocks, bits=3, dtype=torch.float16, hq=hq)
+    cache = PagedKVCache(len(lens), h, max_blocks=max_blocks, bits=3, dtype=torch.float16, hq=hq,
+                         bridge_rounding=bridge_rounding)
     for b in range(len(lens)):
         cache.prefill(b, torch.from_numpy(hk[b]).cuda(), torch.from_numpy(hv[b]).cuda())
     q = (rng.standard_normal((len(lens), hq, 128)) * q_scale / np.sqrt(128)).astype(np.float16)
@@ -109,21 +122,20 @@ def test_alpha_path_tight_against_exact_restore(h, hq):
     for b, L in enumerate(lens):
         nb = L // 64
         k, v = history_oracle(hk[b], hv[b], nb, "exact")
-        want = attention64(q[b].astype(np.float64), k, v)
-        ok, err = O.within_tolerance(got32[b], want, *TIGHT)
+        q64 = q[b].astype(np.float64)
+        want = attention64(q64, k, v)
+        ok, err = O.within_tolerance(got32[b], want, TIGHT[0], TIGHT[1] + mma_bar(q64, k, v))
         assert ok, (b, L, err)
         kb, vb = history_oracle(hk[b], hv[b], nb, "bridge")
         ok, err = O.within_tolerance(got16[b], attention64(q[b].astype(np.float64), kb, vb), *O.TOLERANCE["float16"])
         assert ok, (b, L, err)
 
 
-@pytest.mark.parametrize("q_scale", [1e-3, 300.0, 4000.0])
+@pytest.mark.parametrize("q_scale", [1e-3, float(np.sqrt(128)), 300.0, 4000.0])
 def test_alpha_path_q_magnitudes(q_scale):
     """q far from unit scale: tiny values and values whose q * 2^7 leaves the fp16 range.
 
-    fp32 carries a logit s to about 2^-24 |s|, so an exact fp32 computation already
-    moves the output by ~1e-7 |s| per unit of value spread; the bar adds 1e-6 * max |s|
-    (q x 300 gives logits near 10^3)."""
+    The bar adds the tensor-core bound of mma_bar, which grows with |q|."""
     rng = np.random.default_rng(7)
     lens = [64 * 12 + 5, 64 * 4]
     cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=13, q_scale=q_scale)
@@ -134,9 +146,9 @@ def test_alpha_path_q_magnitudes(q_scale):
         k, v = history_oracle(hk[b], hv[b], L // 64, "exact")
         q64 = q[b].astype(np.float64)
         want = attention64(q64, k, v)
-        logit = np.abs(np.einsum("jd,jtd->jt", q64, np.repeat(k, 4, 0))).max() / np.sqrt(128.0)
-        ok, err = O.within_tolerance(out32[b].cpu().numpy(), want, TIGHT[0], TIGHT[1] + 1e-6 * logit)
-        assert ok, (q_scale, b, err, logit)
+        bar = mma_bar(q64, k, v)
+        ok, err = O.within_tolerance(out32[b].cpu().numpy(), want, TIGHT[0], TIGHT[1] + bar)
+        assert ok, (q_scale, b, err, bar)
 
 
 def test_alpha_path_zero_and_constant_blocks():
@@ -157,7 +169,9 @@ def test_alpha_path_zero_and_constant_blocks():
     cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
     cache.check()
     k, v = history_oracle(hk, hv, L // 64, "exact")
-    ok, err = O.within_tolerance(out32[0].cpu().numpy(), attention64(q[0].astype(np.float64), k, v), *TIGHT)
+    q64 = q[0].astype(np.float64)
+    ok, err = O.within_tolerance(out32[0].cpu().numpy(), attention64(q64, k, v), TIGHT[0],
+                                 TIGHT[1] + mma_bar(q64, k, v))
     assert ok, err
 
 
@@ -205,3 +219,31 @@ def test_seal_writes_renorm_factors():
         for b in range(3):
             pages = cache.block_table[b, :nb[b]].long()
             assert torch.equal(sealed[:, pages], pool["alpha"][:, pages]), b
+
+
+def test_bridge_rounding_option_matches_bridge_on_unscaled_queries():
+    """cfg0-style queries (N(0,1), not scaled by 1/sqrt(128)): the bridge's fp16 rounding of
+    restored rows alone moves outputs past the parity bar, so a cache built with
+    bridge_rounding=True (restore kernel, rows rounded like restore_group) is the one that
+    matches the bridge there; the default path matches the exact restore."""
+    rng = np.random.default_rng(9)
+    lens = [64 * 15 + 3, 64 * 8]
+    for bridge in (True, False):
+        r = np.random.default_rng(9)
+        cache, hk, hv, q = make_cache(r, lens, 2, 8, max_blocks=16, q_scale=float(np.sqrt(128)),
+                                      bridge_rounding=bridge)
+        assert cache.uses_alpha_path() == (not bridge)
+        out32 = torch.empty((len(lens), 8, 128), dtype=torch.float32, device="cuda")
+        out = cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
+        cache.check()
+        for b, L in enumerate(lens):
+            q64 = q[b].astype(np.float64)
+            if bridge:
+                kb, vb = history_oracle(hk[b], hv[b], L // 64, "bridge")
+                ok, err = O.within_tolerance(out[b].float().cpu().numpy(), attention64(q64, kb, vb),
+                                             *O.TOLERANCE["float16"])
+            else:
+                k, v = history_oracle(hk[b], hv[b], L // 64, "exact")
+                ok, err = O.within_tolerance(out32[b].cpu().numpy(), attention64(q64, k, v), TIGHT[0],
+                                             TIGHT[1] + mma_bar(q64, k, v))
+            assert ok, (bridge, b, err)
