@@ -230,15 +230,21 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
                           int64_t blk_stride_head, int64_t blk_stride_page,
                           int32_t *status, void *stream);
 
-/* nsnkv_seal_full_tails that also writes the sealed blocks' renorm factors (k_alpha / v_alpha, fp32 [64] per block). */
+/*
+ * nsnkv_seal_full_tails that also writes the sealed blocks' renorm factors
+ * (k_alpha / v_alpha, fp32 [64] per block) in the same kernel.  seq_counters
+ * (int32 [batch], may be NULL) must be zero before the first call and are left zero:
+ * with them the last CTA of each sequence advances n_blocks / tail_len, so the call is
+ * one launch; without them a second kernel advances the counters.
+ */
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
                                 int32_t *tail_len, int32_t *n_blocks, int pending_append,
                                 const int32_t *block_table, int64_t table_stride,
                                 uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                 uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
-                                float *k_alpha, float *v_alpha, int64_t blk_stride_head, int64_t blk_stride_page,
-                                int32_t *status, void *stream);
+                                float *k_alpha, float *v_alpha, int32_t *seq_counters,
+                                int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream);
 
 /*
  * Combine per-shard attention partials (one row per shard) into the final

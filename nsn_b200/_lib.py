@@ -68,7 +68,7 @@ SIGNATURES = [
     ("nsnkv_seal_full_tails", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P, c_int64,
                                       P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_seal_full_tails_alpha", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P,
-                                            c_int64, P, P, P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
+                                            c_int64, P, P, P, P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),

@@ -540,41 +540,62 @@ __global__ void unpack_kernel(const uint8_t *payload, int64_t count, int bits, u
 }
 
 // ----------------------------------------------------------------- paged-cache seal
-// One CTA per (kv head, K|V, sequence).  A sequence whose tail holds 64 tokens
-// has that tail encoded into its next page; nothing else is touched here.
+template <int BITS>
+__device__ void renorm_block(const uint8_t *codes, const uint16_t *norm, const uint16_t *mn, const uint16_t *sc,
+                             float *alpha);
+
+// One CTA per (kv head, K|V, sequence).  A sequence whose tail holds 64 tokens has that
+// tail encoded into its next page, and with k_alpha the page's renorm factors written
+// by the same CTA.  With `done` (per-sequence counters, zero between calls) the CTA that
+// finishes a sequence last also advances its n_blocks / tail_len and resets the counter,
+// so no separate counter kernel runs; every CTA reads the counters before it counts.
 template <typename T, int BITS>
 __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_tail, int64_t tss, int64_t tsh,
-                                                   const int32_t *tail_len, const int32_t *n_blocks, int pending,
+                                                   int32_t *tail_len, int32_t *n_blocks, int pending,
                                                    const int32_t *table, int64_t table_stride, uint8_t *k_codes,
                                                    uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                                    uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                                                   uint16_t *v_scale, int64_t sh, int64_t sp, int32_t *status) {
+                                                   uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done,
+                                                   int64_t sh, int64_t sp, int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
   const int h = blockIdx.x, kv = blockIdx.y;
   const int64_t b = blockIdx.z;
-  if (tail_len[b] + pending < kBlock) return;
-  const int32_t page = table[b * table_stride + n_blocks[b]];
-  const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
-  const T *src = (kv == 0 ? k_tail : v_tail) + (b * tss + h * tsh) * kDim;
-  if constexpr (std::is_same<T, __half>::value) {
-    FastSmem &f = *reinterpret_cast<FastSmem *>(smem_raw);
-    if (kv == 0)
-      encode_block_fast<BITS>(src, k_codes + blk * code_bytes(BITS), nullptr, k_norm + blk * kBlock,
-                              k_min + blk * kDim, k_scale + blk * kDim, status, f);
-    else
-      encode_block_fast<BITS>(src, v_codes + blk * code_bytes(BITS), nullptr, v_norm + blk * kBlock,
-                              v_min + blk * kDim, v_scale + blk * kDim, status, f);
-    return;
+  const int32_t tl = tail_len[b], nbk = n_blocks[b];
+  const bool full = tl + pending >= kBlock;
+  if (!full && !done) return;
+  if (full) {
+    const int32_t page = table[b * table_stride + nbk];
+    const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
+    const T *src = (kv == 0 ? k_tail : v_tail) + (b * tss + h * tsh) * kDim;
+    uint8_t *codes = (kv == 0 ? k_codes : v_codes) + blk * code_bytes(BITS);
+    uint16_t *nrm = (kv == 0 ? k_norm : v_norm) + blk * kBlock;
+    uint16_t *mn = (kv == 0 ? k_min : v_min) + blk * kDim;
+    uint16_t *sc = (kv == 0 ? k_scale : v_scale) + blk * kDim;
+    if constexpr (std::is_same<T, __half>::value) {
+      encode_block_fast<BITS>(src, codes, nullptr, nrm, mn, sc, status, *reinterpret_cast<FastSmem *>(smem_raw));
+    } else {
+      BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
+      int st = load_block<T>(src, s);
+      __syncthreads();
+      encode_in_smem<BITS>(s, 0, codes, nullptr, nrm, mn, sc, status, st);
+    }
+    if (k_alpha) {
+      __syncthreads();  // this CTA's code and metadata stores are visible to all its threads
+      renorm_block<BITS>(codes, nrm, mn, sc, (kv == 0 ? k_alpha : v_alpha) + blk * kBlock);
+    }
   }
-  int st = load_block<T>(src, s);
-  __syncthreads();
-  if (kv == 0)
-    encode_in_smem<BITS>(s, 0, k_codes + blk * code_bytes(BITS), nullptr, k_norm + blk * kBlock, k_min + blk * kDim,
-                         k_scale + blk * kDim, status, st);
-  else
-    encode_in_smem<BITS>(s, 0, v_codes + blk * code_bytes(BITS), nullptr, v_norm + blk * kBlock, v_min + blk * kDim,
-                         v_scale + blk * kDim, status, st);
+  if (done) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int per_seq = static_cast<int>(gridDim.x * gridDim.y);
+      if (atomicAdd(&done[b], 1) == per_seq - 1) {
+        n_blocks[b] = nbk + (full ? 1 : 0);
+        tail_len[b] = tl + pending - (full ? kBlock : 0);
+        done[b] = 0;
+      }
+    }
+  }
 }
 
 __global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_blocks, int pending) {
@@ -628,28 +649,6 @@ __global__ void __launch_bounds__(256) renorm_blocks_kernel(const uint8_t *codes
   const int64_t blk = r * row_stride + offset + i;
   renorm_block<BITS>(codes + blk * code_bytes(BITS), norm + blk * kBlock, mn + blk * kDim, sc + blk * kDim,
                      alpha + blk * kBlock);
-}
-
-// The blocks seal_kernel writes in the same step (same predicate and page).
-template <int BITS>
-__global__ void __launch_bounds__(256) renorm_seal_kernel(const int32_t *tail_len, const int32_t *n_blocks,
-                                                          int pending, const int32_t *table, int64_t table_stride,
-                                                          const uint8_t *k_codes, const uint16_t *k_norm,
-                                                          const uint16_t *k_min, const uint16_t *k_scale,
-                                                          const uint8_t *v_codes, const uint16_t *v_norm,
-                                                          const uint16_t *v_min, const uint16_t *v_scale,
-                                                          float *k_alpha, float *v_alpha, int64_t sh, int64_t sp) {
-  const int h = blockIdx.x, kv = blockIdx.y;
-  const int64_t b = blockIdx.z;
-  if (tail_len[b] + pending < kBlock) return;
-  const int32_t page = table[b * table_stride + n_blocks[b]];
-  const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
-  if (kv == 0)
-    renorm_block<BITS>(k_codes + blk * code_bytes(BITS), k_norm + blk * kBlock, k_min + blk * kDim,
-                       k_scale + blk * kDim, k_alpha + blk * kBlock);
-  else
-    renorm_block<BITS>(v_codes + blk * code_bytes(BITS), v_norm + blk * kBlock, v_min + blk * kDim,
-                       v_scale + blk * kDim, v_alpha + blk * kBlock);
 }
 
 // ----------------------------------------------------------------- host dispatch
@@ -741,8 +740,8 @@ template <typename T>
 static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tail, int64_t tss, int64_t tsh,
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
-                       uint16_t *vm, uint16_t *vs, float *ka, float *va, int64_t sh, int64_t sp, int32_t *status,
-                       cudaStream_t st) {
+                       uint16_t *vm, uint16_t *vs, float *ka, float *va, int32_t *done, int64_t sh, int64_t sp,
+                       int32_t *status, cudaStream_t st) {
   const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
@@ -751,11 +750,8 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
       return NSNKV_ERR_CUDA;                                                                               \
     k<<<grid, 256, smem, st>>>(static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss, tsh,   \
-                               tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, sh, \
-                               sp, status);                                                                \
-    if (ka)                                                                                                \
-      renorm_seal_kernel<B><<<grid, 256, 0, st>>>(tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, \
-                                                  vn, vm, vs, ka, va, sh, sp);                             \
+                               tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
+                               va, done, sh, sp, status);                                                  \
     break;                                                                                                 \
   }
   switch (bits) {
@@ -766,7 +762,8 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
       return NSNKV_ERR_ARG;
   }
 #undef NSNKV_SEAL
-  seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending);
+  if (!done)
+    seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
@@ -854,7 +851,7 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
                      int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks, int pending_append,
                      const int32_t *block_table, int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm,
                      uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_stride_head,
+                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done, int64_t blk_stride_head,
                      int64_t blk_stride_page, int32_t *status, void *stream) {
   if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
   if (batch == 0) return NSNKV_OK;
@@ -868,13 +865,13 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
     case NSNKV_F16:
       return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
                                  n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
-                                 k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, blk_stride_head,
+                                 k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, done, blk_stride_head,
                                  blk_stride_page, status, st);
     case NSNKV_BF16:
       return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                                         tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
                                         k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha,
-                                        blk_stride_head, blk_stride_page, status, st);
+                                        done, blk_stride_head, blk_stride_page, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -888,7 +885,7 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tai
                           int32_t *status, void *stream) {
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, nullptr, nullptr, blk_stride_head, blk_stride_page, status, stream);
+                   v_min, v_scale, nullptr, nullptr, nullptr, blk_stride_head, blk_stride_page, status, stream);
 }
 
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
@@ -896,12 +893,12 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void 
                                 int32_t *n_blocks, int pending_append, const int32_t *block_table,
                                 int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min,
                                 uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_stride_head,
-                                int64_t blk_stride_page, int32_t *status, void *stream) {
+                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *seq_counters,
+                                int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream) {
   if (!k_alpha || !v_alpha) return NSNKV_ERR_ARG;
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, k_alpha, v_alpha, blk_stride_head, blk_stride_page, status, stream);
+                   v_min, v_scale, k_alpha, v_alpha, seq_counters, blk_stride_head, blk_stride_page, status, stream);
 }
 
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,

@@ -147,6 +147,7 @@ class PagedKVCache:
         self.k_tail = torch.zeros((batch, h, w.BLOCK, w.DIM), dtype=dtype, device=dev)
         self.v_tail = torch.zeros_like(self.k_tail)
         self.status = L.status_tensor(dev)
+        self.seal_counters = torch.zeros(batch, dtype=torch.int32, device=dev)  # left at zero by every seal
         self.out = torch.empty((batch, self.hq, w.DIM), dtype=dtype, device=dev)
         lib = L.load()
         self.ws = torch.empty(lib.nsnkv_decode_attn_workspace_bytes(batch, self.hq, h, max_blocks, w.BLOCK - 1),
@@ -273,7 +274,8 @@ class PagedKVCache:
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
             L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
-            L.ptr(self.v_pool["alpha"]), self.pages, 1, L.ptr(self.status), L.stream_handle(self.device))
+            L.ptr(self.v_pool["alpha"]), L.ptr(self.seal_counters), self.pages, 1, L.ptr(self.status),
+            L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, out=None):
