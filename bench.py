@@ -569,8 +569,8 @@ def main():
                          "bytes_per_launch": bytes_attn},
             "e2e": e2e,
             # attend: sealed kernel + tail kernel + merge (restore kernel + merge without the renorm
-            # path); seal: encode + renorm + counters (encode + counters without it)
-            "gpu_launches": (6 if cache.uses_alpha_path() else 4) * args.steps,
+            # path); seal: one launch (encode + renorm + counters), two without the renorm path
+            "gpu_launches": 4 * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

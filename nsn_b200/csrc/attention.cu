@@ -362,9 +362,8 @@ __device__ __forceinline__ void warp_softmax_pv(WarpState &ws, const float (&raw
 }
 
 template <int BITS, typename T>
-__global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
+__device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *smem_raw) {
   constexpr int CB = code_bytes(BITS);
-  extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS> &S = *reinterpret_cast<AttnSmem<BITS> *>(smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -585,6 +584,23 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
   if (st) set_status(a.status, st);
 }
 
+// Programmatic dependent launch (sm_90+).  launch_dependents lets the next grid in the
+// stream start once every CTA of this grid has issued it; wait returns once the grids
+// this one depends on have completed and their memory is visible (at once when there
+// are none).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The restore-path CTA.  Launched after attn_sealed3_kernel with a programmatic
+// dependency (native-row chunks only), it overlaps that kernel's last wave; the final
+// wait keeps this grid from completing before it, so the merge launched next sees both.
+template <int BITS, typename T>
+__global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  attn_partial_cta<BITS, T>(a, smem_raw);
+  pdl_wait();
+}
+
 // Combine the chunk partials of one (sequence, query head).
 template <typename T>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G, T *out, float *out_f32,
@@ -757,6 +773,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   SSmem &S = *reinterpret_cast<SSmem *>(smem_raw);
   constexpr float kLog2e = 1.4426950408889634f;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  pdl_launch_dependents();  // the native-row chunks (next grid) may fill this grid's last wave
   const int chunk = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int G = a.hq / a.h;
@@ -1116,13 +1133,29 @@ static int max_chunks_for(int32_t max_blocks, int32_t max_tail, int32_t ch) {
   return static_cast<int>((max_blocks + ch - 1) / ch + (raw + static_cast<int64_t>(ch) * kBlock - 1) / (static_cast<int64_t>(ch) * kBlock));
 }
 
+// after_sealed: launched with a programmatic dependency on the attn_sealed3_kernel grid
+// just before it in the stream.
 template <int BITS, typename T>
-static int launch_attn(const AttnArgs &a, dim3 grid, cudaStream_t st) {
+static int launch_attn(const AttnArgs &a, dim3 grid, cudaStream_t st, bool after_sealed = false) {
   auto k = attn_partial_kernel<BITS, T>;
   const size_t smem = sizeof(AttnSmem<BITS>);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return NSNKV_ERR_CUDA;
-  k<<<grid, kThreads, smem, st>>>(a);
+  if (!after_sealed) {
+    k<<<grid, kThreads, smem, st>>>(a);
+  } else {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
+  }
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
@@ -1235,9 +1268,9 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
     const int sealed_chunks = (max_blocks + a.chunk_blocks - 1) / a.chunk_blocks;
     attn_sealed3_kernel<<<dim3(sealed_chunks, h, static_cast<unsigned>(batch)), kThreads, smem, st>>>(a);
     if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
-    if (any_tail) {
+    if (any_tail) {  // native-row chunks, overlapping the sealed grid's last wave
       a.raw_only = 1;
-      rc = launch_attn<3, __half>(a, dim3(a.max_chunks - sealed_chunks, h, static_cast<unsigned>(batch)), st);
+      rc = launch_attn<3, __half>(a, dim3(a.max_chunks - sealed_chunks, h, static_cast<unsigned>(batch)), st, true);
     }
   } else {
     dim3 grid(a.max_chunks, h, static_cast<unsigned>(batch));
