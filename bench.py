@@ -46,9 +46,9 @@ def peaks():
     return HBM_FALLBACK, "fallback"
 
 
-def traffic_for(bytes_attn):
+def traffic_for(bytes_attn, sealed3=True):
     """DRAM bytes per attention launch: the ncu capture's traffic/algorithmic ratio times this launch's bytes."""
-    p = ROOT / "profiles" / "attn_partial_cfg2_traffic.json"
+    p = ROOT / "profiles" / ("attn_sealed3_cfg2_traffic.json" if sealed3 else "attn_partial_cfg2_traffic.json")
     if not p.exists():
         return None
     d = json.loads(p.read_text())
@@ -563,9 +563,9 @@ def main():
                                     "+ attn_merge_kernel)") if cache.uses_alpha_path() else
                                    "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn),
-                         "traffic_note": "ncu dram read+write of attn_partial at one full-size bench launch "
-                                         "(profiles/attn_partial_cfg2.md), scaled to this launch's algorithmic bytes",
+                         "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn, cache.uses_alpha_path()),
+                         "traffic_note": "ncu dram read+write of the dominant kernel at one full-size bench launch "
+                                         "(profiles/attn_sealed3_cfg2.md), scaled to this launch's algorithmic bytes",
                          "bytes_per_launch": bytes_attn},
             "e2e": e2e,
             # attend: sealed kernel + tail kernel + merge (restore kernel + merge without the renorm
