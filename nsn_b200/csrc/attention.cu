@@ -597,6 +597,7 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 template <int BITS, typename T>
 __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
+  pdl_launch_dependents();  // the merge grid may be resident (and waiting) before this one ends
   attn_partial_cta<BITS, T>(a, smem_raw);
   pdl_wait();
 }
@@ -605,6 +606,8 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
 template <typename T>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G, T *out, float *out_f32,
                                                           float *lse) {
+  pdl_wait();  // launched with a programmatic dependency: the partials are complete only now
+  pdl_launch_dependents();
   const int hqi = blockIdx.x;
   const int64_t b = blockIdx.y;
   const int c = threadIdx.x;
@@ -773,6 +776,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   SSmem &S = *reinterpret_cast<SSmem *>(smem_raw);
   constexpr float kLog2e = 1.4426950408889634f;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  pdl_wait();               // launched with a programmatic dependency on the kernel before it
   pdl_launch_dependents();  // the native-row chunks (next grid) may fill this grid's last wave
   const int chunk = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -1266,7 +1270,19 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
     a.part_ml = a.part_o + batch * hq * static_cast<int64_t>(a.max_chunks) * kDim;
     // sealed chunks here, native-row chunks on attn_partial_kernel, then the merge kernel
     const int sealed_chunks = (max_blocks + a.chunk_blocks - 1) / a.chunk_blocks;
-    attn_sealed3_kernel<<<dim3(sealed_chunks, h, static_cast<unsigned>(batch)), kThreads, smem, st>>>(a);
+    {  // programmatic dependency on the kernel before it (it waits on entry)
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(sealed_chunks, h, static_cast<unsigned>(batch));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, attn_sealed3_kernel, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
+    }
     if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
     if (any_tail) {  // native-row chunks, overlapping the sealed grid's last wave
       a.raw_only = 1;
@@ -1278,12 +1294,24 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
                             : dispatch_bits<__nv_bfloat16>(bits, G, a, grid, st);
   }
   if (rc != NSNKV_OK) return rc;
-  dim3 mgrid(hq, static_cast<unsigned>(batch));
+  // the merge launches with a programmatic dependency on the kernel before it and waits
+  // for it on entry, so its launch overlaps that kernel's end
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(hq, static_cast<unsigned>(batch));
+  cfg.blockDim = dim3(kDim);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (dtype == NSNKV_F16)
-    attn_merge_kernel<__half><<<mgrid, kDim, 0, st>>>(a, G, static_cast<__half *>(out), out_f32, lse);
+    e = cudaLaunchKernelEx(&cfg, attn_merge_kernel<__half>, a, G, static_cast<__half *>(out), out_f32, lse);
   else
-    attn_merge_kernel<__nv_bfloat16><<<mgrid, kDim, 0, st>>>(a, G, static_cast<__nv_bfloat16 *>(out), out_f32, lse);
-  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+    e = cudaLaunchKernelEx(&cfg, attn_merge_kernel<__nv_bfloat16>, a, G, static_cast<__nv_bfloat16 *>(out), out_f32,
+                           lse);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 }  // namespace nsnkv
 

@@ -558,6 +558,10 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
                                                    uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done,
                                                    int64_t sh, int64_t sp, int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  // launched with a programmatic dependency: wait for the kernel before it, then let the
+  // next one (the following decode step) launch while this grid runs
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int h = blockIdx.x, kv = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int32_t tl = tail_len[b], nbk = n_blocks[b];
@@ -749,9 +753,20 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     auto k = seal_kernel<T, B>;                                                                            \
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
       return NSNKV_ERR_CUDA;                                                                               \
-    k<<<grid, 256, smem, st>>>(static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss, tsh,   \
-                               tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
-                               va, done, sh, sp, status);                                                  \
+    cudaLaunchConfig_t cfg{};                                                                              \
+    cfg.gridDim = grid;                                                                                    \
+    cfg.blockDim = dim3(256);                                                                              \
+    cfg.dynamicSmemBytes = smem;                                                                           \
+    cfg.stream = st;                                                                                       \
+    cudaLaunchAttribute attr[1];                                                                           \
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                       \
+    attr[0].val.programmaticStreamSerializationAllowed = 1;                                                \
+    cfg.attrs = attr;                                                                                      \
+    cfg.numAttrs = 1;                                                                                      \
+    if (cudaLaunchKernelEx(&cfg, k, static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss,   \
+                           tsh, tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
+                           va, done, sh, sp, status) != cudaSuccess)                                       \
+      return NSNKV_ERR_LAUNCH;                                                                             \
     break;                                                                                                 \
   }
   switch (bits) {
