@@ -970,7 +970,6 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       s[m][0] = sg.ka[16 * m + g] * fmaf(sc[m][0] + sc[m][1], c1, dlt);
       s[m][1] = sg.ka[16 * m + g + 8] * fmaf(sc[m][2] + sc[m][3], c1, dlt);
       bm = fmaxf(bm, fmaxf(s[m][0], s[m][1]));
-      if (tig < G && !(isfinite(s[m][0]) && isfinite(s[m][1]))) st |= NSNKV_ST_OUTPUT_NONFINITE;
     }
     bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
     bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
@@ -1068,6 +1067,9 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   // ---- combine the four warps and write this chunk's partial
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
+  // a non-finite score or weight leaves the running sum non-finite (checked once per chunk;
+  // the merge kernel also checks every output)
+  if (tig < G && !isfinite(l_run)) st |= NSNKV_ST_OUTPUT_NONFINITE;
   __syncthreads();
   MergeSmem &M = S.u.merge;
   if (tig < G) {

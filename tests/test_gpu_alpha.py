@@ -247,3 +247,21 @@ def test_bridge_rounding_option_matches_bridge_on_unscaled_queries():
                 ok, err = O.within_tolerance(out32[b].cpu().numpy(), attention64(q64, k, v), TIGHT[0],
                                              TIGHT[1] + mma_bar(q64, k, v))
             assert ok, (bridge, b, err)
+
+
+@pytest.mark.parametrize("where", ["k_scale_inf", "k_min_nan", "v_scale_inf", "v_min_nan", "alpha_nan"])
+def test_alpha_path_flags_nonfinite_metadata(where):
+    """A non-finite value in a sealed block's metadata surfaces as NumericalFailure from check()."""
+    from nsn_b200 import primitives as w
+    rng = np.random.default_rng(13)
+    cache, hk, hv, q = make_cache(rng, [64 * 6 + 7], 2, 8, max_blocks=8)
+    page = int(cache.block_table[0, 3])
+    pool, key, val = {"k_scale_inf": (cache.k_pool, "scale", float("inf")),
+                      "k_min_nan": (cache.k_pool, "min", float("nan")),
+                      "v_scale_inf": (cache.v_pool, "scale", float("inf")),
+                      "v_min_nan": (cache.v_pool, "min", float("nan")),
+                      "alpha_nan": (cache.v_pool, "alpha", float("nan"))}[where]
+    pool[key][1, page, 17] = val
+    cache.attend(torch.from_numpy(q).cuda())
+    with pytest.raises(w.NumericalFailure):
+        cache.check()
