@@ -756,6 +756,13 @@ __device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
+// 2^x for x <= 0 (softmax weights): one MUFU.EX2; results below 2^-126 flush to zero.
+__device__ __forceinline__ float ex2_neg(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -975,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
     bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
     const float m_new = fmaxf(m_run, bm);
-    const float r = m_run == -INFINITY ? 0.f : exp2f((m_run - m_new) * kLog2e);
+    const float r = m_run == -INFINITY ? 0.f : ex2_neg((m_run - m_new) * kLog2e);
     const float mb = m_new * kLog2e;
     float psum = 0.f, wsum = 0.f;
     uint32_t PB[4][2];
@@ -983,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     for (int m = 0; m < 4; ++m)
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const float p = exp2f(fmaf(s[m][i], kLog2e, -mb));
+        const float p = ex2_neg(fmaf(s[m][i], kLog2e, -mb));
         const float pv = p * sg.va[16 * m + g + 8 * i];
         psum += p;
         wsum += pv;
