@@ -617,15 +617,41 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G
   const int raw_per_chunk = a.chunk_blocks * kBlock;
   const int n_chunks = (nb + a.chunk_blocks - 1) / a.chunk_blocks + (tail_total + raw_per_chunk - 1) / raw_per_chunk;
   const int64_t row0 = (b * a.hq + hqi) * a.max_chunks;
-  float M = -INFINITY;
-  for (int i = 0; i < n_chunks; ++i) M = fmaxf(M, a.part_ml[(row0 + i) * 2]);
-  float L = 0.f, o = 0.f;
   constexpr float kLog2e = 1.4426950408889634f;
-  for (int i = 0; i < n_chunks; ++i) {
+  // The chunks' (m, l) are read once by the CTA (thread i takes chunk i, i + 128, ...)
+  // and their weights kept in shared memory; each thread then sums its channel over the
+  // chunks with independent loads.  Long single sequences have ~100 chunks per head.
+  constexpr int kMaxW = 512;
+  __shared__ float wgt[kMaxW];
+  __shared__ float red[2][4];
+  float M = -INFINITY;
+  for (int i = c; i < n_chunks; i += kDim) M = fmaxf(M, a.part_ml[(row0 + i) * 2]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if ((c & 31) == 0) red[0][c >> 5] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+  float L = 0.f;
+  for (int i = c; i < n_chunks; i += kDim) {
     const float m = a.part_ml[(row0 + i) * 2];
     const float w = m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e);
     L += w * a.part_ml[(row0 + i) * 2 + 1];
-    o += w * a.part_o[(row0 + i) * kDim + c];
+    if (i < kMaxW) wgt[i] = w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  if ((c & 31) == 0) red[1][c >> 5] = L;
+  __syncthreads();
+  L = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+  float o = 0.f;
+  if (n_chunks <= kMaxW) {
+#pragma unroll 8
+    for (int i = 0; i < n_chunks; ++i) o += wgt[i] * a.part_o[(row0 + i) * kDim + c];
+  } else {
+    for (int i = 0; i < n_chunks; ++i) {
+      const float m = a.part_ml[(row0 + i) * 2];
+      o += (m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e)) * a.part_o[(row0 + i) * kDim + c];
+    }
   }
   const float y = __fdiv_rn(o, L);
   const T yt = Elem<T>::from_f(y);
@@ -1128,10 +1154,11 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   return static_cast<int>(ch);
 }
 
-// The sealed INT3 kernel's chunks: the same target, up to 32 blocks.
+// The sealed INT3 kernel's chunks: about one CTA per resident slot (148 SMs x 4), in
+// multiples of 4 blocks (one round of its four warps), up to 32 blocks.
 static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail) {
   const int64_t units = batch * h;
-  const int64_t target = 148 * 12;
+  const int64_t target = 148 * 4;
   const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
   const int64_t per_unit = (target + units - 1) / units;
   int64_t ch = (work + per_unit - 1) / per_unit;
