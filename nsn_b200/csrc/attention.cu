@@ -713,6 +713,7 @@ namespace s3 {
 constexpr int kRing = 6;  // TMA stages per CTA: block li of a chunk lives in stage li % kRing
 constexpr int kRec = 60;  // words of a lane's constant record: stride 4 * odd -> conflict-free 128-bit loads
 constexpr int kCB = 3072;  // INT3 code bytes per block
+constexpr int kMaxChunk = 32;  // blocks per chunk (page indices staged in shared memory)
 
 struct SStage {
   uint8_t kc[kCB];
@@ -722,12 +723,19 @@ struct SStage {
 };
 static_assert(sizeof(SStage) == 7680, "stage layout");
 
+struct SMerge {
+  MergeSmem part;
+  float wt[kWarps][kHeads];  // exp(m_warp - m_chunk) per (warp, head)
+};
+
 struct SSmem {
   union {
     SStage stage[kRing];
-    MergeSmem merge;  // after the last block of every warp
+    SMerge merge;  // after the last block of every warp
   } u;
   uint32_t rec[32][kRec];  // per lane: [0,18) qa, [20,38) qz, [40,56) Delta A fragments
+  __half qs[4][kDim];  // this kv head's query rows (G <= 4)
+  int32_t pages[kMaxChunk];  // page of each block of the chunk
   // Block B completes on full[B % kRing][(B / kRing) & 1], parity (B / (2 kRing)) & 1.  Two
   // barriers per stage: warp B % 4 consumed block B - 2 kRing (the same barrier's previous
   // phase) before it waits for B, so a parity wait never meets a barrier two phases behind.
@@ -823,9 +831,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   // Block li of the chunk goes to warp li % 4 and stage li % kRing; the warp that
   // finishes block li starts the copy of block li + kRing into the stage it frees, so a
   // stage is only ever refilled by its last reader.
-  auto issue = [&](int li) {
-    const int i = blk0 + li;
-    const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
+  auto issue = [&](int li, int32_t page) {
     const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
     SStage &sg = S.u.stage[li % kRing];
     uint64_t *bar = &S.full[li % kRing][(li / kRing) & 1];
@@ -840,19 +846,35 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     bulk_g2s(sg.ka, a.ka + bi * kBlock, kBlock * 4, bar);
     bulk_g2s(sg.va, a.va + bi * kBlock, kBlock * 4, bar);
   };
-  // thread 0 initialises the ring and starts the first copies before anything else
-  if (tid == 0) {
-    S.failed = 0;
+  // One round of global loads starts the CTA: q (8 bytes per thread) and the chunk's page
+  // indices (warp 0, one coalesced load), staged in shared memory.  The copy issue never
+  // waits on a global load: each cp.async.bulk is ordered after the loads before it, and
+  // issuing one can itself stall on the TMA queue, so the first blocks are issued by every
+  // warp (block li by warp li % 4) once the pages are in shared memory.
+  uint2 qv = make_uint2(0u, 0u);
+  if (tid < G * kDim / 4) qv = reinterpret_cast<const uint2 *>(qb)[tid];
+  if (warp == 0) {
+    int32_t pg = 0;
+    if (lane < nloc) pg = a.table ? a.table[b * a.table_stride + blk0 + lane] : blk0 + lane;
+    S.pages[lane] = pg;
+    if (lane == 0) {
+      S.failed = 0;
 #pragma unroll
-    for (int s = 0; s < kRing; ++s)
+      for (int s = 0; s < kRing; ++s)
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        mbar_init(&S.full[s][x], 1);
-        S.nissued[s][x] = 0;
-      }
-    fence_mbar_init();
-    for (int li = 0; li < kRing && li < nloc; ++li) issue(li);
+        for (int x = 0; x < 2; ++x) {
+          mbar_init(&S.full[s][x], 1);
+          S.nissued[s][x] = 0;
+        }
+      fence_mbar_init();
+    }
+    __syncwarp();
   }
+  if (tid < G * kDim / 4) reinterpret_cast<uint2 *>(&S.qs[0][0])[tid] = qv;
+  __syncthreads();  // q and the pages staged; the ring initialised before any copy or wait
+  if (lane == 0)
+    for (int li = warp; li < kRing && li < nloc; li += kWarps) issue(li, S.pages[li]);
+  __syncwarp();
 
   // ---- per-head q exponent kq_h: |q_h| < 2^(8 + kq_h), so q * 2^(7 - pos - kq_h) is a finite fp16
   // (each MMA column is one head, so the shift may differ per head); every warp computes all four
@@ -861,7 +883,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   for (int hh = 0; hh < 4; ++hh) {
     float mx = 0.f;
     if (hh < G) {
-      const uint2 u = *reinterpret_cast<const uint2 *>(qb + hh * kDim + 4 * lane);
+      const uint2 u = *reinterpret_cast<const uint2 *>(&S.qs[hh][4 * lane]);
       const float2 x0 = Elem<__half>::to_f2(u.x), x1 = Elem<__half>::to_f2(u.y);
       mx = fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x1.x), fabsf(x1.y)));
     }
@@ -883,8 +905,8 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       if ((r & 3) != warp) continue;
       float lo = 0.f, hi = 0.f;
       if (hb < G) {
-        if (ktab(r, 1) >= 0) lo = __half2float(qb[hb * kDim + 32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
-        if (ktab(r, 3) >= 0) hi = __half2float(qb[hb * kDim + 32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
+        if (ktab(r, 1) >= 0) lo = __half2float(S.qs[hb][32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
+        if (ktab(r, 3) >= 0) hi = __half2float(S.qs[hb][32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
       }
       __half2 s2 = __floats2half2_rn(lo, hi);
       const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
@@ -896,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       if (((ks + 2) & 3) != warp) continue;
       uint32_t a0 = 0u, a2 = 0u;
       if (g < G) {
-        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qb + g * kDim + 32 * tig + 4 * ks);
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(&S.qs[g][32 * tig + 4 * ks]);
         a0 = qw[0];
         a2 = qw[1];
       }
@@ -904,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       rec[41 + 2 * ks] = a2;
     }
   }
-  __syncthreads();  // records written; the ring initialised before any wait
+  __syncthreads();  // records written
   const int kq = pick(tig);
 
   const float c1 = kScale * pow2(17 + kq), c2 = kScale;
@@ -1089,13 +1111,16 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       }
     }
     __syncwarp();
-    if (lane == 0 && li + kRing < nloc) issue(li + kRing);
+    if (lane == 0 && li + kRing < nloc) issue(li + kRing, S.pages[li + kRing]);
   }
   __syncthreads();
-  if (S.failed && tid == 0)  // a copy never landed: give every started copy a bounded chance to finish
-    for (int s = 0; s < kRing; ++s)
-      for (int x = 0; x < 2; ++x)
-        if (S.nissued[s][x] > 0) mbar_wait_bounded(&S.full[s][x], (S.nissued[s][x] - 1) & 1, a.status);
+  if (S.failed) {  // a copy never landed: give every started copy a bounded chance to finish
+    if (tid == 0)
+      for (int s = 0; s < kRing; ++s)
+        for (int x = 0; x < 2; ++x)
+          if (S.nissued[s][x] > 0) mbar_wait_bounded(&S.full[s][x], (S.nissued[s][x] - 1) & 1, a.status);
+    __syncthreads();  // the stages are reused below
+  }
 
   // ---- combine the four warps and write this chunk's partial
 #pragma unroll
@@ -1103,8 +1128,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   // a non-finite score or weight leaves the running sum non-finite (checked once per chunk;
   // the merge kernel also checks every output)
   if (tig < G && !isfinite(l_run)) st |= NSNKV_ST_OUTPUT_NONFINITE;
-  __syncthreads();
-  MergeSmem &M = S.u.merge;
+  MergeSmem &M = S.u.merge.part;
   if (tig < G) {
     if (g == 0) {
       M.m[warp][tig] = m_run;
@@ -1118,24 +1142,30 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     }
   }
   __syncthreads();
-  for (int e = tid; e < G * kDim; e += kThreads) {
-    const int n = e / kDim, c = e % kDim;
+  if (tid < G) {  // one thread per head: the warps' weights, the chunk's max and sum
+    const int n = tid;
     float mx = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
-    float o = 0.f, l = 0.f;
+    float l = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
-      o += wt * M.acc[w][n][c];
+      S.u.merge.wt[w][n] = wt;
       l += wt * M.l[w][n];
     }
     const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
+    a.part_ml[row * 2] = mx;
+    a.part_ml[row * 2 + 1] = l;
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) o += S.u.merge.wt[w][n] * M.acc[w][n][c];
+    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
     a.part_o[row * kDim + c] = o;
-    if (c == 0) {
-      a.part_ml[row * 2] = mx;
-      a.part_ml[row * 2 + 1] = l;
-    }
   }
   if (st) set_status(a.status, st);
 }
