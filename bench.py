@@ -226,6 +226,7 @@ def run_cfg1(args, rank, world, local, dist):
     from nsn_b200 import primitives as P
     from nsn_b200 import workloads
     from nsn_b200.kernel import decode_attention
+    from nsn_b200.paged import block_record_pools
     device = torch.device("cuda", local)
     c = workloads.CONFIGS[1]
     h, hq, nb, t = c["h"], c["hq"], c["blocks"], c["tail"]
@@ -234,15 +235,18 @@ def run_cfg1(args, rank, world, local, dist):
     v = workloads.torch_kv(gen, (h, nb * 64 + t, 128), (), c["v_sigma"], device=device)
     q = (torch.randn((1, hq, 128), generator=gen, device=device) * c["q_scale"]).half()
 
-    def pool_of(x, alpha):
-        pool = dict(codes=torch.empty((h, nb, 3072), dtype=torch.uint8, device=device),
-                    norm=torch.empty((h, nb, 64), dtype=torch.float16, device=device),
-                    min=torch.empty((h, nb, 128), dtype=torch.float16, device=device),
-                    scale=torch.empty((h, nb, 128), dtype=torch.float16, device=device))
+    def pools_of(alpha):
+        # the renorm-factor path in the paged cache's block-record layout, the restore path in dense arrays
         if alpha:
-            pool["alpha"] = torch.empty((h, nb, 64), dtype=torch.float32, device=device)
-        P.encode_blocks(x[:, :nb * 64].reshape(h, nb, 64, 128), 3, out=pool, out_row_stride=nb)
-        return pool
+            _, kp_, vp_ = block_record_pools(h, nb, 3, device)
+        else:
+            kp_, vp_ = [dict(codes=torch.empty((h, nb, 3072), dtype=torch.uint8, device=device),
+                             norm=torch.empty((h, nb, 64), dtype=torch.float16, device=device),
+                             min=torch.empty((h, nb, 128), dtype=torch.float16, device=device),
+                             scale=torch.empty((h, nb, 128), dtype=torch.float16, device=device)) for _ in range(2)]
+        for x, pool in ((k, kp_), (v, vp_)):
+            P.encode_blocks(x[:, :nb * 64].reshape(h, nb, 64, 128), 3, out=pool, out_row_stride=nb)
+        return kp_, vp_
 
     kt = k[None, :, nb * 64:].contiguous()
     vt = v[None, :, nb * 64:].contiguous()
@@ -254,7 +258,7 @@ def run_cfg1(args, rank, world, local, dist):
     stream = torch.cuda.current_stream(device)
     res = {}
     for name, alpha in (("renorm_factor_path", True), ("restore_path", False)):
-        kp, vp = pool_of(k, alpha), pool_of(v, alpha)
+        kp, vp = pools_of(alpha)
 
         def call():
             decode_attention(q, kp, vp, h=h, bits=3, blk_stride_head=nb, blk_stride_page=1, n_blocks=nb,

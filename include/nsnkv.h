@@ -79,6 +79,24 @@ int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks
                         int32_t *status, void *stream);
 
 /*
+ * Block strides.  The paged cache keeps the blocks of INT3 fp16 caches as block
+ * records: per (kv head, page) one record of 2 * (code_bytes + 768) bytes (7680 for
+ * INT3) holding K codes | K min (128 fp16) | K scale (128 fp16) | K renorm factors
+ * (64 fp32), then the same four fields for V; the norms stay in dense arrays.  Entry
+ * points that take blk_bytes address block o of the codes, min, scale and factor
+ * arrays at base + o * blk_bytes (blk_bytes a multiple of 16, at least code_bytes);
+ * blk_bytes = 0 means dense arrays (code_bytes, 256, 256 and 256 bytes per block).
+ * Norm arrays are always dense (128 bytes per block).
+ *
+ * nsnkv_encode_blocks with block strides: codes, mn and scale are fields of records
+ * blk_bytes apart (0: identical to nsnkv_encode_blocks).
+ */
+int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits,
+                                int norm_order, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
+                                uint16_t *scale, uint8_t *headers, int64_t header_start, int64_t out_row_stride,
+                                int64_t out_offset, int64_t blk_bytes, int32_t *status, void *stream);
+
+/*
  * Reconstruct rows of sealed blocks followed by an optional native tail.
  * Replaces nsn_decode (loop_kv_nb06_primitives.py:57-66), restore_group
  * (loop_kv_nb06_codec.py:36-38) and the VF01 bridge restore_v/materialize
@@ -144,7 +162,14 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
  *                      alpha_t = n_t / max(||d_t||, 1e-12) (0 when n_t == 0) with
  *                      d = min + scale * code: the factor nsn_decode applies to a row
  *                      (loop_kv_nb06_primitives.py:57-66); nsnkv_block_renorm and
- *                      nsnkv_seal_full_tails_alpha write it.
+ *                      nsnkv_seal_full_tails_alpha write it.  Both may be NULL: the
+ *                      blocks then take the nsnkv_decode_attn path (with blk_bytes).
+ *   blk_bytes          block stride of the codes, min, scale and factor arrays (0: dense;
+ *                      see nsnkv_encode_blocks_strided).  When each block's K fields and
+ *                      then its V fields form one block record (k_min = k_codes + CB,
+ *                      k_scale = k_codes + CB + 256, k_alpha = k_codes + CB + 512,
+ *                      v_codes = k_codes + CB + 768, the same offsets from v_codes, and
+ *                      blk_bytes = 2 * (CB + 768)), a block moves in one copy.
  * INT3 fp16 caches with hq / h <= 4 then run the sealed blocks on the tensor cores
  * without restoring any K or V value (the codes are the MMA operands); the norms are
  * not read.  Other shapes take the nsnkv_decode_attn path.  The result matches
@@ -155,7 +180,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale,
-                            const float *k_alpha, const float *v_alpha,
+                            const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
                             int64_t blk_stride_head, int64_t blk_stride_page,
                             const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
@@ -168,11 +193,12 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
 /*
  * Per-token renorm factors of sealed blocks (see nsnkv_decode_attn_alpha), for the
  * blocks nsnkv_encode_blocks lays out: block (row r, i) of rows x blocks_per_row has
- * index r*row_stride + offset + i in codes / norm / min / scale / alpha.
+ * index r*row_stride + offset + i in codes / norm / min / scale / alpha; blk_bytes is
+ * the block stride of codes / min / scale / alpha (0: dense).
  */
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
                        const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
-                       void *stream);
+                       int64_t blk_bytes, void *stream);
 
 /* Workspace bytes nsnkv_decode_attn needs for these sizes. */
 int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t max_blocks, int32_t max_tail);
@@ -235,7 +261,8 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
  * (k_alpha / v_alpha, fp32 [64] per block) in the same kernel.  seq_counters
  * (int32 [batch], may be NULL) must be zero before the first call and are left zero:
  * with them the last CTA of each sequence advances n_blocks / tail_len, so the call is
- * one launch; without them a second kernel advances the counters.
+ * one launch; without them a second kernel advances the counters.  blk_bytes is the
+ * block stride of the codes / min / scale / alpha arrays (0: dense).
  */
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
@@ -243,7 +270,7 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 const int32_t *block_table, int64_t table_stride,
                                 uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                 uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
-                                float *k_alpha, float *v_alpha, int32_t *seq_counters,
+                                float *k_alpha, float *v_alpha, int64_t blk_bytes, int32_t *seq_counters,
                                 int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream);
 
 /*

@@ -37,6 +37,8 @@ struct AttnArgs {
   const uint16_t *vn, *vm, *vs;
   const float *ka, *va;  // per-token renorm factors (sealed INT3 path), or null
   int64_t sh, sp;
+  int64_t cs, ms;    // bytes from one block to the next: code arrays, min / scale / factor arrays
+  int32_t one_copy;  // sealed kernel: each block's K then V arrays form one record of cs bytes
   const int32_t *table;
   int64_t table_stride;
   const int32_t *nblk;
@@ -407,14 +409,14 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *sme
       const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
       Stage<BITS> &sg = S.stage[s];
       mbar_expect_tx(&S.full[s], 2 * CB + 2 * (kBlock * 2 + 2 * kDim * 2));
-      bulk_g2s(sg.kc, a.kc + bi * CB, CB, &S.full[s]);
-      bulk_g2s(sg.vc, a.vc + bi * CB, CB, &S.full[s]);
+      bulk_g2s(sg.kc, a.kc + bi * a.cs, CB, &S.full[s]);
+      bulk_g2s(sg.vc, a.vc + bi * a.cs, CB, &S.full[s]);
       bulk_g2s(sg.kn, a.kn + bi * kBlock, kBlock * 2, &S.full[s]);
-      bulk_g2s(sg.km, a.km + bi * kDim, kDim * 2, &S.full[s]);
-      bulk_g2s(sg.ks, a.ks + bi * kDim, kDim * 2, &S.full[s]);
+      bulk_g2s(sg.km, blk_ptr(a.km, bi, a.ms), kDim * 2, &S.full[s]);
+      bulk_g2s(sg.ks, blk_ptr(a.ks, bi, a.ms), kDim * 2, &S.full[s]);
       bulk_g2s(sg.vn, a.vn + bi * kBlock, kBlock * 2, &S.full[s]);
-      bulk_g2s(sg.vm, a.vm + bi * kDim, kDim * 2, &S.full[s]);
-      bulk_g2s(sg.vs, a.vs + bi * kDim, kDim * 2, &S.full[s]);
+      bulk_g2s(sg.vm, blk_ptr(a.vm, bi, a.ms), kDim * 2, &S.full[s]);
+      bulk_g2s(sg.vs, blk_ptr(a.vs, bi, a.ms), kDim * 2, &S.full[s]);
     };
     if (tid == 0) {
 #pragma unroll
@@ -715,13 +717,17 @@ constexpr int kRec = 60;  // words of a lane's constant record: stride 4 * odd -
 constexpr int kCB = 3072;  // INT3 code bytes per block
 constexpr int kMaxChunk = 32;  // blocks per chunk (page indices staged in shared memory)
 
+// One block as the paged cache's block record holds it: K codes, min, scale, factors,
+// then the same for V (one copy when the arrays are laid out so).
 struct SStage {
   uint8_t kc[kCB];
+  uint16_t km[kDim], ks[kDim];
+  float ka[kBlock];
   uint8_t vc[kCB];
-  uint16_t km[kDim], ks[kDim], vm[kDim], vs[kDim];
-  float ka[kBlock], va[kBlock];
+  uint16_t vm[kDim], vs[kDim];
+  float va[kBlock];
 };
-static_assert(sizeof(SStage) == 7680, "stage layout");
+static_assert(sizeof(SStage) == 7680 && offsetof(SStage, vc) == 3840, "stage layout = K record, V record");
 
 struct SMerge {
   MergeSmem part;
@@ -837,14 +843,18 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     uint64_t *bar = &S.full[li % kRing][(li / kRing) & 1];
     S.nissued[li % kRing][(li / kRing) & 1] += 1;
     mbar_expect_tx(bar, sizeof(SStage));
-    bulk_g2s(sg.kc, a.kc + bi * kCB, kCB, bar);
-    bulk_g2s(sg.vc, a.vc + bi * kCB, kCB, bar);
-    bulk_g2s(sg.km, a.km + bi * kDim, kDim * 2, bar);
-    bulk_g2s(sg.ks, a.ks + bi * kDim, kDim * 2, bar);
-    bulk_g2s(sg.vm, a.vm + bi * kDim, kDim * 2, bar);
-    bulk_g2s(sg.vs, a.vs + bi * kDim, kDim * 2, bar);
-    bulk_g2s(sg.ka, a.ka + bi * kBlock, kBlock * 4, bar);
-    bulk_g2s(sg.va, a.va + bi * kBlock, kBlock * 4, bar);
+    if (a.one_copy) {  // the block record: one copy (each cp.async.bulk issue can wait on the TMA queue)
+      bulk_g2s(sg.kc, a.kc + bi * a.cs, sizeof(SStage), bar);
+      return;
+    }
+    bulk_g2s(sg.kc, a.kc + bi * a.cs, kCB, bar);
+    bulk_g2s(sg.vc, a.vc + bi * a.cs, kCB, bar);
+    bulk_g2s(sg.km, blk_ptr(a.km, bi, a.ms), kDim * 2, bar);
+    bulk_g2s(sg.ks, blk_ptr(a.ks, bi, a.ms), kDim * 2, bar);
+    bulk_g2s(sg.vm, blk_ptr(a.vm, bi, a.ms), kDim * 2, bar);
+    bulk_g2s(sg.vs, blk_ptr(a.vs, bi, a.ms), kDim * 2, bar);
+    bulk_g2s(sg.ka, blk_ptr(a.ka, bi, a.ms), kBlock * 4, bar);
+    bulk_g2s(sg.va, blk_ptr(a.va, bi, a.ms), kBlock * 4, bar);
   };
   // One round of global loads starts the CTA: q (8 bytes per thread) and the chunk's page
   // indices (warp 0, one coalesced load), staged in shared memory.  The copy issue never
@@ -1260,7 +1270,7 @@ namespace nsnkv {
 static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, const void *q, const uint8_t *k_codes,
                             const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
                             const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min,
-                            const uint16_t *v_scale, const float *k_alpha, const float *v_alpha,
+                            const uint16_t *v_scale, const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
                             int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
                             int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
                             void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
@@ -1284,8 +1294,19 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   if (!tail_len && tail_len_const > max_tail) return NSNKV_ERR_ARG;
   if (workspace_bytes < nsnkv_decode_attn_workspace_bytes(batch, hq, h, max_blocks, max_tail)) return NSNKV_ERR_ARG;
   if (batch > 65535 || h > 65535) return NSNKV_ERR_ARG;
+  const int64_t cb = code_bytes(bits);
+  if (blk_bytes != 0 && (blk_bytes < cb || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
 
   AttnArgs a{};
+  a.cs = blk_bytes ? blk_bytes : cb;
+  a.ms = blk_bytes ? blk_bytes : kDim * 2;
+  {  // K record then V record, contiguous: [codes | min | scale | factors] twice
+    const uint8_t *r = k_codes;
+    const auto at = [&](const void *p, int64_t off) { return static_cast<const void *>(r + off) == p; };
+    a.one_copy = blk_bytes == 2 * (cb + 768) && at(k_min, cb) && at(k_scale, cb + 256) && at(k_alpha, cb + 512) &&
+                 at(v_codes, cb + 768) && at(v_min, 2 * cb + 768) && at(v_scale, 2 * cb + 1024) &&
+                 at(v_alpha, 2 * cb + 1280);
+  }
   a.batch = batch;
   a.hq = hq;
   a.h = h;
@@ -1393,7 +1414,7 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
                       float *out_f32, float *lse, void *workspace, int64_t workspace_bytes, int32_t *status,
                       void *stream) {
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, nullptr, nullptr, blk_stride_head, blk_stride_page, block_table, table_stride,
+                          v_scale, nullptr, nullptr, 0, blk_stride_head, blk_stride_page, block_table, table_stride,
                           n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                           tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
                           workspace_bytes, status, stream);
@@ -1403,16 +1424,17 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
-                            const float *v_alpha, int64_t blk_stride_head, int64_t blk_stride_page,
+                            const float *v_alpha, int64_t blk_bytes, int64_t blk_stride_head, int64_t blk_stride_page,
                             const int32_t *block_table, int64_t table_stride, const int32_t *n_blocks,
                             int32_t n_blocks_const, int32_t max_blocks, void *k_tail, void *v_tail,
                             int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
                             int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new,
                             void *out, float *out_f32, float *lse, void *workspace, int64_t workspace_bytes,
                             int32_t *status, void *stream) {
-  if (max_blocks > 0 && (!k_alpha || !v_alpha)) return NSNKV_ERR_ARG;
+  if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, k_alpha, v_alpha, blk_stride_head, blk_stride_page, block_table, table_stride,
+                          v_scale, k_alpha, v_alpha, blk_bytes, blk_stride_head, blk_stride_page, block_table,
+                          table_stride,
                           n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                           tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
                           workspace_bytes, status, stream);

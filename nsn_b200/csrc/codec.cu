@@ -392,7 +392,8 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
                                                             uint8_t *codes, uint8_t *q_out, uint16_t *norm,
                                                             uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                             int64_t header_start, int64_t out_row_stride,
-                                                            int64_t out_offset, int32_t *status) {
+                                                            int64_t out_offset, int64_t cs, int64_t ms,
+                                                            int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
   const int64_t b = blockIdx.x;
@@ -400,9 +401,8 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
   const int64_t o = r * out_row_stride + out_offset + i;
   int st = load_block<T>(x + b * kBlock * kDim, s);
   __syncthreads();
-  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * code_bytes(BITS) : nullptr,
-                       q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, mn + o * kDim,
-                       scale + o * kDim, status, st);
+  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * cs : nullptr, q_out ? q_out + b * kBlock * kDim : nullptr,
+                       norm + o * kBlock, blk_ptr(mn, o, ms), blk_ptr(scale, o, ms), status, st);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
 }
 
@@ -411,15 +411,16 @@ __global__ void __launch_bounds__(256, 4) encode_blocks_fast_kernel(const __half
                                                                    uint8_t *codes, uint8_t *q_out, uint16_t *norm,
                                                                    uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                                    int64_t header_start, int64_t out_row_stride,
-                                                                   int64_t out_offset, int32_t *status) {
+                                                                   int64_t out_offset, int64_t cs, int64_t ms,
+                                                                   int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
   const int64_t b = blockIdx.x;
   const int64_t r = b / blocks_per_row, i = b % blocks_per_row;
   const int64_t o = r * out_row_stride + out_offset + i;
-  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * code_bytes(BITS) : nullptr,
-                          q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, mn + o * kDim,
-                          scale + o * kDim, status, s);
+  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * cs : nullptr,
+                          q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, blk_ptr(mn, o, ms),
+                          blk_ptr(scale, o, ms), status, s);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
 }
 
@@ -556,7 +557,7 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
                                                    uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                                    uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
                                                    uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done,
-                                                   int64_t sh, int64_t sp, int32_t *status) {
+                                                   int64_t sh, int64_t sp, int64_t cs, int64_t ms, int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // launched with a programmatic dependency: wait for the kernel before it, then let the
   // next one (the following decode step) launch while this grid runs
@@ -571,10 +572,10 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
     const int32_t page = table[b * table_stride + nbk];
     const int64_t blk = h * sh + static_cast<int64_t>(page) * sp;
     const T *src = (kv == 0 ? k_tail : v_tail) + (b * tss + h * tsh) * kDim;
-    uint8_t *codes = (kv == 0 ? k_codes : v_codes) + blk * code_bytes(BITS);
+    uint8_t *codes = (kv == 0 ? k_codes : v_codes) + blk * cs;
     uint16_t *nrm = (kv == 0 ? k_norm : v_norm) + blk * kBlock;
-    uint16_t *mn = (kv == 0 ? k_min : v_min) + blk * kDim;
-    uint16_t *sc = (kv == 0 ? k_scale : v_scale) + blk * kDim;
+    uint16_t *mn = blk_ptr(kv == 0 ? k_min : v_min, blk, ms);
+    uint16_t *sc = blk_ptr(kv == 0 ? k_scale : v_scale, blk, ms);
     if constexpr (std::is_same<T, __half>::value) {
       encode_block_fast<BITS>(src, codes, nullptr, nrm, mn, sc, status, *reinterpret_cast<FastSmem *>(smem_raw));
     } else {
@@ -585,7 +586,7 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
     }
     if (k_alpha) {
       __syncthreads();  // this CTA's code and metadata stores are visible to all its threads
-      renorm_block<BITS>(codes, nrm, mn, sc, (kv == 0 ? k_alpha : v_alpha) + blk * kBlock);
+      renorm_block<BITS>(codes, nrm, mn, sc, blk_ptr(kv == 0 ? k_alpha : v_alpha, blk, ms));
     }
   }
   if (done) {
@@ -643,24 +644,25 @@ __device__ void renorm_block(const uint8_t *codes, const uint16_t *norm, const u
   }
 }
 
-// Blocks laid out as nsnkv_encode_blocks writes them: block (row r, i) at r * row_stride + offset + i.
+// Blocks laid out as nsnkv_encode_blocks writes them: block (row r, i) at r * row_stride + offset + i;
+// consecutive blocks are cs bytes apart in codes and ms bytes apart in min / scale / alpha.
 template <int BITS>
 __global__ void __launch_bounds__(256) renorm_blocks_kernel(const uint8_t *codes, const uint16_t *norm,
                                                             const uint16_t *mn, const uint16_t *sc,
                                                             int64_t blocks_per_row, int64_t row_stride,
-                                                            int64_t offset, float *alpha) {
+                                                            int64_t offset, float *alpha, int64_t cs, int64_t ms) {
   const int64_t r = blockIdx.x / blocks_per_row, i = blockIdx.x % blocks_per_row;
   const int64_t blk = r * row_stride + offset + i;
-  renorm_block<BITS>(codes + blk * code_bytes(BITS), norm + blk * kBlock, mn + blk * kDim, sc + blk * kDim,
-                     alpha + blk * kBlock);
+  renorm_block<BITS>(codes + blk * cs, norm + blk * kBlock, blk_ptr(mn, blk, ms), blk_ptr(sc, blk, ms),
+                     blk_ptr(alpha, blk, ms));
 }
 
 // ----------------------------------------------------------------- host dispatch
 template <typename T>
 static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits, int norm_order, uint8_t *codes,
                          uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale, uint8_t *headers,
-                         int64_t header_start, int64_t out_row_stride, int64_t out_offset, int32_t *status,
-                         cudaStream_t st) {
+                         int64_t header_start, int64_t out_row_stride, int64_t out_offset, int64_t cs, int64_t ms,
+                         int32_t *status, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>(n_blocks));
   if (std::is_same<T, __half>::value && norm_order == 0) {
     const size_t smem = sizeof(FastSmem);
@@ -670,7 +672,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
       return NSNKV_ERR_CUDA;                                                                               \
     k<<<grid, 256, smem, st>>>(static_cast<const __half *>(x), bpr, codes, q_out, norm, mn, scale, headers, \
-                               header_start, out_row_stride, out_offset, status);                          \
+                               header_start, out_row_stride, out_offset, cs, ms, status);                  \
     break;                                                                                                 \
   }
     switch (bits) {
@@ -690,7 +692,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)       \
       return NSNKV_ERR_CUDA;                                                                              \
     k<<<grid, 256, smem, st>>>(static_cast<const T *>(x), norm_order, bpr, codes, q_out, norm, mn, scale, \
-                               headers, header_start, out_row_stride, out_offset, status);                \
+                               headers, header_start, out_row_stride, out_offset, cs, ms, status);        \
     break;                                                                                                \
   }
   switch (bits) {
@@ -745,7 +747,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
                        uint16_t *vm, uint16_t *vs, float *ka, float *va, int32_t *done, int64_t sh, int64_t sp,
-                       int32_t *status, cudaStream_t st) {
+                       int64_t cs, int64_t ms, int32_t *status, cudaStream_t st) {
   const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
@@ -765,7 +767,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     cfg.numAttrs = 1;                                                                                      \
     if (cudaLaunchKernelEx(&cfg, k, static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss,   \
                            tsh, tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
-                           va, done, sh, sp, status) != cudaSuccess)                                       \
+                           va, done, sh, sp, cs, ms, status) != cudaSuccess)                               \
       return NSNKV_ERR_LAUNCH;                                                                             \
     break;                                                                                                 \
   }
@@ -792,12 +794,14 @@ int nsnkv_version(void) { return 1; }
 
 int64_t nsnkv_block_code_bytes(int bits) { return (bits >= 3 && bits <= 5) ? code_bytes(bits) : 0; }
 
-int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits, int norm_order,
-                        uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale,
-                        uint8_t *headers, int64_t header_start, int64_t out_row_stride, int64_t out_offset,
-                        int32_t *status, void *stream) {
+int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits,
+                                int norm_order, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
+                                uint16_t *scale, uint8_t *headers, int64_t header_start, int64_t out_row_stride,
+                                int64_t out_offset, int64_t blk_bytes, int32_t *status, void *stream) {
   if (rows < 0 || blocks_per_row < 0 || bits < 3 || bits > 5 || (norm_order != 0 && norm_order != 1))
     return NSNKV_ERR_ARG;
+  if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
+  const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   const int64_t n_blocks = rows * blocks_per_row;
   if (n_blocks == 0) return NSNKV_OK;
   if (n_blocks > 0x7FFFFFFF || !x || !norm || !mn || !scale || !status || !aligned16(x)) return NSNKV_ERR_ARG;
@@ -807,16 +811,24 @@ int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks
   switch (x_dtype) {
     case NSNKV_F16:
       return launch_encode<__half>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                   headers, header_start, out_row_stride, out_offset, status, st);
+                                   headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
     case NSNKV_BF16:
       return launch_encode<__nv_bfloat16>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn,
-                                          scale, headers, header_start, out_row_stride, out_offset, status, st);
+                                          scale, headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
     case NSNKV_F32:
       return launch_encode<float>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                  headers, header_start, out_row_stride, out_offset, status, st);
+                                  headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
+}
+
+int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits, int norm_order,
+                        uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale,
+                        uint8_t *headers, int64_t header_start, int64_t out_row_stride, int64_t out_offset,
+                        int32_t *status, void *stream) {
+  return nsnkv_encode_blocks_strided(x, x_dtype, rows, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
+                                     headers, header_start, out_row_stride, out_offset, 0, status, stream);
 }
 
 int nsnkv_restore(const uint8_t *codes, int codes_unpacked, const uint16_t *norm, const uint16_t *mn,
@@ -866,9 +878,11 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
                      int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks, int pending_append,
                      const int32_t *block_table, int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm,
                      uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done, int64_t blk_stride_head,
-                     int64_t blk_stride_page, int32_t *status, void *stream) {
+                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int32_t *done,
+                     int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream) {
   if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
+  if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
+  const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   if (batch == 0) return NSNKV_OK;
   if (!k_tail || !v_tail || !tail_len || !n_blocks || !block_table || !k_codes || !v_codes || !status)
     return NSNKV_ERR_ARG;
@@ -881,12 +895,12 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
       return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
                                  n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
                                  k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, done, blk_stride_head,
-                                 blk_stride_page, status, st);
+                                 blk_stride_page, cs, ms, status, st);
     case NSNKV_BF16:
       return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                                         tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
                                         k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha,
-                                        done, blk_stride_head, blk_stride_page, status, st);
+                                        done, blk_stride_head, blk_stride_page, cs, ms, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -900,7 +914,7 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tai
                           int32_t *status, void *stream) {
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, nullptr, nullptr, nullptr, blk_stride_head, blk_stride_page, status, stream);
+                   v_min, v_scale, nullptr, nullptr, 0, nullptr, blk_stride_head, blk_stride_page, status, stream);
 }
 
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
@@ -908,18 +922,22 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void 
                                 int32_t *n_blocks, int pending_append, const int32_t *block_table,
                                 int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min,
                                 uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *seq_counters,
-                                int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream) {
+                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes,
+                                int32_t *seq_counters, int64_t blk_stride_head, int64_t blk_stride_page,
+                                int32_t *status, void *stream) {
   if (!k_alpha || !v_alpha) return NSNKV_ERR_ARG;
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, k_alpha, v_alpha, seq_counters, blk_stride_head, blk_stride_page, status, stream);
+                   v_min, v_scale, k_alpha, v_alpha, blk_bytes, seq_counters, blk_stride_head, blk_stride_page,
+                   status, stream);
 }
 
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
                        const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
-                       void *stream) {
+                       int64_t blk_bytes, void *stream) {
   if (bits < 3 || bits > 5 || rows < 0 || blocks_per_row < 0 || offset < 0) return NSNKV_ERR_ARG;
+  if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
+  const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   if (rows == 0 || blocks_per_row == 0) return NSNKV_OK;
   if (!codes || !norm || !min || !scale || !alpha || row_stride < blocks_per_row + offset) return NSNKV_ERR_ARG;
   if (rows * blocks_per_row > 0x7fffffffLL) return NSNKV_ERR_TOO_LARGE;
@@ -927,13 +945,16 @@ int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uin
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bits) {
     case 3:
-      renorm_blocks_kernel<3><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      renorm_blocks_kernel<3><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
+                                                     alpha, cs, ms);
       break;
     case 4:
-      renorm_blocks_kernel<4><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      renorm_blocks_kernel<4><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
+                                                     alpha, cs, ms);
       break;
     default:
-      renorm_blocks_kernel<5><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset, alpha);
+      renorm_blocks_kernel<5><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
+                                                     alpha, cs, ms);
       break;
   }
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;

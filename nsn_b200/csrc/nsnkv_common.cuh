@@ -16,6 +16,12 @@ constexpr float kEps = 1e-12f;
 constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128)
 
 __host__ __device__ constexpr int code_bytes(int bits) { return kBlock * kDim * bits / 8; }
+// Block i of an array whose blocks are `bytes` apart (a dense array, or one field of the
+// paged cache's block records).
+template <typename T>
+__host__ __device__ __forceinline__ T *blk_ptr(T *base, int64_t i, int64_t bytes) {
+  return reinterpret_cast<T *>(reinterpret_cast<uintptr_t>(base) + static_cast<uintptr_t>(i * bytes));
+}
 
 // ----------------------------------------------------------------- dtype helpers
 template <typename T> struct Elem;

@@ -46,13 +46,16 @@ def workspace(nbytes: int, device) -> torch.Tensor:
 def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_page, n_blocks, max_blocks,
                      k_tail=None, v_tail=None, tail_stride_seq=0, tail_stride_head=0, tail_len=0, max_tail=0,
                      block_table=None, k_new=None, v_new=None, out=None, out_f32=None, lse=None, status=None,
-                     ws=None):
-    """Direct binding of nsnkv_decode_attn (nsnkv_decode_attn_alpha when both pools carry "alpha").
+                     ws=None, blk_bytes=None):
+    """Direct binding of nsnkv_decode_attn (nsnkv_decode_attn_alpha when both pools carry
+    "alpha" or their arrays are fields of block records).
 
     q [B, hq, 128]; k_pool/v_pool dicts of codes/norm/min/scale tensors, plus the
     per-token renorm factors "alpha" (fp32, 64 per block) when the cache keeps them
     (or None when max_blocks == 0); n_blocks/tail_len either ints (same for every
-    sequence) or int32 CUDA tensors [B].  Returns (out, status).
+    sequence) or int32 CUDA tensors [B].  blk_bytes: the block stride of the
+    codes / min / scale / alpha arrays (None: read from the tensors' strides, 0: dense).
+    Returns (out, status).
     """
     L.require_cuda()
     B, hq = q.shape[0], q.shape[1]
@@ -69,11 +72,18 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     tl_t = tail_len if isinstance(tail_len, torch.Tensor) else None
     kp = k_pool or {}
     vp = v_pool or {}
+    if blk_bytes is None:
+        blk_bytes = 0
+        if max_blocks:
+            blk_bytes = w.blk_bytes_of(kp, bits)
+            w.require(w.blk_bytes_of(vp, bits) == blk_bytes, "K and V pool layouts")
     blocks = (L.ptr(kp.get("codes")), L.ptr(kp.get("norm")), L.ptr(kp.get("min")), L.ptr(kp.get("scale")),
               L.ptr(vp.get("codes")), L.ptr(vp.get("norm")), L.ptr(vp.get("min")), L.ptr(vp.get("scale")))
-    if kp.get("alpha") is not None and vp.get("alpha") is not None:
+    has_alpha = kp.get("alpha") is not None and vp.get("alpha") is not None
+    if has_alpha or blk_bytes:
         entry, name = lib.nsnkv_decode_attn_alpha, "nsnkv_decode_attn_alpha"
-        blocks = blocks + (L.ptr(kp["alpha"]), L.ptr(vp["alpha"]))
+        alphas = (L.ptr(kp["alpha"]), L.ptr(vp["alpha"])) if has_alpha else (L.ptr(None), L.ptr(None))
+        blocks = blocks + alphas + (int(blk_bytes),)
     else:
         entry, name = lib.nsnkv_decode_attn, "nsnkv_decode_attn"
     rc = entry(

@@ -22,6 +22,10 @@ Layout (head-major pools so one sequence's blocks of one head are contiguous):
   whenever a block is (sealed, prefilled or imported) so attention does not recompute
   ||d|| per step; derived data, not part of the reference's format or of the exports
   block (sequence b, head j, block i) = pool row j, page block_table[b, i]
+  For caches on the tensor-core path (INT3, fp16, hq / h <= 4) codes / min / scale /
+  alpha of K and then of V are fields of one block record per (head, page),
+  records [h, pages, 7680] uint8, so the attention kernel moves a block with one copy;
+  the pool dicts hold views of those fields (norms stay dense).
   block_table [batch, max_blocks] int32 (sequence b owns pages b*max_blocks ..)
   n_blocks, tail_len [batch] int32 (device), k_tail/v_tail [batch, h, 64, 128].
 """
@@ -112,6 +116,29 @@ def sequence_from_bytes(blob: bytes, device="cpu"):
     return groups[0], tails[0], groups[1], tails[1]
 
 
+def block_record_pools(h: int, pages: int, bits: int, device):
+    """Zeroed block records [h, pages, 2 * (code_bytes + 768)] uint8 and the K / V pool dicts.
+
+    Record (head j, page p): K codes | K min (128 fp16) | K scale (128 fp16) | K alpha
+    (64 fp32), then the same four fields for V (7680 bytes for INT3).  The pool dicts
+    hold views of those fields, so every operator that takes a pool writes or reads the
+    records; norms [h, pages, 64] fp16 stay dense.  nsnkv_decode_attn_alpha moves each
+    block with one copy when given these pools (blk_bytes = the record size).
+    """
+    cb = w.code_bytes(bits)
+    half = cb + 2 * w.DIM * 2 + w.BLOCK * 4
+    rec = torch.zeros((h, pages, 2 * half), dtype=torch.uint8, device=device)
+
+    def fields(off):
+        return dict(codes=rec[..., off:off + cb],
+                    norm=torch.zeros((h, pages, w.BLOCK), dtype=torch.float16, device=device),
+                    min=rec[..., off + cb:off + cb + 2 * w.DIM].view(torch.float16),
+                    scale=rec[..., off + cb + 2 * w.DIM:off + cb + 4 * w.DIM].view(torch.float16),
+                    alpha=rec[..., off + cb + 4 * w.DIM:off + half].view(torch.float32))
+
+    return rec, fields(0), fields(half)
+
+
 class PagedKVCache:
     def __init__(self, batch: int, h: int, max_blocks: int, bits: int = 3, dtype=torch.float16, device="cuda",
                  hq: int | None = None, bridge_rounding: bool = False):
@@ -140,7 +167,13 @@ class PagedKVCache:
                 p["alpha"] = torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float32, device=dev)
             return p
 
-        self.k_pool, self.v_pool = pool(), pool()
+        self.records = None
+        self.blk_bytes = 0
+        if self.uses_alpha_path():
+            self.records, self.k_pool, self.v_pool = block_record_pools(h, self.pages, bits, dev)
+            self.blk_bytes = self.records.shape[-1]
+        else:
+            self.k_pool, self.v_pool = pool(), pool()
         self.block_table = torch.arange(self.pages, dtype=torch.int32, device=dev).reshape(batch, max_blocks)
         self.n_blocks = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.tail_len = torch.zeros(batch, dtype=torch.int32, device=dev)
@@ -252,7 +285,8 @@ class PagedKVCache:
             n_blocks=self.n_blocks, max_blocks=self.max_blocks, k_tail=self.k_tail, v_tail=self.v_tail,
             tail_stride_seq=self.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=self.tail_len,
             max_tail=w.BLOCK - 1, block_table=self.block_table, k_new=k_new, v_new=v_new,
-            out=self.out if out is None else out, out_f32=out_f32, lse=lse, status=self.status, ws=self.ws)[0]
+            out=self.out if out is None else out, out_f32=out_f32, lse=lse, status=self.status, ws=self.ws,
+            blk_bytes=self.blk_bytes)[0]
 
     def seal(self, pending_append: int = 1):
         lib = L.load()
@@ -274,8 +308,8 @@ class PagedKVCache:
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
             L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
-            L.ptr(self.v_pool["alpha"]), L.ptr(self.seal_counters), self.pages, 1, L.ptr(self.status),
-            L.stream_handle(self.device))
+            L.ptr(self.v_pool["alpha"]), self.blk_bytes, L.ptr(self.seal_counters), self.pages, 1,
+            L.ptr(self.status), L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, out=None):

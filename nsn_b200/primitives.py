@@ -147,11 +147,12 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
         codes, n, m, s = out["codes"], out["norm"], out["min"], out["scale"]
         hdr = out.get("headers") if headers_start is not None else None
         stride, offset = (out_row_stride if out_row_stride is not None else bpr), out_offset
+    blk = 0 if out is None else blk_bytes_of(out, bits)
     q = torch.empty(lead + (BLOCK, DIM), dtype=torch.uint8, device=dev) if unpacked else None
     if nblk:
-        L.check(L.load().nsnkv_encode_blocks(
+        L.check(L.load().nsnkv_encode_blocks_strided(
             L.ptr(xc), L.DTYPE_CODE[x.dtype], rows, bpr, bits, order, L.ptr(codes), L.ptr(q), L.ptr(n), L.ptr(m),
-            L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, L.ptr(status), L.stream_handle(dev)),
+            L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, blk, L.ptr(status), L.stream_handle(dev)),
             "nsnkv_encode_blocks")
         if out is not None and out.get("alpha") is not None and codes is not None:
             block_renorm(out, bits, rows, bpr, stride, offset)
@@ -162,6 +163,40 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
         res["status"] = status
     res.update(codes=codes, q=q, metas=(n, m, s), headers=hdr)
     return res
+
+
+def blk_bytes_of(pool, bits: int) -> int:
+    """Block stride (bytes) shared by a pool's codes / min / scale / alpha arrays.
+
+    0 when every array is dense (code_bytes, 256, 256 and 256 bytes per block); the
+    common stride when they are fields of block records (the paged cache's layout for
+    INT3 fp16 caches, see nsnkv_encode_blocks_strided).  Norms are always dense.
+    """
+    per = {"codes": code_bytes(bits), "min": DIM, "scale": DIM, "alpha": BLOCK}
+    found = set()
+    dense = True
+    for key, e in per.items():
+        t = pool.get(key)
+        if t is None:
+            continue
+        try:
+            v = t.view(-1, e)
+        except RuntimeError:
+            raise ContractError(f"pool {key} layout") from None
+        require(v.stride(1) == 1, f"pool {key} layout")
+        if v.shape[0] <= 1:
+            continue
+        sb = v.stride(0) * t.element_size()
+        found.add(sb)
+        dense = dense and sb == e * t.element_size()
+    nrm = pool.get("norm")
+    require(nrm is None or nrm.is_contiguous(), "pool norm layout")
+    if dense:
+        return 0
+    require(len(found) == 1, "pool block strides")
+    sb = found.pop()
+    require(sb % 16 == 0 and sb >= code_bytes(bits), "pool block strides")
+    return sb
 
 
 def block_renorm(pool, bits: int, rows: int, blocks_per_row: int, row_stride: int, offset: int = 0):
@@ -176,7 +211,8 @@ def block_renorm(pool, bits: int, rows: int, blocks_per_row: int, row_stride: in
     if rows and blocks_per_row:
         L.check(L.load().nsnkv_block_renorm(
             bits, rows, blocks_per_row, L.ptr(pool["codes"]), L.ptr(pool["norm"]), L.ptr(pool["min"]),
-            L.ptr(pool["scale"]), row_stride, offset, L.ptr(pool["alpha"]), L.stream_handle(pool["codes"].device)),
+            L.ptr(pool["scale"]), row_stride, offset, L.ptr(pool["alpha"]), blk_bytes_of(pool, bits),
+            L.stream_handle(pool["codes"].device)),
             "nsnkv_block_renorm")
 
 

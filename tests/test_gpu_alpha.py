@@ -265,3 +265,48 @@ def test_alpha_path_flags_nonfinite_metadata(where):
     cache.attend(torch.from_numpy(q).cuda())
     with pytest.raises(w.NumericalFailure):
         cache.check()
+
+
+def test_block_records_match_dense_arrays():
+    """The cache's block records (one copy per block) and dense copies of the same arrays
+    (eight copies per block) give bit-identical attention, on both entry points."""
+    from nsn_b200.kernel import decode_attention
+    from nsn_b200 import primitives as w
+    rng = np.random.default_rng(21)
+    lens = [64 * 40 + 9, 64 * 3, 64 * 77 + 63, 5]
+    cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=80)
+    assert cache.blk_bytes == 7680 and w.blk_bytes_of(cache.k_pool, 3) == 7680
+    qt = torch.from_numpy(q).cuda()
+    common = dict(h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1, n_blocks=cache.n_blocks,
+                  max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
+                  tail_stride_seq=cache.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=cache.tail_len,
+                  max_tail=w.BLOCK - 1, block_table=cache.block_table)
+    for keys in (("codes", "norm", "min", "scale", "alpha"), ("codes", "norm", "min", "scale")):
+        rec = [{k: p[k] for k in keys} for p in (cache.k_pool, cache.v_pool)]
+        dense = [{k: p[k].contiguous() for k in keys} for p in (cache.k_pool, cache.v_pool)]
+        assert w.blk_bytes_of(dense[0], 3) == 0
+        a, sa = decode_attention(qt, rec[0], rec[1], **common)
+        b, sb = decode_attention(qt, dense[0], dense[1], **common)
+        torch.cuda.synchronize()
+        assert int(sa.item()) == 0 and int(sb.item()) == 0
+        assert torch.equal(a, b), keys
+
+
+def test_encode_into_block_records_matches_dense():
+    """encode_blocks into record views writes the dense encoder's bytes, and the factors
+    nsnkv_block_renorm writes there equal the dense ones."""
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    from nsn_b200.paged import block_record_pools
+    rng = np.random.default_rng(22)
+    x = torch.from_numpy(workloads.np_kv(rng, (2, 6, 64, 128), workloads.K_OUTLIERS_4, 0.5)).cuda()
+    rec, kp, _ = block_record_pools(2, 9, 3, "cuda")
+    w.encode_blocks(x, 3, out=kp, out_row_stride=9, out_offset=2)
+    ref = w.encode_blocks(x, 3)
+    dense = dict(codes=ref["codes"], norm=ref["metas"][0].reshape(2, 6, 64), min=ref["metas"][1].reshape(2, 6, 128),
+                 scale=ref["metas"][2].reshape(2, 6, 128), alpha=torch.zeros((2, 6, 64), device="cuda"))
+    w.block_renorm(dense, 3, 2, 6, 6)
+    torch.cuda.synchronize()
+    for k in ("codes", "norm", "min", "scale", "alpha"):
+        assert torch.equal(kp[k][:, 2:8], dense[k]), k
+    assert int(rec[:, :2].count_nonzero()) == 0 and int(rec[:, 8:].count_nonzero()) == 0

@@ -70,3 +70,38 @@ def test_sequence_container_rejects_corruption():
     bad[:8] = b"NOTNSNKV"
     with pytest.raises(w.ContractError):
         sequence_from_bytes(bytes(bad))
+
+
+def test_block_record_pools_layout():
+    """The paged cache's block records: K fields then V fields per (head, page), views in the pool dicts."""
+    from nsn_b200 import primitives as w
+    from nsn_b200.paged import block_record_pools
+    rec, kp, vp = block_record_pools(2, 5, 3, "cpu")
+    assert tuple(rec.shape) == (2, 5, 7680)
+    assert w.blk_bytes_of(kp, 3) == 7680 and w.blk_bytes_of(vp, 3) == 7680
+    base = rec.data_ptr()
+    offs = {k: kp[k].data_ptr() - base for k in ("codes", "min", "scale", "alpha")}
+    assert offs == {"codes": 0, "min": 3072, "scale": 3328, "alpha": 3584}
+    assert vp["codes"].data_ptr() - base == 3840 and vp["alpha"].data_ptr() - base == 3840 + 3584
+    # writes through the views land in the records
+    kp["alpha"][1, 3, 5] = 2.5
+    vp["min"][0, 4, 127] = 1.0
+    assert rec[1, 3, 3584 + 20:3584 + 24].view(torch.float32).item() == 2.5
+    assert rec[0, 4, 3840 + 3072 + 254:3840 + 3072 + 256].view(torch.float16).item() == 1.0
+    assert kp["norm"].is_contiguous() and tuple(kp["norm"].shape) == (2, 5, 64)
+
+
+def test_blk_bytes_of_dense_and_rejected_layouts():
+    from nsn_b200 import primitives as w
+    from nsn_b200.paged import block_record_pools
+    dense = dict(codes=torch.zeros((2, 4, 3072), dtype=torch.uint8), norm=torch.zeros((2, 4, 64), dtype=torch.float16),
+                 min=torch.zeros((2, 4, 128), dtype=torch.float16), scale=torch.zeros((2, 4, 128), dtype=torch.float16),
+                 alpha=torch.zeros((2, 4, 64), dtype=torch.float32))
+    assert w.blk_bytes_of(dense, 3) == 0
+    _, kp, _ = block_record_pools(2, 4, 3, "cpu")
+    mixed = dict(kp, codes=dense["codes"])  # dense codes with record metadata
+    with pytest.raises(w.ContractError):
+        w.blk_bytes_of(mixed, 3)
+    bad = dict(dense, min=torch.zeros((2, 128, 4), dtype=torch.float16).transpose(1, 2))
+    with pytest.raises(w.ContractError):
+        w.blk_bytes_of(bad, 3)
