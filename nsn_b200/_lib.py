@@ -40,7 +40,7 @@ SIGNATURES = [
     ("nsnkv_encode_blocks", c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, P, P, P, P, P, c_int64, c_int64,
                                     c_int64, P, P]),
     ("nsnkv_encode_blocks_strided", c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, P, P, P, P, P, c_int64,
-                                            c_int64, c_int64, c_int64, P, P]),
+                                            c_int64, c_int64, c_int64, c_int, P, P]),
     ("nsnkv_restore", c_int, [P, c_int, P, P, P, c_int64, c_int64, c_int, P, c_int64, c_int, P, P, P]),
     ("nsnkv_pack", c_int, [P, c_int64, c_int, P, P, P]),
     ("nsnkv_unpack", c_int, [P, c_int64, c_int, P, P]),
@@ -53,13 +53,13 @@ SIGNATURES = [
                                   P, P, P, P, P, P, c_int64, P, P]),
     ("nsnkv_decode_attn_workspace_bytes", c_int64, [c_int64, c_int, c_int, c_int32, c_int32]),
     ("nsnkv_decode_attn_alpha", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
-                                        P, P, P, P, P, P, P, P, P, P, c_int64,
+                                        P, P, P, P, P, P, P, P, P, P, c_int64, c_int,
                                         c_int64, c_int64, P, c_int64,
                                         P, c_int32, c_int32,
                                         P, P, c_int64, c_int64,
                                         P, c_int32, c_int32,
                                         P, P, P, P, P, P, c_int64, P, P]),
-    ("nsnkv_block_renorm", c_int, [c_int, c_int64, c_int64, P, P, P, P, c_int64, c_int64, P, c_int64, P]),
+    ("nsnkv_block_renorm", c_int, [c_int, c_int64, c_int64, P, P, P, P, c_int64, c_int64, P, c_int64, c_int, P]),
     ("nsnkv_decode_attn_noalloc", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
                                           P, P, P, P, P, P, P, P,
                                           c_int64, c_int64, P, c_int64,
@@ -70,8 +70,8 @@ SIGNATURES = [
     ("nsnkv_seal_full_tails", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P, c_int64,
                                       P, P, P, P, P, P, P, P, c_int64, c_int64, P, P]),
     ("nsnkv_seal_full_tails_alpha", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P,
-                                            c_int64, P, P, P, P, P, P, P, P, P, P, c_int64, P, c_int64, c_int64, P,
-                                            P]),
+                                            c_int64, P, P, P, P, P, P, P, P, P, P, c_int64, c_int, P, c_int64,
+                                            c_int64, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),

@@ -817,6 +817,9 @@ __device__ __forceinline__ uint32_t split_hilo(float w) {
 
 }  // namespace s3
 
+// VP: the V codes are paired rows (token rows 2j and 2j+1 interleaved at 16 bits, the
+// paged cache's block records); otherwise the reference's packed rows.
+template <bool VP>
 __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArgs a) {
   using namespace s3;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1068,28 +1071,47 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
 #pragma unroll
     for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
     {
-      const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + vword;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const int ta = 16 * ks + 2 * tig;
-        uint32_t L[4], H[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t = ta + (u & 1) + 8 * (u >> 1);  // ta, ta+1, ta+8, ta+9
-          const uint32_t w0 = vw[12 * t], w1 = vw[12 * t + 1];
-          L[u] = prmt(w0, w1, selL);
-          H[u] = prmt(w0, w1, selH);
-        }
+        // P[pr][k]: window k of this lane's field for tokens 16ks + 2tig + 8pr (low half) and
+        // the token after it (high half)
         uint32_t P[2][6];
+        if constexpr (VP) {
+          // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k], so both tokens'
+          // windows come from the same three words (conflict-free: banks 24 tig + 3 g + c)
+          const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
 #pragma unroll
-        for (int pr = 0; pr < 2; ++pr) {
-          const int x = 2 * pr, y = 2 * pr + 1;
-          P[pr][0] = prmt(L[x], L[y], vsel(0));
-          P[pr][1] = prmt(L[x], L[y], vsel(1));
-          P[pr][2] = prmt(L[x], L[y], vsel(2));
-          P[pr][3] = prmt(H[x], H[y], vsel(3));
-          P[pr][4] = prmt(H[x], H[y], vsel(4));
-          P[pr][5] = prmt(H[x], H[y], vsel(5));
+          for (int pr = 0; pr < 2; ++pr) {
+            const int j = 8 * ks + tig + 4 * pr;
+            const uint32_t w0 = vw[24 * j], w1 = vw[24 * j + 1], w2 = vw[24 * j + 2];
+            P[pr][0] = w0;
+            P[pr][1] = prmt(w0, w1, 0x6341u);
+            P[pr][2] = w1;
+            P[pr][3] = prmt(w1, w2, 0x6341u);
+            P[pr][4] = w2;
+            P[pr][5] = prmt(w2, w2, 0x3311u);
+          }
+        } else {
+          const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + vword;
+          const int ta = 16 * ks + 2 * tig;
+          uint32_t L[4], H[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int t = ta + (u & 1) + 8 * (u >> 1);  // ta, ta+1, ta+8, ta+9
+            const uint32_t w0 = vw[12 * t], w1 = vw[12 * t + 1];
+            L[u] = prmt(w0, w1, selL);
+            H[u] = prmt(w0, w1, selH);
+          }
+#pragma unroll
+          for (int pr = 0; pr < 2; ++pr) {
+            const int x = 2 * pr, y = 2 * pr + 1;
+            P[pr][0] = prmt(L[x], L[y], vsel(0));
+            P[pr][1] = prmt(L[x], L[y], vsel(1));
+            P[pr][2] = prmt(L[x], L[y], vsel(2));
+            P[pr][3] = prmt(H[x], H[y], vsel(3));
+            P[pr][4] = prmt(H[x], H[y], vsel(4));
+            P[pr][5] = prmt(H[x], H[y], vsel(5));
+          }
         }
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
@@ -1271,7 +1293,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
                             const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min,
                             const uint16_t *v_scale, const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
-                            int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
+                            int v_paired, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
                             int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
                             void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
                             const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new,
@@ -1296,6 +1318,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   if (batch > 65535 || h > 65535) return NSNKV_ERR_ARG;
   const int64_t cb = code_bytes(bits);
   if (blk_bytes != 0 && (blk_bytes < cb || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
+  if (v_paired != 0 && v_paired != 1) return NSNKV_ERR_ARG;
 
   AttnArgs a{};
   a.cs = blk_bytes ? blk_bytes : cb;
@@ -1342,13 +1365,16 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   const int G = hq / h;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = NSNKV_OK;
-  if (k_alpha && v_alpha && bits == 3 && dtype == NSNKV_F16 && G <= 4 && max_blocks > 0) {
+  const bool sealed_path = k_alpha && v_alpha && bits == 3 && dtype == NSNKV_F16 && G <= 4;
+  if (v_paired && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // paired rows: tensor-core kernel only
+  if (sealed_path && max_blocks > 0) {
     // sealed chunks on the tensor-core kernel, native-row chunks on attn_partial_kernel
     if (!aligned16(k_alpha) || !aligned16(v_alpha)) return NSNKV_ERR_ARG;
     a.ka = k_alpha;
     a.va = v_alpha;
     const size_t smem = sizeof(s3::SSmem);
-    if (cudaFuncSetAttribute(attn_sealed3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    const auto kern = v_paired ? attn_sealed3_kernel<true> : attn_sealed3_kernel<false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return NSNKV_ERR_CUDA;
     // whole chunks of up to 32 blocks (8 per warp) amortise the per-CTA set-up; fewer chunks
     // than nsnkv_decode_attn_workspace_bytes() sized for, so the same workspace holds them
@@ -1368,7 +1394,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, attn_sealed3_kernel, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
+      if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
     }
     if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
     if (any_tail) {  // native-row chunks, overlapping the sealed grid's last wave
@@ -1414,7 +1440,7 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
                       float *out_f32, float *lse, void *workspace, int64_t workspace_bytes, int32_t *status,
                       void *stream) {
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, nullptr, nullptr, 0, blk_stride_head, blk_stride_page, block_table, table_stride,
+                          v_scale, nullptr, nullptr, 0, 0, blk_stride_head, blk_stride_page, block_table, table_stride,
                           n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                           tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
                           workspace_bytes, status, stream);
@@ -1424,20 +1450,19 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
-                            const float *v_alpha, int64_t blk_bytes, int64_t blk_stride_head, int64_t blk_stride_page,
-                            const int32_t *block_table, int64_t table_stride, const int32_t *n_blocks,
-                            int32_t n_blocks_const, int32_t max_blocks, void *k_tail, void *v_tail,
-                            int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
+                            const float *v_alpha, int64_t blk_bytes, int v_paired, int64_t blk_stride_head,
+                            int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
+                            const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail,
+                            void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
                             int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new,
                             void *out, float *out_f32, float *lse, void *workspace, int64_t workspace_bytes,
                             int32_t *status, void *stream) {
   if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, k_alpha, v_alpha, blk_bytes, blk_stride_head, blk_stride_page, block_table,
-                          table_stride,
-                          n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
-                          tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
-                          workspace_bytes, status, stream);
+                          v_scale, k_alpha, v_alpha, blk_bytes, v_paired, blk_stride_head, blk_stride_page,
+                          block_table, table_stride, n_blocks, n_blocks_const, max_blocks, k_tail, v_tail,
+                          tail_stride_seq, tail_stride_head, tail_len, tail_len_const, max_tail, k_new, v_new, out,
+                          out_f32, lse, workspace, workspace_bytes, status, stream);
 }
 
 static int merge_shards_launch(int n_shards, int64_t rows, const float *o, int64_t o_stride, const float *lse,

@@ -66,7 +66,7 @@ __device__ __forceinline__ void pack_block(BlockSmem &s) {
 // Encode the block held in s.x.  Outputs go to global memory (any may be null).
 // Mirrors nsn_encode (loop_kv_nb06_primitives.py:37-55) step for step.
 template <int BITS>
-__device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uint8_t *q_out,
+__device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, bool paired, uint8_t *q_out,
                                uint16_t *norm, uint16_t *mn, uint16_t *scale, int32_t *status, int in_status) {
   const int tid = threadIdx.x;
   constexpr float kLevels = static_cast<float>((1 << BITS) - 1);
@@ -119,8 +119,17 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, uin
   if (codes) {
     pack_block<BITS>(s);
     __syncthreads();
-    for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
-      reinterpret_cast<uint4 *>(codes)[k] = reinterpret_cast<const uint4 *>(s.packed)[k];
+    if (paired) {  // word j*8*BITS + k = [row 2j half k | row 2j+1 half k]
+      const uint16_t *h16 = reinterpret_cast<const uint16_t *>(s.packed);
+      for (int w = tid; w < code_bytes(BITS) / 4; w += blockDim.x) {
+        const int j = w / (8 * BITS), k = w % (8 * BITS);
+        reinterpret_cast<uint32_t *>(codes)[w] =
+            h16[2 * j * 8 * BITS + k] | (static_cast<uint32_t>(h16[(2 * j + 1) * 8 * BITS + k]) << 16);
+      }
+    } else {
+      for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
+        reinterpret_cast<uint4 *>(codes)[k] = reinterpret_cast<const uint4 *>(s.packed)[k];
+    }
   }
   if (st) set_status(status, st);
 }
@@ -228,7 +237,8 @@ __device__ __forceinline__ void stage_block(const __half *src, FastSmem &s) {
 }
 
 template <int BITS>
-__device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
+__device__ void encode_block_fast(const __half *src, uint8_t *codes, bool paired, uint8_t *q_out, uint16_t *norm,
+                                  uint16_t *mn,
                                   uint16_t *scale, int32_t *status, FastSmem &s) {
   const int t = threadIdx.x;
   constexpr uint32_t kL = (1u << BITS) - 1u;
@@ -366,9 +376,22 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, uint8_t *q_
       const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
       uint32_t out[BITS];
       pack32<BITS>(w, out);
-      uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + BITS * t;
+      if (paired) {
+        // thread t holds words BITS*(t&3).. of row t>>2; thread t^4 the same words of the other row
+        // of the pair.  Pair word j*8*BITS + k = [row 2j half k | row 2j+1 half k]: the even row's
+        // thread writes the even k, the odd row's thread the odd k.
+        const bool odd = (t >> 2) & 1;
+        uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + (t >> 3) * 8 * BITS + 2 * BITS * (t & 3) + (odd ? 1 : 0);
 #pragma unroll
-      for (int i = 0; i < BITS; ++i) dst[i] = out[i];
+        for (int i = 0; i < BITS; ++i) {
+          const uint32_t other = __shfl_xor_sync(0xffffffffu, out[i], 4);
+          dst[2 * i] = odd ? __byte_perm(other, out[i], 0x7632) : __byte_perm(out[i], other, 0x5410);
+        }
+      } else {
+        uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + BITS * t;
+#pragma unroll
+        for (int i = 0; i < BITS; ++i) dst[i] = out[i];
+      }
     }
   }
   if (st) set_status(status, st);
@@ -392,7 +415,7 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
                                                             uint8_t *codes, uint8_t *q_out, uint16_t *norm,
                                                             uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                             int64_t header_start, int64_t out_row_stride,
-                                                            int64_t out_offset, int64_t cs, int64_t ms,
+                                                            int64_t out_offset, int64_t cs, int64_t ms, int paired,
                                                             int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
@@ -401,7 +424,8 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
   const int64_t o = r * out_row_stride + out_offset + i;
   int st = load_block<T>(x + b * kBlock * kDim, s);
   __syncthreads();
-  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * cs : nullptr, q_out ? q_out + b * kBlock * kDim : nullptr,
+  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * cs : nullptr, paired != 0,
+                       q_out ? q_out + b * kBlock * kDim : nullptr,
                        norm + o * kBlock, blk_ptr(mn, o, ms), blk_ptr(scale, o, ms), status, st);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
 }
@@ -412,13 +436,13 @@ __global__ void __launch_bounds__(256, 4) encode_blocks_fast_kernel(const __half
                                                                    uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                                    int64_t header_start, int64_t out_row_stride,
                                                                    int64_t out_offset, int64_t cs, int64_t ms,
-                                                                   int32_t *status) {
+                                                                   int paired, int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
   const int64_t b = blockIdx.x;
   const int64_t r = b / blocks_per_row, i = b % blocks_per_row;
   const int64_t o = r * out_row_stride + out_offset + i;
-  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * cs : nullptr,
+  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * cs : nullptr, paired != 0,
                           q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, blk_ptr(mn, o, ms),
                           blk_ptr(scale, o, ms), status, s);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
@@ -542,8 +566,8 @@ __global__ void unpack_kernel(const uint8_t *payload, int64_t count, int bits, u
 
 // ----------------------------------------------------------------- paged-cache seal
 template <int BITS>
-__device__ void renorm_block(const uint8_t *codes, const uint16_t *norm, const uint16_t *mn, const uint16_t *sc,
-                             float *alpha);
+__device__ void renorm_block(const uint8_t *codes, bool paired, const uint16_t *norm, const uint16_t *mn,
+                             const uint16_t *sc, float *alpha);
 
 // One CTA per (kv head, K|V, sequence).  A sequence whose tail holds 64 tokens has that
 // tail encoded into its next page, and with k_alpha the page's renorm factors written
@@ -557,7 +581,8 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
                                                    uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                                    uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
                                                    uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done,
-                                                   int64_t sh, int64_t sp, int64_t cs, int64_t ms, int32_t *status) {
+                                                   int64_t sh, int64_t sp, int64_t cs, int64_t ms, int v_paired,
+                                                   int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // launched with a programmatic dependency: wait for the kernel before it, then let the
   // next one (the following decode step) launch while this grid runs
@@ -576,17 +601,19 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
     uint16_t *nrm = (kv == 0 ? k_norm : v_norm) + blk * kBlock;
     uint16_t *mn = blk_ptr(kv == 0 ? k_min : v_min, blk, ms);
     uint16_t *sc = blk_ptr(kv == 0 ? k_scale : v_scale, blk, ms);
+    const bool paired = kv == 1 && v_paired != 0;
     if constexpr (std::is_same<T, __half>::value) {
-      encode_block_fast<BITS>(src, codes, nullptr, nrm, mn, sc, status, *reinterpret_cast<FastSmem *>(smem_raw));
+      encode_block_fast<BITS>(src, codes, paired, nullptr, nrm, mn, sc, status,
+                              *reinterpret_cast<FastSmem *>(smem_raw));
     } else {
       BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
       int st = load_block<T>(src, s);
       __syncthreads();
-      encode_in_smem<BITS>(s, 0, codes, nullptr, nrm, mn, sc, status, st);
+      encode_in_smem<BITS>(s, 0, codes, paired, nullptr, nrm, mn, sc, status, st);
     }
     if (k_alpha) {
       __syncthreads();  // this CTA's code and metadata stores are visible to all its threads
-      renorm_block<BITS>(codes, nrm, mn, sc, blk_ptr(kv == 0 ? k_alpha : v_alpha, blk, ms));
+      renorm_block<BITS>(codes, paired, nrm, mn, sc, blk_ptr(kv == 0 ? k_alpha : v_alpha, blk, ms));
     }
   }
   if (done) {
@@ -622,16 +649,17 @@ __global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_
 // each block does not recompute ||d|| on every step.  One 256-thread CTA per block:
 // thread (t = tid / 4, quarter) sums 32 channels of token t.
 template <int BITS>
-__device__ void renorm_block(const uint8_t *codes, const uint16_t *norm, const uint16_t *mn, const uint16_t *sc,
-                             float *alpha) {
+__device__ void renorm_block(const uint8_t *codes, bool paired, const uint16_t *norm, const uint16_t *mn,
+                             const uint16_t *sc, float *alpha) {
   const int t = threadIdx.x >> 2, part = threadIdx.x & 3;
-  constexpr int total = code_bytes(BITS);
+  constexpr int row_bytes = kDim * BITS / 8;
   float ss = 0.f;
   for (int c = 32 * part; c < 32 * part + 32; ++c) {
-    const int bit = (t * kDim + c) * BITS;
+    const int bit = c * BITS;  // within token t's packed row
     const int byte = bit >> 3, sh = bit & 7;
-    uint32_t w = codes[byte];
-    if (sh + BITS > 8 && byte + 1 < total) w |= static_cast<uint32_t>(codes[byte + 1]) << 8;
+    uint32_t w = codes[code_byte_at(t, byte, BITS, paired)];
+    if (sh + BITS > 8 && byte + 1 < row_bytes)
+      w |= static_cast<uint32_t>(codes[code_byte_at(t, byte + 1, BITS, paired)]) << 8;
     const float x = static_cast<float>((w >> sh) & ((1u << BITS) - 1u));
     const float d = __fadd_rn(half_bits_to_f(mn[c]), __fmul_rn(half_bits_to_f(sc[c]), x));
     ss = __fmaf_rn(d, d, ss);
@@ -650,11 +678,12 @@ template <int BITS>
 __global__ void __launch_bounds__(256) renorm_blocks_kernel(const uint8_t *codes, const uint16_t *norm,
                                                             const uint16_t *mn, const uint16_t *sc,
                                                             int64_t blocks_per_row, int64_t row_stride,
-                                                            int64_t offset, float *alpha, int64_t cs, int64_t ms) {
+                                                            int64_t offset, float *alpha, int64_t cs, int64_t ms,
+                                                            int paired) {
   const int64_t r = blockIdx.x / blocks_per_row, i = blockIdx.x % blocks_per_row;
   const int64_t blk = r * row_stride + offset + i;
-  renorm_block<BITS>(codes + blk * cs, norm + blk * kBlock, blk_ptr(mn, blk, ms), blk_ptr(sc, blk, ms),
-                     blk_ptr(alpha, blk, ms));
+  renorm_block<BITS>(codes + blk * cs, paired != 0, norm + blk * kBlock, blk_ptr(mn, blk, ms),
+                     blk_ptr(sc, blk, ms), blk_ptr(alpha, blk, ms));
 }
 
 // ----------------------------------------------------------------- host dispatch
@@ -662,7 +691,7 @@ template <typename T>
 static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits, int norm_order, uint8_t *codes,
                          uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale, uint8_t *headers,
                          int64_t header_start, int64_t out_row_stride, int64_t out_offset, int64_t cs, int64_t ms,
-                         int32_t *status, cudaStream_t st) {
+                         int paired, int32_t *status, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>(n_blocks));
   if (std::is_same<T, __half>::value && norm_order == 0) {
     const size_t smem = sizeof(FastSmem);
@@ -672,7 +701,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
       return NSNKV_ERR_CUDA;                                                                               \
     k<<<grid, 256, smem, st>>>(static_cast<const __half *>(x), bpr, codes, q_out, norm, mn, scale, headers, \
-                               header_start, out_row_stride, out_offset, cs, ms, status);                  \
+                               header_start, out_row_stride, out_offset, cs, ms, paired, status);          \
     break;                                                                                                 \
   }
     switch (bits) {
@@ -692,7 +721,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)       \
       return NSNKV_ERR_CUDA;                                                                              \
     k<<<grid, 256, smem, st>>>(static_cast<const T *>(x), norm_order, bpr, codes, q_out, norm, mn, scale, \
-                               headers, header_start, out_row_stride, out_offset, cs, ms, status);        \
+                               headers, header_start, out_row_stride, out_offset, cs, ms, paired, status); \
     break;                                                                                                \
   }
   switch (bits) {
@@ -747,7 +776,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
                        uint16_t *vm, uint16_t *vs, float *ka, float *va, int32_t *done, int64_t sh, int64_t sp,
-                       int64_t cs, int64_t ms, int32_t *status, cudaStream_t st) {
+                       int64_t cs, int64_t ms, int v_paired, int32_t *status, cudaStream_t st) {
   const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
@@ -767,7 +796,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     cfg.numAttrs = 1;                                                                                      \
     if (cudaLaunchKernelEx(&cfg, k, static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss,   \
                            tsh, tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
-                           va, done, sh, sp, cs, ms, status) != cudaSuccess)                               \
+                           va, done, sh, sp, cs, ms, v_paired, status) != cudaSuccess)                     \
       return NSNKV_ERR_LAUNCH;                                                                             \
     break;                                                                                                 \
   }
@@ -797,9 +826,10 @@ int64_t nsnkv_block_code_bytes(int bits) { return (bits >= 3 && bits <= 5) ? cod
 int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits,
                                 int norm_order, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
                                 uint16_t *scale, uint8_t *headers, int64_t header_start, int64_t out_row_stride,
-                                int64_t out_offset, int64_t blk_bytes, int32_t *status, void *stream) {
+                                int64_t out_offset, int64_t blk_bytes, int paired, int32_t *status, void *stream) {
   if (rows < 0 || blocks_per_row < 0 || bits < 3 || bits > 5 || (norm_order != 0 && norm_order != 1))
     return NSNKV_ERR_ARG;
+  if (paired != 0 && paired != 1) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   const int64_t n_blocks = rows * blocks_per_row;
@@ -811,13 +841,13 @@ int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_
   switch (x_dtype) {
     case NSNKV_F16:
       return launch_encode<__half>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                   headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
+                                   headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
     case NSNKV_BF16:
       return launch_encode<__nv_bfloat16>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn,
-                                          scale, headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
+                                          scale, headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
     case NSNKV_F32:
       return launch_encode<float>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                  headers, header_start, out_row_stride, out_offset, cs, ms, status, st);
+                                  headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -828,7 +858,7 @@ int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks
                         uint8_t *headers, int64_t header_start, int64_t out_row_stride, int64_t out_offset,
                         int32_t *status, void *stream) {
   return nsnkv_encode_blocks_strided(x, x_dtype, rows, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                     headers, header_start, out_row_stride, out_offset, 0, status, stream);
+                                     headers, header_start, out_row_stride, out_offset, 0, 0, status, stream);
 }
 
 int nsnkv_restore(const uint8_t *codes, int codes_unpacked, const uint16_t *norm, const uint16_t *mn,
@@ -878,8 +908,9 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
                      int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks, int pending_append,
                      const int32_t *block_table, int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm,
                      uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int32_t *done,
+                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int v_paired, int32_t *done,
                      int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream) {
+  if (v_paired != 0 && v_paired != 1) return NSNKV_ERR_ARG;
   if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
@@ -895,12 +926,12 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
       return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
                                  n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
                                  k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, done, blk_stride_head,
-                                 blk_stride_page, cs, ms, status, st);
+                                 blk_stride_page, cs, ms, v_paired, status, st);
     case NSNKV_BF16:
       return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                                         tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
                                         k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha,
-                                        done, blk_stride_head, blk_stride_page, cs, ms, status, st);
+                                        done, blk_stride_head, blk_stride_page, cs, ms, v_paired, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -914,7 +945,7 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype, void *k_tai
                           int32_t *status, void *stream) {
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, nullptr, nullptr, 0, nullptr, blk_stride_head, blk_stride_page, status, stream);
+                   v_min, v_scale, nullptr, nullptr, 0, 0, nullptr, blk_stride_head, blk_stride_page, status, stream);
 }
 
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void *k_tail, void *v_tail,
@@ -922,20 +953,21 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void 
                                 int32_t *n_blocks, int pending_append, const int32_t *block_table,
                                 int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min,
                                 uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes,
+                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int v_paired,
                                 int32_t *seq_counters, int64_t blk_stride_head, int64_t blk_stride_page,
                                 int32_t *status, void *stream) {
   if (!k_alpha || !v_alpha) return NSNKV_ERR_ARG;
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, k_alpha, v_alpha, blk_bytes, seq_counters, blk_stride_head, blk_stride_page,
-                   status, stream);
+                   v_min, v_scale, k_alpha, v_alpha, blk_bytes, v_paired, seq_counters, blk_stride_head,
+                   blk_stride_page, status, stream);
 }
 
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
                        const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
-                       int64_t blk_bytes, void *stream) {
+                       int64_t blk_bytes, int paired, void *stream) {
   if (bits < 3 || bits > 5 || rows < 0 || blocks_per_row < 0 || offset < 0) return NSNKV_ERR_ARG;
+  if (paired != 0 && paired != 1) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   if (rows == 0 || blocks_per_row == 0) return NSNKV_OK;
@@ -946,15 +978,15 @@ int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uin
   switch (bits) {
     case 3:
       renorm_blocks_kernel<3><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms);
+                                                     alpha, cs, ms, paired);
       break;
     case 4:
       renorm_blocks_kernel<4><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms);
+                                                     alpha, cs, ms, paired);
       break;
     default:
       renorm_blocks_kernel<5><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms);
+                                                     alpha, cs, ms, paired);
       break;
   }
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;

@@ -16,6 +16,13 @@ constexpr float kEps = 1e-12f;
 constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128)
 
 __host__ __device__ constexpr int code_bytes(int bits) { return kBlock * kDim * bits / 8; }
+// Byte b of token t's packed code row inside a block.  Dense: rows back to back.  Paired
+// (the V codes of the paged cache's block records): the rows of tokens 2j and 2j+1
+// interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j half k | row 2j+1 half k].
+__host__ __device__ __forceinline__ int code_byte_at(int t, int b, int bits, bool paired) {
+  return paired ? 4 * ((t >> 1) * 8 * bits + (b >> 1)) + 2 * (t & 1) + (b & 1) : t * 16 * bits + b;
+}
+
 // Block i of an array whose blocks are `bytes` apart (a dense array, or one field of the
 // paged cache's block records).
 template <typename T>

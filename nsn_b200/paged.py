@@ -123,7 +123,9 @@ def block_record_pools(h: int, pages: int, bits: int, device):
     (64 fp32), then the same four fields for V (7680 bytes for INT3).  The pool dicts
     hold views of those fields, so every operator that takes a pool writes or reads the
     records; norms [h, pages, 64] fp16 stay dense.  nsnkv_decode_attn_alpha moves each
-    block with one copy when given these pools (blk_bytes = the record size).
+    block with one copy when given these pools (blk_bytes = the record size).  The V
+    codes are paired rows (``pool["paired"]``, see primitives.pair_rows): the order the
+    tensor-core kernel reads cheapest; exports and imports convert.
     """
     cb = w.code_bytes(bits)
     half = cb + 2 * w.DIM * 2 + w.BLOCK * 4
@@ -136,7 +138,9 @@ def block_record_pools(h: int, pages: int, bits: int, device):
                     scale=rec[..., off + cb + 2 * w.DIM:off + cb + 4 * w.DIM].view(torch.float16),
                     alpha=rec[..., off + cb + 4 * w.DIM:off + half].view(torch.float32))
 
-    return rec, fields(0), fields(half)
+    vp = fields(half)
+    vp["paired"] = True  # V codes as paired rows (primitives.pair_rows)
+    return rec, fields(0), vp
 
 
 class PagedKVCache:
@@ -219,7 +223,10 @@ class PagedKVCache:
         def group(pool):
             if nb == 0:
                 return None
-            return dict(codes=pool["codes"][:, pages].unsqueeze(0).contiguous(),
+            codes = pool["codes"][:, pages]
+            if pool.get("paired"):
+                codes = w.unpair_rows(codes, self.bits)
+            return dict(codes=codes.unsqueeze(0).contiguous(),
                         metas=(pool["norm"][:, pages].reshape(1, h, nb, w.BLOCK, 1).contiguous(),
                                pool["min"][:, pages].reshape(1, h, nb, 1, w.DIM).contiguous(),
                                pool["scale"][:, pages].reshape(1, h, nb, 1, w.DIM).contiguous()),
@@ -249,7 +256,8 @@ class PagedKVCache:
         for g, pool in ((kg, self.k_pool), (vg, self.v_pool)):
             if g is None:
                 continue
-            pool["codes"][:, pages] = g["codes"][0].to(self.device)
+            codes = g["codes"][0].to(self.device)
+            pool["codes"][:, pages] = w.pair_rows(codes, self.bits) if pool.get("paired") else codes
             pool["norm"][:, pages] = g["metas"][0].reshape(h, n, w.BLOCK).to(self.device)
             pool["min"][:, pages] = g["metas"][1].reshape(h, n, w.DIM).to(self.device)
             pool["scale"][:, pages] = g["metas"][2].reshape(h, n, w.DIM).to(self.device)
@@ -308,7 +316,8 @@ class PagedKVCache:
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
             L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
-            L.ptr(self.v_pool["alpha"]), self.blk_bytes, L.ptr(self.seal_counters), self.pages, 1,
+            L.ptr(self.v_pool["alpha"]), self.blk_bytes, int(bool(self.v_pool.get("paired"))),
+            L.ptr(self.seal_counters), self.pages, 1,
             L.ptr(self.status), L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")
 

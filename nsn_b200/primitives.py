@@ -152,7 +152,8 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
     if nblk:
         L.check(L.load().nsnkv_encode_blocks_strided(
             L.ptr(xc), L.DTYPE_CODE[x.dtype], rows, bpr, bits, order, L.ptr(codes), L.ptr(q), L.ptr(n), L.ptr(m),
-            L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, blk, L.ptr(status), L.stream_handle(dev)),
+            L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, blk,
+            int(bool(out is not None and out.get("paired"))), L.ptr(status), L.stream_handle(dev)),
             "nsnkv_encode_blocks")
         if out is not None and out.get("alpha") is not None and codes is not None:
             block_renorm(out, bits, rows, bpr, stride, offset)
@@ -163,6 +164,27 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
         res["status"] = status
     res.update(codes=codes, q=q, metas=(n, m, s), headers=hdr)
     return res
+
+
+def pair_rows(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Packed blocks [..., code_bytes] in the reference's row order -> paired rows.
+
+    Paired rows (the V codes of the paged cache's block records): the packed rows of
+    tokens 2j and 2j+1 interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j
+    half k | row 2j+1 half k].  The same bytes in another order.
+    """
+    lead = tuple(codes.shape[:-1])
+    require(codes.dtype == torch.uint8 and codes.shape[-1] == code_bytes(bits), "packed block shape")
+    h = codes.contiguous().view(torch.int16).reshape(lead + (BLOCK // 2, 2, 8 * bits))
+    return h.transpose(-1, -2).contiguous().view(torch.uint8).reshape(lead + (code_bytes(bits),))
+
+
+def unpair_rows(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Inverse of pair_rows: paired rows -> the reference's packed row order."""
+    lead = tuple(codes.shape[:-1])
+    require(codes.dtype == torch.uint8 and codes.shape[-1] == code_bytes(bits), "packed block shape")
+    h = codes.contiguous().view(torch.int16).reshape(lead + (BLOCK // 2, 8 * bits, 2))
+    return h.transpose(-1, -2).contiguous().view(torch.uint8).reshape(lead + (code_bytes(bits),))
 
 
 def blk_bytes_of(pool, bits: int) -> int:
@@ -212,7 +234,7 @@ def block_renorm(pool, bits: int, rows: int, blocks_per_row: int, row_stride: in
         L.check(L.load().nsnkv_block_renorm(
             bits, rows, blocks_per_row, L.ptr(pool["codes"]), L.ptr(pool["norm"]), L.ptr(pool["min"]),
             L.ptr(pool["scale"]), row_stride, offset, L.ptr(pool["alpha"]), blk_bytes_of(pool, bits),
-            L.stream_handle(pool["codes"].device)),
+            int(bool(pool.get("paired"))), L.stream_handle(pool["codes"].device)),
             "nsnkv_block_renorm")
 
 

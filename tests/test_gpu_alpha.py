@@ -184,7 +184,9 @@ def test_alpha_path_agrees_with_restore_path():
     cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=31)
     qt = torch.from_numpy(q).cuda()
     fast = cache.attend(qt).float().cpu().numpy()
-    pools = [{k: p[k] for k in ("codes", "norm", "min", "scale")} for p in (cache.k_pool, cache.v_pool)]
+    # the restore path reads the reference's code order: dense copies, V rows unpaired
+    pools = [{k: p[k].contiguous() for k in ("codes", "norm", "min", "scale")} for p in (cache.k_pool, cache.v_pool)]
+    pools[1]["codes"] = w.unpair_rows(pools[1]["codes"], 3)
     slow, st = decode_attention(
         qt, pools[0], pools[1], h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1,
         n_blocks=cache.n_blocks, max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
@@ -268,28 +270,54 @@ def test_alpha_path_flags_nonfinite_metadata(where):
 
 
 def test_block_records_match_dense_arrays():
-    """The cache's block records (one copy per block) and dense copies of the same arrays
-    (eight copies per block) give bit-identical attention, on both entry points."""
+    """The cache's block records (one copy per block, V codes as paired rows) and dense
+    copies of the same arrays in the reference's order (eight copies per block) give
+    bit-identical attention; so do records with unpaired V codes on the restore path."""
     from nsn_b200.kernel import decode_attention
     from nsn_b200 import primitives as w
     rng = np.random.default_rng(21)
     lens = [64 * 40 + 9, 64 * 3, 64 * 77 + 63, 5]
     cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=80)
-    assert cache.blk_bytes == 7680 and w.blk_bytes_of(cache.k_pool, 3) == 7680
+    assert cache.blk_bytes == 7680 and w.blk_bytes_of(cache.k_pool, 3) == 7680 and cache.v_pool["paired"]
     qt = torch.from_numpy(q).cuda()
     common = dict(h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1, n_blocks=cache.n_blocks,
                   max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
                   tail_stride_seq=cache.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=cache.tail_len,
                   max_tail=w.BLOCK - 1, block_table=cache.block_table)
-    for keys in (("codes", "norm", "min", "scale", "alpha"), ("codes", "norm", "min", "scale")):
-        rec = [{k: p[k] for k in keys} for p in (cache.k_pool, cache.v_pool)]
-        dense = [{k: p[k].contiguous() for k in keys} for p in (cache.k_pool, cache.v_pool)]
-        assert w.blk_bytes_of(dense[0], 3) == 0
-        a, sa = decode_attention(qt, rec[0], rec[1], **common)
-        b, sb = decode_attention(qt, dense[0], dense[1], **common)
-        torch.cuda.synchronize()
-        assert int(sa.item()) == 0 and int(sb.item()) == 0
-        assert torch.equal(a, b), keys
+
+    def dense_of(keys):
+        d = [{k: p[k].contiguous() for k in keys} for p in (cache.k_pool, cache.v_pool)]
+        d[1]["codes"] = w.unpair_rows(d[1]["codes"], 3)
+        return d
+
+    # renorm-factor path: records with paired V rows against dense arrays
+    keys = ("codes", "norm", "min", "scale", "alpha")
+    dense = dense_of(keys)
+    assert w.blk_bytes_of(dense[0], 3) == 0
+    a, sa = decode_attention(qt, cache.k_pool, cache.v_pool, **common)
+    b, sb = decode_attention(qt, dense[0], dense[1], **common)
+    torch.cuda.synchronize()
+    assert int(sa.item()) == 0 and int(sb.item()) == 0
+    assert torch.equal(a, b)
+    # restore path: the same record strides with V rows back in the reference's order
+    from nsn_b200.paged import block_record_pools
+    rec, kp, vp = block_record_pools(cache.h, cache.pages, 3, "cuda")
+    rec.copy_(cache.records)
+    vp["codes"].copy_(w.unpair_rows(vp["codes"], 3))
+    del vp["paired"]
+    keys = ("codes", "norm", "min", "scale")
+    for p_, src in ((kp, cache.k_pool), (vp, cache.v_pool)):
+        p_["norm"].copy_(src["norm"])
+    dense = dense_of(keys)
+    a, sa = decode_attention(qt, {k: kp[k] for k in keys}, {k: vp[k] for k in keys}, **common)
+    b, sb = decode_attention(qt, dense[0], dense[1], **common)
+    torch.cuda.synchronize()
+    assert int(sa.item()) == 0 and int(sb.item()) == 0
+    assert torch.equal(a, b)
+    # paired V rows without factors have no kernel
+    with pytest.raises(w.ContractError):
+        decode_attention(qt, {k: cache.k_pool[k] for k in keys}, dict({k: cache.v_pool[k] for k in keys}, paired=True),
+                         **common)
 
 
 def test_encode_into_block_records_matches_dense():
@@ -310,3 +338,28 @@ def test_encode_into_block_records_matches_dense():
     for k in ("codes", "norm", "min", "scale", "alpha"):
         assert torch.equal(kp[k][:, 2:8], dense[k]), k
     assert int(rec[:, :2].count_nonzero()) == 0 and int(rec[:, 8:].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("bits", [3, 5])
+def test_paired_rows_encode_and_renorm(bits):
+    """Encoding into a pool flagged paired writes pair_rows of the dense encoder's codes, and
+    nsnkv_block_renorm reading paired rows gives the dense factors (generic and fp16 encoders)."""
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(23 + bits)
+    for dtype in (torch.float16, torch.bfloat16):
+        x = torch.from_numpy(workloads.np_kv(rng, (3, 4, 64, 128), (), 0.5)).cuda().to(dtype)
+        pool = dict(codes=torch.zeros((3, 6, w.code_bytes(bits)), dtype=torch.uint8, device="cuda"),
+                    norm=torch.zeros((3, 6, 64), dtype=torch.float16, device="cuda"),
+                    min=torch.zeros((3, 6, 128), dtype=torch.float16, device="cuda"),
+                    scale=torch.zeros((3, 6, 128), dtype=torch.float16, device="cuda"),
+                    alpha=torch.zeros((3, 6, 64), dtype=torch.float32, device="cuda"), paired=True)
+        w.encode_blocks(x, bits, out=pool, out_row_stride=6, out_offset=1)
+        ref = w.encode_blocks(x, bits)
+        dense = dict(codes=ref["codes"], norm=ref["metas"][0].reshape(3, 4, 64), min=ref["metas"][1].reshape(3, 4, 128),
+                     scale=ref["metas"][2].reshape(3, 4, 128), alpha=torch.zeros((3, 4, 64), device="cuda"))
+        w.block_renorm(dense, bits, 3, 4, 4)
+        torch.cuda.synchronize()
+        assert torch.equal(pool["codes"][:, 1:5], w.pair_rows(dense["codes"], bits)), dtype
+        assert torch.equal(pool["alpha"][:, 1:5], dense["alpha"]), dtype
+        assert torch.equal(w.unpair_rows(pool["codes"][:, 1:5], bits), dense["codes"]), dtype

@@ -105,6 +105,7 @@ def _oracle_step(hist_k, hist_v, q, bits=3):
 
 
 def test_paged_cache_steps_and_seals():
+    from nsn_b200 import primitives as w
     from nsn_b200 import workloads
     from nsn_b200.paged import PagedKVCache
     rng = np.random.default_rng(21)
@@ -142,7 +143,10 @@ def test_paged_cache_steps_and_seals():
             x = hist[b][:, :nb[b] * 64].reshape(1, h, nb[b], 64, 128).astype(np.float32)
             q8, n, m, s_, st = O.nsn_encode(x, 3)
             pages = cache.block_table[b, :nb[b]].long().cpu()
-            got = pool["codes"][:, pages].cpu().numpy().reshape(-1, 3072)
+            codes = pool["codes"][:, pages]
+            if pool.get("paired"):  # the block records keep V codes as paired rows
+                codes = w.unpair_rows(codes, 3)
+            got = codes.cpu().numpy().reshape(-1, 3072)
             want = np.stack([O.pack3(blk) for blk in q8.reshape(-1, 64, 128)])
             assert np.array_equal(got, want), (b, kv)
             assert np.array_equal(bits16(pool["norm"][:, pages]).reshape(-1), n.view(np.uint16).reshape(-1))

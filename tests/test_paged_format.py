@@ -105,3 +105,22 @@ def test_blk_bytes_of_dense_and_rejected_layouts():
     bad = dict(dense, min=torch.zeros((2, 128, 4), dtype=torch.float16).transpose(1, 2))
     with pytest.raises(w.ContractError):
         w.blk_bytes_of(bad, 3)
+
+
+@pytest.mark.parametrize("bits", [3, 4, 5])
+def test_pair_rows_layout_and_round_trip(bits):
+    """Paired rows: word j*8*bits + k = [row 2j half k | row 2j+1 half k]; unpair_rows inverts it."""
+    from nsn_b200 import primitives as w
+    from nsn_b200.paged import block_record_pools
+    rng = np.random.default_rng(bits)
+    cb = w.code_bytes(bits)
+    codes = torch.from_numpy(rng.integers(0, 256, size=(2, 3, cb), dtype=np.uint8))
+    p = w.pair_rows(codes, bits)
+    assert p.shape == codes.shape and torch.equal(w.unpair_rows(p, bits), codes)
+    rows = codes.view(torch.int16).reshape(2, 3, 64, 8 * bits)
+    words = p.view(torch.int32).reshape(2, 3, 32, 8 * bits)
+    j, k = 5, 7
+    want = (rows[..., 2 * j, k].to(torch.int32) & 0xFFFF) | (rows[..., 2 * j + 1, k].to(torch.int32) << 16)
+    assert torch.equal(words[..., j, k], want)
+    _, kp, vp = block_record_pools(1, 2, 3, "cpu")
+    assert vp.get("paired") is True and not kp.get("paired")
