@@ -88,20 +88,25 @@ int nsnkv_encode_blocks(const void *x, int x_dtype, int64_t rows, int64_t blocks
  * blk_bytes = 0 means dense arrays (code_bytes, 256, 256 and 256 bytes per block).
  * Norm arrays are always dense (128 bytes per block).
  *
- * Paired code rows.  In the records the V codes of a block are "paired": the packed
- * rows of tokens 2j and 2j+1 (16*bits bytes each, the reference's LSB-first bitstream)
- * interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j half k | row 2j+1 half k].
- * Same bytes, another order: the tensor-core kernel then reads both tokens of a pair
- * from one word.  Entry points with a paired / v_paired flag (0 or 1) read or write
- * that order; everything else takes the reference's order.
+ * Code orders.  The same packed bytes in three orders (code_order):
+ *   0  the reference's rows back to back (LSB-first bitstream, 16*bits bytes per token);
+ *   1  paired rows, the V codes of the records: the rows of tokens 2j and 2j+1
+ *      interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j half k | row 2j+1 half k];
+ *   2  paired halves, the K codes of the records: in each row, each 32-code group
+ *      (2*bits 16-bit halves: A = the first bits, B = the rest) stored as words
+ *      [A half m | B half m], m < bits.
+ * The tensor-core kernel then reads two codes of one register (two tokens of a channel
+ * for V, two channels of a token for K) from the same word.  The decode and seal entry
+ * points take rec_order (1: K in order 2 and V in order 1, as in the records; 0: both in
+ * order 0); everything without such an argument takes order 0.
  *
  * nsnkv_encode_blocks with block strides: codes, mn and scale are fields of records
- * blk_bytes apart (0: identical to nsnkv_encode_blocks); paired = 1 writes paired rows.
+ * blk_bytes apart (0: identical to nsnkv_encode_blocks); codes written in code_order.
  */
 int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits,
                                 int norm_order, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
                                 uint16_t *scale, uint8_t *headers, int64_t header_start, int64_t out_row_stride,
-                                int64_t out_offset, int64_t blk_bytes, int paired, int32_t *status, void *stream);
+                                int64_t out_offset, int64_t blk_bytes, int code_order, int32_t *status, void *stream);
 
 /*
  * Reconstruct rows of sealed blocks followed by an optional native tail.
@@ -177,8 +182,9 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
  *                      k_scale = k_codes + CB + 256, k_alpha = k_codes + CB + 512,
  *                      v_codes = k_codes + CB + 768, the same offsets from v_codes, and
  *                      blk_bytes = 2 * (CB + 768)), a block moves in one copy.
- *   v_paired           1: the V codes are paired rows (the records' order); only the
- *                      tensor-core path reads them (NSNKV_ERR_UNSUPPORTED otherwise).
+ *   rec_order          1: K and V codes in the records' orders (K paired halves, V paired
+ *                      rows); only the tensor-core path reads them (NSNKV_ERR_UNSUPPORTED
+ *                      otherwise).
  * INT3 fp16 caches with hq / h <= 4 then run the sealed blocks on the tensor cores
  * without restoring any K or V value (the codes are the MMA operands); the norms are
  * not read.  Other shapes take the nsnkv_decode_attn path.  The result matches
@@ -189,7 +195,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale,
-                            const float *k_alpha, const float *v_alpha, int64_t blk_bytes, int v_paired,
+                            const float *k_alpha, const float *v_alpha, int64_t blk_bytes, int rec_order,
                             int64_t blk_stride_head, int64_t blk_stride_page,
                             const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
@@ -203,11 +209,11 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
  * Per-token renorm factors of sealed blocks (see nsnkv_decode_attn_alpha), for the
  * blocks nsnkv_encode_blocks lays out: block (row r, i) of rows x blocks_per_row has
  * index r*row_stride + offset + i in codes / norm / min / scale / alpha; blk_bytes is
- * the block stride of codes / min / scale / alpha (0: dense); paired = 1 reads paired rows.
+ * the block stride of codes / min / scale / alpha (0: dense); codes read in code_order.
  */
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
                        const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
-                       int64_t blk_bytes, int paired, void *stream);
+                       int64_t blk_bytes, int code_order, void *stream);
 
 /* Workspace bytes nsnkv_decode_attn needs for these sizes. */
 int64_t nsnkv_decode_attn_workspace_bytes(int64_t batch, int hq, int h, int32_t max_blocks, int32_t max_tail);
@@ -271,8 +277,8 @@ int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
  * (int32 [batch], may be NULL) must be zero before the first call and are left zero:
  * with them the last CTA of each sequence advances n_blocks / tail_len, so the call is
  * one launch; without them a second kernel advances the counters.  blk_bytes is the
- * block stride of the codes / min / scale / alpha arrays (0: dense); v_paired = 1 writes
- * the V codes as paired rows.
+ * block stride of the codes / min / scale / alpha arrays (0: dense); rec_order = 1 writes
+ * the codes in the records' orders (K paired halves, V paired rows).
  */
 int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
@@ -280,7 +286,7 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 const int32_t *block_table, int64_t table_stride,
                                 uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                 uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
-                                float *k_alpha, float *v_alpha, int64_t blk_bytes, int v_paired, int32_t *seq_counters,
+                                float *k_alpha, float *v_alpha, int64_t blk_bytes, int rec_order, int32_t *seq_counters,
                                 int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream);
 
 /*

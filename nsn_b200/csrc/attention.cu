@@ -817,9 +817,10 @@ __device__ __forceinline__ uint32_t split_hilo(float w) {
 
 }  // namespace s3
 
-// VP: the V codes are paired rows (token rows 2j and 2j+1 interleaved at 16 bits, the
-// paged cache's block records); otherwise the reference's packed rows.
-template <bool VP>
+// REC: the codes are in the paged cache's block-record orders: K as paired halves (each
+// 32-code group of a row stored as words [A half m | B half m]), V as paired rows (token
+// rows 2j and 2j+1 interleaved at 16 bits).  Otherwise the reference's packed rows.
+template <bool REC>
 __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArgs a) {
   using namespace s3;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -917,7 +918,12 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     for (int r = 0; r < 18; ++r) {
       if ((r & 3) != warp) continue;
       float lo = 0.f, hi = 0.f;
-      if (hb < G) {
+      if (REC) {  // register r: channels 32 tig + r and 32 tig + 16 + r, both at window position vpos(r)
+        if (r < 16 && hb < G) {
+          lo = __half2float(S.qs[hb][32 * tig + r]) * pow2(7 - vpos(r) - kb);
+          hi = __half2float(S.qs[hb][32 * tig + 16 + r]) * pow2(7 - vpos(r) - kb);
+        }
+      } else if (hb < G) {
         if (ktab(r, 1) >= 0) lo = __half2float(S.qs[hb][32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
         if (ktab(r, 3) >= 0) hi = __half2float(S.qs[hb][32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
       }
@@ -961,7 +967,8 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     const SStage &sg = S.u.stage[li % kRing];
 
     // ---- K weights of this block: W[r] = hi (even g) or lo (odd g) of q * scale * 2^(7-pos-kq)
-    uint32_t W[18];
+    constexpr int KR = REC ? 16 : 18;  // K registers per token row of a lane group
+    uint32_t W[KR];
     {
       uint32_t nat[16];
       const uint4 *ksv = reinterpret_cast<const uint4 *>(sg.ks + 32 * tig);
@@ -976,16 +983,21 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       uint32_t qa[20], qz[20];
       const uint4 *rq = reinterpret_cast<const uint4 *>(rec);
 #pragma unroll
-      for (int i = 0; i < 5; ++i) {
+      for (int i = 0; i < (KR + 3) / 4; ++i) {
         const uint4 x = rq[i], y = rq[5 + i];
         qa[4 * i] = x.x, qa[4 * i + 1] = x.y, qa[4 * i + 2] = x.z, qa[4 * i + 3] = x.w;
         qz[4 * i] = y.x, qz[4 * i + 1] = y.y, qz[4 * i + 2] = y.z, qz[4 * i + 3] = y.w;
       }
 #pragma unroll
-      for (int r = 0; r < 18; ++r) {
-        const uint32_t lo_src = ktab(r, 1) >= 0 ? nat[ktab(r, 1) >> 1] : 0u;
-        const uint32_t hi_src = ktab(r, 3) >= 0 ? nat[ktab(r, 3) >> 1] : 0u;
-        const uint32_t b2 = prmt(lo_src, hi_src, ksel(r));
+      for (int r = 0; r < KR; ++r) {
+        uint32_t b2;
+        if constexpr (REC) {  // scales of channels 32 tig + r and 32 tig + 16 + r
+          b2 = prmt(nat[r >> 1], nat[8 + (r >> 1)], (r & 1) ? 0x7632u : 0x5410u);
+        } else {
+          const uint32_t lo_src = ktab(r, 1) >= 0 ? nat[ktab(r, 1) >> 1] : 0u;
+          const uint32_t hi_src = ktab(r, 3) >= 0 ? nat[ktab(r, 3) >> 1] : 0u;
+          b2 = prmt(lo_src, hi_src, ksel(r));
+        }
         W[r] = hfma2u(qz[r], b2, hmul2u(qa[r], b2));
       }
     }
@@ -1015,19 +1027,33 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
           const int m = 2 * half + mm;
           const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
           const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
-          X0[mm][0] = u0, X0[mm][1] = __funnelshift_r(u0, u1, 8), X0[mm][2] = u1;
-          X0[mm][3] = __funnelshift_r(u1, u2, 8), X0[mm][4] = u2, X0[mm][5] = u2 >> 8;
-          X1[mm][0] = v0, X1[mm][1] = __funnelshift_r(v0, v1, 8), X1[mm][2] = v1;
-          X1[mm][3] = __funnelshift_r(v1, v2, 8), X1[mm][4] = v2, X1[mm][5] = v2 >> 8;
+          if constexpr (REC) {  // paired halves: windows of both 48-bit halves of the group at once
+            X0[mm][0] = u0, X0[mm][1] = prmt(u0, u1, 0x6341u), X0[mm][2] = u1;
+            X0[mm][3] = prmt(u1, u2, 0x6341u), X0[mm][4] = u2, X0[mm][5] = prmt(u2, u2, 0x3311u);
+            X1[mm][0] = v0, X1[mm][1] = prmt(v0, v1, 0x6341u), X1[mm][2] = v1;
+            X1[mm][3] = prmt(v1, v2, 0x6341u), X1[mm][4] = v2, X1[mm][5] = prmt(v2, v2, 0x3311u);
+          } else {
+            X0[mm][0] = u0, X0[mm][1] = __funnelshift_r(u0, u1, 8), X0[mm][2] = u1;
+            X0[mm][3] = __funnelshift_r(u1, u2, 8), X0[mm][4] = u2, X0[mm][5] = u2 >> 8;
+            X1[mm][0] = v0, X1[mm][1] = __funnelshift_r(v0, v1, 8), X1[mm][2] = v1;
+            X1[mm][3] = __funnelshift_r(v1, v2, 8), X1[mm][4] = v2, X1[mm][5] = v2 >> 8;
+          }
           sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
         }
 #pragma unroll
-        for (int k = 0; k < 9; ++k)
+        for (int k = 0; k < KR / 2; ++k)
 #pragma unroll
           for (int mm = 0; mm < 2; ++mm) {
             const int r0 = 2 * k, r1 = 2 * k + 1;
-            mma16816<__half>(sc[2 * half + mm], X0[mm][ktab(r0, 0)] & kmask(r0), X1[mm][ktab(r0, 0)] & kmask(r0),
-                             X0[mm][ktab(r1, 0)] & kmask(r1), X1[mm][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+            if constexpr (REC) {
+              constexpr uint32_t seven = 0x00070007u;
+              const uint32_t m0 = seven << vpos(r0), m1 = seven << vpos(r1);
+              mma16816<__half>(sc[2 * half + mm], X0[mm][vwin(r0)] & m0, X1[mm][vwin(r0)] & m0,
+                               X0[mm][vwin(r1)] & m1, X1[mm][vwin(r1)] & m1, W[r0], W[r1]);
+            } else {
+              mma16816<__half>(sc[2 * half + mm], X0[mm][ktab(r0, 0)] & kmask(r0), X1[mm][ktab(r0, 0)] & kmask(r0),
+                               X0[mm][ktab(r1, 0)] & kmask(r1), X1[mm][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+            }
           }
       }
     }
@@ -1076,7 +1102,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
         // P[pr][k]: window k of this lane's field for tokens 16ks + 2tig + 8pr (low half) and
         // the token after it (high half)
         uint32_t P[2][6];
-        if constexpr (VP) {
+        if constexpr (REC) {
           // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k], so both tokens'
           // windows come from the same three words (conflict-free: banks 24 tig + 3 g + c)
           const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
@@ -1293,7 +1319,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
                             const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min,
                             const uint16_t *v_scale, const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
-                            int v_paired, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
+                            int rec_order, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
                             int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
                             void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
                             const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new,
@@ -1318,7 +1344,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   if (batch > 65535 || h > 65535) return NSNKV_ERR_ARG;
   const int64_t cb = code_bytes(bits);
   if (blk_bytes != 0 && (blk_bytes < cb || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
-  if (v_paired != 0 && v_paired != 1) return NSNKV_ERR_ARG;
+  if (rec_order != 0 && rec_order != 1) return NSNKV_ERR_ARG;
 
   AttnArgs a{};
   a.cs = blk_bytes ? blk_bytes : cb;
@@ -1366,14 +1392,14 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = NSNKV_OK;
   const bool sealed_path = k_alpha && v_alpha && bits == 3 && dtype == NSNKV_F16 && G <= 4;
-  if (v_paired && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // paired rows: tensor-core kernel only
+  if (rec_order && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // record orders: tensor-core kernel only
   if (sealed_path && max_blocks > 0) {
     // sealed chunks on the tensor-core kernel, native-row chunks on attn_partial_kernel
     if (!aligned16(k_alpha) || !aligned16(v_alpha)) return NSNKV_ERR_ARG;
     a.ka = k_alpha;
     a.va = v_alpha;
     const size_t smem = sizeof(s3::SSmem);
-    const auto kern = v_paired ? attn_sealed3_kernel<true> : attn_sealed3_kernel<false>;
+    const auto kern = rec_order ? attn_sealed3_kernel<true> : attn_sealed3_kernel<false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return NSNKV_ERR_CUDA;
     // whole chunks of up to 32 blocks (8 per warp) amortise the per-CTA set-up; fewer chunks
@@ -1450,7 +1476,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
-                            const float *v_alpha, int64_t blk_bytes, int v_paired, int64_t blk_stride_head,
+                            const float *v_alpha, int64_t blk_bytes, int rec_order, int64_t blk_stride_head,
                             int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail,
                             void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
@@ -1459,7 +1485,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             int32_t *status, void *stream) {
   if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, k_alpha, v_alpha, blk_bytes, v_paired, blk_stride_head, blk_stride_page,
+                          v_scale, k_alpha, v_alpha, blk_bytes, rec_order, blk_stride_head, blk_stride_page,
                           block_table, table_stride, n_blocks, n_blocks_const, max_blocks, k_tail, v_tail,
                           tail_stride_seq, tail_stride_head, tail_len, tail_len_const, max_tail, k_new, v_new, out,
                           out_f32, lse, workspace, workspace_bytes, status, stream);

@@ -66,7 +66,7 @@ __device__ __forceinline__ void pack_block(BlockSmem &s) {
 // Encode the block held in s.x.  Outputs go to global memory (any may be null).
 // Mirrors nsn_encode (loop_kv_nb06_primitives.py:37-55) step for step.
 template <int BITS>
-__device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, bool paired, uint8_t *q_out,
+__device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, int order, uint8_t *q_out,
                                uint16_t *norm, uint16_t *mn, uint16_t *scale, int32_t *status, int in_status) {
   const int tid = threadIdx.x;
   constexpr float kLevels = static_cast<float>((1 << BITS) - 1);
@@ -119,12 +119,18 @@ __device__ void encode_in_smem(BlockSmem &s, int norm_order, uint8_t *codes, boo
   if (codes) {
     pack_block<BITS>(s);
     __syncthreads();
-    if (paired) {  // word j*8*BITS + k = [row 2j half k | row 2j+1 half k]
-      const uint16_t *h16 = reinterpret_cast<const uint16_t *>(s.packed);
+    const uint16_t *h16 = reinterpret_cast<const uint16_t *>(s.packed);
+    if (order == 1) {  // paired rows: word j*8*BITS + k = [row 2j half k | row 2j+1 half k]
       for (int w = tid; w < code_bytes(BITS) / 4; w += blockDim.x) {
         const int j = w / (8 * BITS), k = w % (8 * BITS);
         reinterpret_cast<uint32_t *>(codes)[w] =
             h16[2 * j * 8 * BITS + k] | (static_cast<uint32_t>(h16[(2 * j + 1) * 8 * BITS + k]) << 16);
+      }
+    } else if (order == 2) {  // paired halves: group word m = [A half m | B half m]
+      for (int w = tid; w < code_bytes(BITS) / 4; w += blockDim.x) {
+        const int grp = w / BITS, m = w % BITS;  // a 32-code group is BITS words
+        reinterpret_cast<uint32_t *>(codes)[w] =
+            h16[2 * BITS * grp + m] | (static_cast<uint32_t>(h16[2 * BITS * grp + BITS + m]) << 16);
       }
     } else {
       for (int k = tid; k < code_bytes(BITS) / 16; k += blockDim.x)
@@ -237,7 +243,7 @@ __device__ __forceinline__ void stage_block(const __half *src, FastSmem &s) {
 }
 
 template <int BITS>
-__device__ void encode_block_fast(const __half *src, uint8_t *codes, bool paired, uint8_t *q_out, uint16_t *norm,
+__device__ void encode_block_fast(const __half *src, uint8_t *codes, int order, uint8_t *q_out, uint16_t *norm,
                                   uint16_t *mn,
                                   uint16_t *scale, int32_t *status, FastSmem &s) {
   const int t = threadIdx.x;
@@ -376,7 +382,7 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, bool paired
       const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
       uint32_t out[BITS];
       pack32<BITS>(w, out);
-      if (paired) {
+      if (order == 1) {
         // thread t holds words BITS*(t&3).. of row t>>2; thread t^4 the same words of the other row
         // of the pair.  Pair word j*8*BITS + k = [row 2j half k | row 2j+1 half k]: the even row's
         // thread writes the even k, the odd row's thread the odd k.
@@ -386,6 +392,16 @@ __device__ void encode_block_fast(const __half *src, uint8_t *codes, bool paired
         for (int i = 0; i < BITS; ++i) {
           const uint32_t other = __shfl_xor_sync(0xffffffffu, out[i], 4);
           dst[2 * i] = odd ? __byte_perm(other, out[i], 0x7632) : __byte_perm(out[i], other, 0x5410);
+        }
+      } else if (order == 2) {
+        // thread t holds exactly one 32-code group (2*BITS halves, half k in word k/2):
+        // word m = [half m | half BITS+m]
+        uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + BITS * t;
+#pragma unroll
+        for (int m = 0; m < BITS; ++m) {
+          const int ka = m, kb = BITS + m;
+          const uint32_t sel = ((ka & 1) ? 0x0032u : 0x0010u) | ((kb & 1) ? 0x7600u : 0x5400u);
+          dst[m] = __byte_perm(out[ka >> 1], out[kb >> 1], sel);
         }
       } else {
         uint32_t *dst = reinterpret_cast<uint32_t *>(codes) + BITS * t;
@@ -415,7 +431,7 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
                                                             uint8_t *codes, uint8_t *q_out, uint16_t *norm,
                                                             uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                             int64_t header_start, int64_t out_row_stride,
-                                                            int64_t out_offset, int64_t cs, int64_t ms, int paired,
+                                                            int64_t out_offset, int64_t cs, int64_t ms, int order,
                                                             int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
@@ -424,7 +440,7 @@ __global__ void __launch_bounds__(256) encode_blocks_kernel(const T *x, int norm
   const int64_t o = r * out_row_stride + out_offset + i;
   int st = load_block<T>(x + b * kBlock * kDim, s);
   __syncthreads();
-  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * cs : nullptr, paired != 0,
+  encode_in_smem<BITS>(s, norm_order, codes ? codes + o * cs : nullptr, order,
                        q_out ? q_out + b * kBlock * kDim : nullptr,
                        norm + o * kBlock, blk_ptr(mn, o, ms), blk_ptr(scale, o, ms), status, st);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
@@ -436,13 +452,13 @@ __global__ void __launch_bounds__(256, 4) encode_blocks_fast_kernel(const __half
                                                                    uint16_t *mn, uint16_t *scale, uint8_t *headers,
                                                                    int64_t header_start, int64_t out_row_stride,
                                                                    int64_t out_offset, int64_t cs, int64_t ms,
-                                                                   int paired, int32_t *status) {
+                                                                   int order, int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
   const int64_t b = blockIdx.x;
   const int64_t r = b / blocks_per_row, i = b % blocks_per_row;
   const int64_t o = r * out_row_stride + out_offset + i;
-  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * cs : nullptr, paired != 0,
+  encode_block_fast<BITS>(x + b * kBlock * kDim, codes ? codes + o * cs : nullptr, order,
                           q_out ? q_out + b * kBlock * kDim : nullptr, norm + o * kBlock, blk_ptr(mn, o, ms),
                           blk_ptr(scale, o, ms), status, s);
   if (headers && threadIdx.x == 0) write_header(headers + o * 12, header_start + kBlock * i, BITS);
@@ -566,7 +582,7 @@ __global__ void unpack_kernel(const uint8_t *payload, int64_t count, int bits, u
 
 // ----------------------------------------------------------------- paged-cache seal
 template <int BITS>
-__device__ void renorm_block(const uint8_t *codes, bool paired, const uint16_t *norm, const uint16_t *mn,
+__device__ void renorm_block(const uint8_t *codes, int order, const uint16_t *norm, const uint16_t *mn,
                              const uint16_t *sc, float *alpha);
 
 // One CTA per (kv head, K|V, sequence).  A sequence whose tail holds 64 tokens has that
@@ -581,7 +597,7 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
                                                    uint16_t *k_norm, uint16_t *k_min, uint16_t *k_scale,
                                                    uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
                                                    uint16_t *v_scale, float *k_alpha, float *v_alpha, int32_t *done,
-                                                   int64_t sh, int64_t sp, int64_t cs, int64_t ms, int v_paired,
+                                                   int64_t sh, int64_t sp, int64_t cs, int64_t ms, int rec_order,
                                                    int32_t *status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // launched with a programmatic dependency: wait for the kernel before it, then let the
@@ -601,19 +617,19 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
     uint16_t *nrm = (kv == 0 ? k_norm : v_norm) + blk * kBlock;
     uint16_t *mn = blk_ptr(kv == 0 ? k_min : v_min, blk, ms);
     uint16_t *sc = blk_ptr(kv == 0 ? k_scale : v_scale, blk, ms);
-    const bool paired = kv == 1 && v_paired != 0;
+    const int order = rec_order ? (kv == 0 ? 2 : 1) : 0;  // the block records' K and V code orders
     if constexpr (std::is_same<T, __half>::value) {
-      encode_block_fast<BITS>(src, codes, paired, nullptr, nrm, mn, sc, status,
+      encode_block_fast<BITS>(src, codes, order, nullptr, nrm, mn, sc, status,
                               *reinterpret_cast<FastSmem *>(smem_raw));
     } else {
       BlockSmem &s = *reinterpret_cast<BlockSmem *>(smem_raw);
       int st = load_block<T>(src, s);
       __syncthreads();
-      encode_in_smem<BITS>(s, 0, codes, paired, nullptr, nrm, mn, sc, status, st);
+      encode_in_smem<BITS>(s, 0, codes, order, nullptr, nrm, mn, sc, status, st);
     }
     if (k_alpha) {
       __syncthreads();  // this CTA's code and metadata stores are visible to all its threads
-      renorm_block<BITS>(codes, paired, nrm, mn, sc, blk_ptr(kv == 0 ? k_alpha : v_alpha, blk, ms));
+      renorm_block<BITS>(codes, order, nrm, mn, sc, blk_ptr(kv == 0 ? k_alpha : v_alpha, blk, ms));
     }
   }
   if (done) {
@@ -649,7 +665,7 @@ __global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_
 // each block does not recompute ||d|| on every step.  One 256-thread CTA per block:
 // thread (t = tid / 4, quarter) sums 32 channels of token t.
 template <int BITS>
-__device__ void renorm_block(const uint8_t *codes, bool paired, const uint16_t *norm, const uint16_t *mn,
+__device__ void renorm_block(const uint8_t *codes, int order, const uint16_t *norm, const uint16_t *mn,
                              const uint16_t *sc, float *alpha) {
   const int t = threadIdx.x >> 2, part = threadIdx.x & 3;
   constexpr int row_bytes = kDim * BITS / 8;
@@ -657,9 +673,9 @@ __device__ void renorm_block(const uint8_t *codes, bool paired, const uint16_t *
   for (int c = 32 * part; c < 32 * part + 32; ++c) {
     const int bit = c * BITS;  // within token t's packed row
     const int byte = bit >> 3, sh = bit & 7;
-    uint32_t w = codes[code_byte_at(t, byte, BITS, paired)];
+    uint32_t w = codes[code_byte_at(t, byte, BITS, order)];
     if (sh + BITS > 8 && byte + 1 < row_bytes)
-      w |= static_cast<uint32_t>(codes[code_byte_at(t, byte + 1, BITS, paired)]) << 8;
+      w |= static_cast<uint32_t>(codes[code_byte_at(t, byte + 1, BITS, order)]) << 8;
     const float x = static_cast<float>((w >> sh) & ((1u << BITS) - 1u));
     const float d = __fadd_rn(half_bits_to_f(mn[c]), __fmul_rn(half_bits_to_f(sc[c]), x));
     ss = __fmaf_rn(d, d, ss);
@@ -679,10 +695,10 @@ __global__ void __launch_bounds__(256) renorm_blocks_kernel(const uint8_t *codes
                                                             const uint16_t *mn, const uint16_t *sc,
                                                             int64_t blocks_per_row, int64_t row_stride,
                                                             int64_t offset, float *alpha, int64_t cs, int64_t ms,
-                                                            int paired) {
+                                                            int order) {
   const int64_t r = blockIdx.x / blocks_per_row, i = blockIdx.x % blocks_per_row;
   const int64_t blk = r * row_stride + offset + i;
-  renorm_block<BITS>(codes + blk * cs, paired != 0, norm + blk * kBlock, blk_ptr(mn, blk, ms),
+  renorm_block<BITS>(codes + blk * cs, order, norm + blk * kBlock, blk_ptr(mn, blk, ms),
                      blk_ptr(sc, blk, ms), blk_ptr(alpha, blk, ms));
 }
 
@@ -691,7 +707,7 @@ template <typename T>
 static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits, int norm_order, uint8_t *codes,
                          uint8_t *q_out, uint16_t *norm, uint16_t *mn, uint16_t *scale, uint8_t *headers,
                          int64_t header_start, int64_t out_row_stride, int64_t out_offset, int64_t cs, int64_t ms,
-                         int paired, int32_t *status, cudaStream_t st) {
+                         int order, int32_t *status, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>(n_blocks));
   if (std::is_same<T, __half>::value && norm_order == 0) {
     const size_t smem = sizeof(FastSmem);
@@ -701,7 +717,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)        \
       return NSNKV_ERR_CUDA;                                                                               \
     k<<<grid, 256, smem, st>>>(static_cast<const __half *>(x), bpr, codes, q_out, norm, mn, scale, headers, \
-                               header_start, out_row_stride, out_offset, cs, ms, paired, status);          \
+                               header_start, out_row_stride, out_offset, cs, ms, order, status);           \
     break;                                                                                                 \
   }
     switch (bits) {
@@ -721,7 +737,7 @@ static int launch_encode(const void *x, int64_t n_blocks, int64_t bpr, int bits,
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)       \
       return NSNKV_ERR_CUDA;                                                                              \
     k<<<grid, 256, smem, st>>>(static_cast<const T *>(x), norm_order, bpr, codes, q_out, norm, mn, scale, \
-                               headers, header_start, out_row_stride, out_offset, cs, ms, paired, status); \
+                               headers, header_start, out_row_stride, out_offset, cs, ms, order, status);  \
     break;                                                                                                \
   }
   switch (bits) {
@@ -776,7 +792,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
                        int32_t *tail_len, int32_t *n_blocks, int pending, const int32_t *table, int64_t ts,
                        uint8_t *kc, uint16_t *kn, uint16_t *km, uint16_t *ks, uint8_t *vc, uint16_t *vn,
                        uint16_t *vm, uint16_t *vs, float *ka, float *va, int32_t *done, int64_t sh, int64_t sp,
-                       int64_t cs, int64_t ms, int v_paired, int32_t *status, cudaStream_t st) {
+                       int64_t cs, int64_t ms, int rec_order, int32_t *status, cudaStream_t st) {
   const size_t smem = std::is_same<T, __half>::value ? sizeof(FastSmem) : sizeof(BlockSmem);
   dim3 grid(h, 2, static_cast<unsigned>(batch));
 #define NSNKV_SEAL(B)                                                                                      \
@@ -796,7 +812,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
     cfg.numAttrs = 1;                                                                                      \
     if (cudaLaunchKernelEx(&cfg, k, static_cast<const T *>(k_tail), static_cast<const T *>(v_tail), tss,   \
                            tsh, tail_len, n_blocks, pending, table, ts, kc, kn, km, ks, vc, vn, vm, vs, ka, \
-                           va, done, sh, sp, cs, ms, v_paired, status) != cudaSuccess)                     \
+                           va, done, sh, sp, cs, ms, rec_order, status) != cudaSuccess)                    \
       return NSNKV_ERR_LAUNCH;                                                                             \
     break;                                                                                                 \
   }
@@ -826,10 +842,10 @@ int64_t nsnkv_block_code_bytes(int bits) { return (bits >= 3 && bits <= 5) ? cod
 int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_t blocks_per_row, int bits,
                                 int norm_order, uint8_t *codes, uint8_t *q_out, uint16_t *norm, uint16_t *mn,
                                 uint16_t *scale, uint8_t *headers, int64_t header_start, int64_t out_row_stride,
-                                int64_t out_offset, int64_t blk_bytes, int paired, int32_t *status, void *stream) {
+                                int64_t out_offset, int64_t blk_bytes, int code_order, int32_t *status, void *stream) {
   if (rows < 0 || blocks_per_row < 0 || bits < 3 || bits > 5 || (norm_order != 0 && norm_order != 1))
     return NSNKV_ERR_ARG;
-  if (paired != 0 && paired != 1) return NSNKV_ERR_ARG;
+  if (code_order < 0 || code_order > 2) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   const int64_t n_blocks = rows * blocks_per_row;
@@ -841,13 +857,13 @@ int nsnkv_encode_blocks_strided(const void *x, int x_dtype, int64_t rows, int64_
   switch (x_dtype) {
     case NSNKV_F16:
       return launch_encode<__half>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                   headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
+                                   headers, header_start, out_row_stride, out_offset, cs, ms, code_order, status, st);
     case NSNKV_BF16:
       return launch_encode<__nv_bfloat16>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn,
-                                          scale, headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
+                                          scale, headers, header_start, out_row_stride, out_offset, cs, ms, code_order, status, st);
     case NSNKV_F32:
       return launch_encode<float>(x, n_blocks, blocks_per_row, bits, norm_order, codes, q_out, norm, mn, scale,
-                                  headers, header_start, out_row_stride, out_offset, cs, ms, paired, status, st);
+                                  headers, header_start, out_row_stride, out_offset, cs, ms, code_order, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -908,9 +924,9 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
                      int64_t tail_stride_head, int32_t *tail_len, int32_t *n_blocks, int pending_append,
                      const int32_t *block_table, int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm,
                      uint16_t *k_min, uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int v_paired, int32_t *done,
+                     uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int rec_order, int32_t *done,
                      int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream) {
-  if (v_paired != 0 && v_paired != 1) return NSNKV_ERR_ARG;
+  if (rec_order != 0 && rec_order != 1) return NSNKV_ERR_ARG;
   if (batch < 0 || h <= 0 || bits < 3 || bits > 5 || (pending_append != 0 && pending_append != 1)) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
@@ -926,12 +942,12 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
       return launch_seal<__half>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len,
                                  n_blocks, pending_append, block_table, table_stride, k_codes, k_norm, k_min,
                                  k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha, done, blk_stride_head,
-                                 blk_stride_page, cs, ms, v_paired, status, st);
+                                 blk_stride_page, cs, ms, rec_order, status, st);
     case NSNKV_BF16:
       return launch_seal<__nv_bfloat16>(batch, h, bits, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                                         tail_len, n_blocks, pending_append, block_table, table_stride, k_codes,
                                         k_norm, k_min, k_scale, v_codes, v_norm, v_min, v_scale, k_alpha, v_alpha,
-                                        done, blk_stride_head, blk_stride_page, cs, ms, v_paired, status, st);
+                                        done, blk_stride_head, blk_stride_page, cs, ms, rec_order, status, st);
     default:
       return NSNKV_ERR_ARG;
   }
@@ -953,21 +969,21 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype, void 
                                 int32_t *n_blocks, int pending_append, const int32_t *block_table,
                                 int64_t table_stride, uint8_t *k_codes, uint16_t *k_norm, uint16_t *k_min,
                                 uint16_t *k_scale, uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min,
-                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int v_paired,
+                                uint16_t *v_scale, float *k_alpha, float *v_alpha, int64_t blk_bytes, int rec_order,
                                 int32_t *seq_counters, int64_t blk_stride_head, int64_t blk_stride_page,
                                 int32_t *status, void *stream) {
   if (!k_alpha || !v_alpha) return NSNKV_ERR_ARG;
   return seal_impl(batch, h, bits, dtype, k_tail, v_tail, tail_stride_seq, tail_stride_head, tail_len, n_blocks,
                    pending_append, block_table, table_stride, k_codes, k_norm, k_min, k_scale, v_codes, v_norm,
-                   v_min, v_scale, k_alpha, v_alpha, blk_bytes, v_paired, seq_counters, blk_stride_head,
+                   v_min, v_scale, k_alpha, v_alpha, blk_bytes, rec_order, seq_counters, blk_stride_head,
                    blk_stride_page, status, stream);
 }
 
 int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uint8_t *codes, const uint16_t *norm,
                        const uint16_t *min, const uint16_t *scale, int64_t row_stride, int64_t offset, float *alpha,
-                       int64_t blk_bytes, int paired, void *stream) {
+                       int64_t blk_bytes, int code_order, void *stream) {
   if (bits < 3 || bits > 5 || rows < 0 || blocks_per_row < 0 || offset < 0) return NSNKV_ERR_ARG;
-  if (paired != 0 && paired != 1) return NSNKV_ERR_ARG;
+  if (code_order < 0 || code_order > 2) return NSNKV_ERR_ARG;
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   if (rows == 0 || blocks_per_row == 0) return NSNKV_OK;
@@ -978,15 +994,15 @@ int nsnkv_block_renorm(int bits, int64_t rows, int64_t blocks_per_row, const uin
   switch (bits) {
     case 3:
       renorm_blocks_kernel<3><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms, paired);
+                                                     alpha, cs, ms, code_order);
       break;
     case 4:
       renorm_blocks_kernel<4><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms, paired);
+                                                     alpha, cs, ms, code_order);
       break;
     default:
       renorm_blocks_kernel<5><<<grid, 256, 0, st>>>(codes, norm, min, scale, blocks_per_row, row_stride, offset,
-                                                     alpha, cs, ms, paired);
+                                                     alpha, cs, ms, code_order);
       break;
   }
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;

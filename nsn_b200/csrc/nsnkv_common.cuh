@@ -16,11 +16,21 @@ constexpr float kEps = 1e-12f;
 constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128)
 
 __host__ __device__ constexpr int code_bytes(int bits) { return kBlock * kDim * bits / 8; }
-// Byte b of token t's packed code row inside a block.  Dense: rows back to back.  Paired
-// (the V codes of the paged cache's block records): the rows of tokens 2j and 2j+1
-// interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j half k | row 2j+1 half k].
-__host__ __device__ __forceinline__ int code_byte_at(int t, int b, int bits, bool paired) {
-  return paired ? 4 * ((t >> 1) * 8 * bits + (b >> 1)) + 2 * (t & 1) + (b & 1) : t * 16 * bits + b;
+// Byte b of token t's packed code row inside a block, for the block's code order:
+//   0  the reference's rows back to back (LSB-first bitstream);
+//   1  paired rows (the V codes of the paged cache's block records): the rows of tokens 2j
+//      and 2j+1 interleaved at 16 bits, 32-bit word j*8*bits + k = [row 2j half k | row 2j+1 half k];
+//   2  paired halves (the K codes of the block records): in each row, each 32-code group
+//      (2*bits 16-bit halves, A = the first bits halves, B = the rest) stored as words
+//      [A half m | B half m], m < bits.
+__host__ __device__ __forceinline__ int code_byte_at(int t, int b, int bits, int order) {
+  if (order == 1) return 4 * ((t >> 1) * 8 * bits + (b >> 1)) + 2 * (t & 1) + (b & 1);
+  if (order == 2) {
+    const int gb = b % (4 * bits), hh = gb >> 1;
+    const int out_half = hh < bits ? 2 * hh : 2 * (hh - bits) + 1;
+    return t * 16 * bits + (b - gb) + 2 * out_half + (gb & 1);
+  }
+  return t * 16 * bits + b;
 }
 
 // Block i of an array whose blocks are `bytes` apart (a dense array, or one field of the

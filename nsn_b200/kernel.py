@@ -80,13 +80,14 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     blocks = (L.ptr(kp.get("codes")), L.ptr(kp.get("norm")), L.ptr(kp.get("min")), L.ptr(kp.get("scale")),
               L.ptr(vp.get("codes")), L.ptr(vp.get("norm")), L.ptr(vp.get("min")), L.ptr(vp.get("scale")))
     has_alpha = kp.get("alpha") is not None and vp.get("alpha") is not None
-    v_paired = bool(vp.get("paired"))
-    w.require(not kp.get("paired"), "K pool code order")
-    w.require(not v_paired or has_alpha, "paired V rows need the renorm-factor path")
+    orders = (int(kp.get("code_order", 0)), int(vp.get("code_order", 0)))
+    w.require(orders in ((0, 0), (2, 1)), "pool code orders (K paired halves with V paired rows, or neither)")
+    rec_order = int(orders == (2, 1))
+    w.require(not rec_order or has_alpha, "the block records' code orders need the renorm-factor path")
     if has_alpha or blk_bytes:
         entry, name = lib.nsnkv_decode_attn_alpha, "nsnkv_decode_attn_alpha"
         alphas = (L.ptr(kp["alpha"]), L.ptr(vp["alpha"])) if has_alpha else (L.ptr(None), L.ptr(None))
-        blocks = blocks + alphas + (int(blk_bytes), int(v_paired))
+        blocks = blocks + alphas + (int(blk_bytes), rec_order)
     else:
         entry, name = lib.nsnkv_decode_attn, "nsnkv_decode_attn"
     rc = entry(

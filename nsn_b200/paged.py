@@ -123,9 +123,10 @@ def block_record_pools(h: int, pages: int, bits: int, device):
     (64 fp32), then the same four fields for V (7680 bytes for INT3).  The pool dicts
     hold views of those fields, so every operator that takes a pool writes or reads the
     records; norms [h, pages, 64] fp16 stay dense.  nsnkv_decode_attn_alpha moves each
-    block with one copy when given these pools (blk_bytes = the record size).  The V
-    codes are paired rows (``pool["paired"]``, see primitives.pair_rows): the order the
-    tensor-core kernel reads cheapest; exports and imports convert.
+    block with one copy when given these pools (blk_bytes = the record size).  The K
+    codes are paired halves and the V codes paired rows (``pool["code_order"]`` 2 and 1,
+    see primitives.pair_halves / pair_rows): the orders the tensor-core kernel reads
+    cheapest; exports and imports convert.
     """
     cb = w.code_bytes(bits)
     half = cb + 2 * w.DIM * 2 + w.BLOCK * 4
@@ -138,9 +139,10 @@ def block_record_pools(h: int, pages: int, bits: int, device):
                     scale=rec[..., off + cb + 2 * w.DIM:off + cb + 4 * w.DIM].view(torch.float16),
                     alpha=rec[..., off + cb + 4 * w.DIM:off + half].view(torch.float32))
 
-    vp = fields(half)
-    vp["paired"] = True  # V codes as paired rows (primitives.pair_rows)
-    return rec, fields(0), vp
+    kp, vp = fields(0), fields(half)
+    kp["code_order"] = 2  # K codes as paired halves (primitives.pair_halves)
+    vp["code_order"] = 1  # V codes as paired rows (primitives.pair_rows)
+    return rec, kp, vp
 
 
 class PagedKVCache:
@@ -223,9 +225,7 @@ class PagedKVCache:
         def group(pool):
             if nb == 0:
                 return None
-            codes = pool["codes"][:, pages]
-            if pool.get("paired"):
-                codes = w.unpair_rows(codes, self.bits)
+            codes = w.from_code_order(pool["codes"][:, pages], self.bits, pool.get("code_order", 0))
             return dict(codes=codes.unsqueeze(0).contiguous(),
                         metas=(pool["norm"][:, pages].reshape(1, h, nb, w.BLOCK, 1).contiguous(),
                                pool["min"][:, pages].reshape(1, h, nb, 1, w.DIM).contiguous(),
@@ -257,7 +257,7 @@ class PagedKVCache:
             if g is None:
                 continue
             codes = g["codes"][0].to(self.device)
-            pool["codes"][:, pages] = w.pair_rows(codes, self.bits) if pool.get("paired") else codes
+            pool["codes"][:, pages] = w.to_code_order(codes, self.bits, pool.get("code_order", 0))
             pool["norm"][:, pages] = g["metas"][0].reshape(h, n, w.BLOCK).to(self.device)
             pool["min"][:, pages] = g["metas"][1].reshape(h, n, w.DIM).to(self.device)
             pool["scale"][:, pages] = g["metas"][2].reshape(h, n, w.DIM).to(self.device)
@@ -316,7 +316,7 @@ class PagedKVCache:
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
             L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
-            L.ptr(self.v_pool["alpha"]), self.blk_bytes, int(bool(self.v_pool.get("paired"))),
+            L.ptr(self.v_pool["alpha"]), self.blk_bytes, int(self.records is not None),
             L.ptr(self.seal_counters), self.pages, 1,
             L.ptr(self.status), L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")

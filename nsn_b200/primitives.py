@@ -153,7 +153,7 @@ def encode_blocks(x: torch.Tensor, bits: int, *, packed=True, unpacked=False, he
         L.check(L.load().nsnkv_encode_blocks_strided(
             L.ptr(xc), L.DTYPE_CODE[x.dtype], rows, bpr, bits, order, L.ptr(codes), L.ptr(q), L.ptr(n), L.ptr(m),
             L.ptr(s), L.ptr(hdr), int(headers_start or 0), stride, offset, blk,
-            int(bool(out is not None and out.get("paired"))), L.ptr(status), L.stream_handle(dev)),
+            int(out.get("code_order", 0)) if out is not None else 0, L.ptr(status), L.stream_handle(dev)),
             "nsnkv_encode_blocks")
         if out is not None and out.get("alpha") is not None and codes is not None:
             block_renorm(out, bits, rows, bpr, stride, offset)
@@ -185,6 +185,39 @@ def unpair_rows(codes: torch.Tensor, bits: int) -> torch.Tensor:
     require(codes.dtype == torch.uint8 and codes.shape[-1] == code_bytes(bits), "packed block shape")
     h = codes.contiguous().view(torch.int16).reshape(lead + (BLOCK // 2, 8 * bits, 2))
     return h.transpose(-1, -2).contiguous().view(torch.uint8).reshape(lead + (code_bytes(bits),))
+
+
+def pair_halves(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Packed blocks [..., code_bytes] in the reference's row order -> paired halves.
+
+    Paired halves (the K codes of the paged cache's block records): in each token row,
+    each 32-code group (2*bits 16-bit halves: A = the first bits, B = the rest) stored
+    as 32-bit words [A half m | B half m], m < bits.
+    """
+    lead = tuple(codes.shape[:-1])
+    require(codes.dtype == torch.uint8 and codes.shape[-1] == code_bytes(bits), "packed block shape")
+    h = codes.contiguous().view(torch.int16).reshape(lead + (BLOCK * 4, 2, bits))
+    return h.transpose(-1, -2).contiguous().view(torch.uint8).reshape(lead + (code_bytes(bits),))
+
+
+def unpair_halves(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Inverse of pair_halves."""
+    lead = tuple(codes.shape[:-1])
+    require(codes.dtype == torch.uint8 and codes.shape[-1] == code_bytes(bits), "packed block shape")
+    h = codes.contiguous().view(torch.int16).reshape(lead + (BLOCK * 4, bits, 2))
+    return h.transpose(-1, -2).contiguous().view(torch.uint8).reshape(lead + (code_bytes(bits),))
+
+
+def to_code_order(codes: torch.Tensor, bits: int, order: int) -> torch.Tensor:
+    """The reference's row order -> code order 0 (unchanged), 1 (paired rows) or 2 (paired halves)."""
+    require(order in (0, 1, 2), "code order")
+    return codes if order == 0 else pair_rows(codes, bits) if order == 1 else pair_halves(codes, bits)
+
+
+def from_code_order(codes: torch.Tensor, bits: int, order: int) -> torch.Tensor:
+    """Inverse of to_code_order."""
+    require(order in (0, 1, 2), "code order")
+    return codes if order == 0 else unpair_rows(codes, bits) if order == 1 else unpair_halves(codes, bits)
 
 
 def blk_bytes_of(pool, bits: int) -> int:
@@ -234,7 +267,7 @@ def block_renorm(pool, bits: int, rows: int, blocks_per_row: int, row_stride: in
         L.check(L.load().nsnkv_block_renorm(
             bits, rows, blocks_per_row, L.ptr(pool["codes"]), L.ptr(pool["norm"]), L.ptr(pool["min"]),
             L.ptr(pool["scale"]), row_stride, offset, L.ptr(pool["alpha"]), blk_bytes_of(pool, bits),
-            int(bool(pool.get("paired"))), L.stream_handle(pool["codes"].device)),
+            int(pool.get("code_order", 0)), L.stream_handle(pool["codes"].device)),
             "nsnkv_block_renorm")
 
 

@@ -186,7 +186,8 @@ def test_alpha_path_agrees_with_restore_path():
     fast = cache.attend(qt).float().cpu().numpy()
     # the restore path reads the reference's code order: dense copies, V rows unpaired
     pools = [{k: p[k].contiguous() for k in ("codes", "norm", "min", "scale")} for p in (cache.k_pool, cache.v_pool)]
-    pools[1]["codes"] = w.unpair_rows(pools[1]["codes"], 3)
+    for p_, src in zip(pools, (cache.k_pool, cache.v_pool)):
+        p_["codes"] = w.from_code_order(p_["codes"], 3, src["code_order"])
     slow, st = decode_attention(
         qt, pools[0], pools[1], h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1,
         n_blocks=cache.n_blocks, max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
@@ -270,15 +271,17 @@ def test_alpha_path_flags_nonfinite_metadata(where):
 
 
 def test_block_records_match_dense_arrays():
-    """The cache's block records (one copy per block, V codes as paired rows) and dense
-    copies of the same arrays in the reference's order (eight copies per block) give
-    bit-identical attention; so do records with unpaired V codes on the restore path."""
+    """The cache's block records (one copy per block, K codes as paired halves, V codes as
+    paired rows) and dense copies of the same arrays in the reference's order (eight copies
+    per block) agree within fp32 accumulation order; records with codes in the reference's
+    order on the restore path match dense arrays bit for bit."""
     from nsn_b200.kernel import decode_attention
     from nsn_b200 import primitives as w
     rng = np.random.default_rng(21)
     lens = [64 * 40 + 9, 64 * 3, 64 * 77 + 63, 5]
     cache, hk, hv, q = make_cache(rng, lens, 2, 8, max_blocks=80)
-    assert cache.blk_bytes == 7680 and w.blk_bytes_of(cache.k_pool, 3) == 7680 and cache.v_pool["paired"]
+    assert cache.blk_bytes == 7680 and w.blk_bytes_of(cache.k_pool, 3) == 7680
+    assert cache.k_pool["code_order"] == 2 and cache.v_pool["code_order"] == 1
     qt = torch.from_numpy(q).cuda()
     common = dict(h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1, n_blocks=cache.n_blocks,
                   max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
@@ -287,24 +290,28 @@ def test_block_records_match_dense_arrays():
 
     def dense_of(keys):
         d = [{k: p[k].contiguous() for k in keys} for p in (cache.k_pool, cache.v_pool)]
-        d[1]["codes"] = w.unpair_rows(d[1]["codes"], 3)
+        for p_, src in zip(d, (cache.k_pool, cache.v_pool)):
+            p_["codes"] = w.from_code_order(p_["codes"], 3, src["code_order"])
         return d
 
-    # renorm-factor path: records with paired V rows against dense arrays
+    # renorm-factor path: records (paired halves / rows) against dense arrays: the K codes
+    # enter the tensor cores in another k order, so fp32 sums may round differently
     keys = ("codes", "norm", "min", "scale", "alpha")
     dense = dense_of(keys)
     assert w.blk_bytes_of(dense[0], 3) == 0
-    a, sa = decode_attention(qt, cache.k_pool, cache.v_pool, **common)
-    b, sb = decode_attention(qt, dense[0], dense[1], **common)
+    fa = torch.empty(q.shape, device="cuda")
+    fb = torch.empty(q.shape, device="cuda")
+    a, sa = decode_attention(qt, cache.k_pool, cache.v_pool, out_f32=fa, **common)
+    b, sb = decode_attention(qt, dense[0], dense[1], out_f32=fb, **common)
     torch.cuda.synchronize()
     assert int(sa.item()) == 0 and int(sb.item()) == 0
-    assert torch.equal(a, b)
+    assert torch.allclose(fa, fb, rtol=TIGHT[0], atol=TIGHT[1]), (fa - fb).abs().max().item()
     # restore path: the same record strides with V rows back in the reference's order
     from nsn_b200.paged import block_record_pools
     rec, kp, vp = block_record_pools(cache.h, cache.pages, 3, "cuda")
     rec.copy_(cache.records)
-    vp["codes"].copy_(w.unpair_rows(vp["codes"], 3))
-    del vp["paired"]
+    for p_ in (kp, vp):
+        p_["codes"].copy_(w.from_code_order(p_["codes"], 3, p_.pop("code_order")))
     keys = ("codes", "norm", "min", "scale")
     for p_, src in ((kp, cache.k_pool), (vp, cache.v_pool)):
         p_["norm"].copy_(src["norm"])
@@ -316,7 +323,7 @@ def test_block_records_match_dense_arrays():
     assert torch.equal(a, b)
     # paired V rows without factors have no kernel
     with pytest.raises(w.ContractError):
-        decode_attention(qt, {k: cache.k_pool[k] for k in keys}, dict({k: cache.v_pool[k] for k in keys}, paired=True),
+        decode_attention(qt, {k: cache.k_pool[k] for k in keys}, dict({k: cache.v_pool[k] for k in keys}, code_order=1),
                          **common)
 
 
@@ -336,14 +343,19 @@ def test_encode_into_block_records_matches_dense():
     w.block_renorm(dense, 3, 2, 6, 6)
     torch.cuda.synchronize()
     for k in ("codes", "norm", "min", "scale", "alpha"):
-        assert torch.equal(kp[k][:, 2:8], dense[k]), k
+        got = kp[k][:, 2:8]
+        if k == "codes":  # the records keep K codes as paired halves
+            got = w.from_code_order(got, 3, kp["code_order"])
+        assert torch.equal(got, dense[k]), k
     assert int(rec[:, :2].count_nonzero()) == 0 and int(rec[:, 8:].count_nonzero()) == 0
 
 
 @pytest.mark.parametrize("bits", [3, 5])
-def test_paired_rows_encode_and_renorm(bits):
-    """Encoding into a pool flagged paired writes pair_rows of the dense encoder's codes, and
-    nsnkv_block_renorm reading paired rows gives the dense factors (generic and fp16 encoders)."""
+@pytest.mark.parametrize("order", [1, 2])
+def test_code_orders_encode_and_renorm(bits, order):
+    """Encoding into a pool with code_order 1 (paired rows) or 2 (paired halves) writes that
+    order of the dense encoder's codes, and nsnkv_block_renorm reading it gives the dense
+    factors (generic and fp16 encoders)."""
     from nsn_b200 import primitives as w
     from nsn_b200 import workloads
     rng = np.random.default_rng(23 + bits)
@@ -353,13 +365,13 @@ def test_paired_rows_encode_and_renorm(bits):
                     norm=torch.zeros((3, 6, 64), dtype=torch.float16, device="cuda"),
                     min=torch.zeros((3, 6, 128), dtype=torch.float16, device="cuda"),
                     scale=torch.zeros((3, 6, 128), dtype=torch.float16, device="cuda"),
-                    alpha=torch.zeros((3, 6, 64), dtype=torch.float32, device="cuda"), paired=True)
+                    alpha=torch.zeros((3, 6, 64), dtype=torch.float32, device="cuda"), code_order=order)
         w.encode_blocks(x, bits, out=pool, out_row_stride=6, out_offset=1)
         ref = w.encode_blocks(x, bits)
         dense = dict(codes=ref["codes"], norm=ref["metas"][0].reshape(3, 4, 64), min=ref["metas"][1].reshape(3, 4, 128),
                      scale=ref["metas"][2].reshape(3, 4, 128), alpha=torch.zeros((3, 4, 64), device="cuda"))
         w.block_renorm(dense, bits, 3, 4, 4)
         torch.cuda.synchronize()
-        assert torch.equal(pool["codes"][:, 1:5], w.pair_rows(dense["codes"], bits)), dtype
+        assert torch.equal(pool["codes"][:, 1:5], w.to_code_order(dense["codes"], bits, order)), dtype
         assert torch.equal(pool["alpha"][:, 1:5], dense["alpha"]), dtype
-        assert torch.equal(w.unpair_rows(pool["codes"][:, 1:5], bits), dense["codes"]), dtype
+        assert torch.equal(w.from_code_order(pool["codes"][:, 1:5], bits, order), dense["codes"]), dtype

@@ -143,9 +143,8 @@ def test_paged_cache_steps_and_seals():
             x = hist[b][:, :nb[b] * 64].reshape(1, h, nb[b], 64, 128).astype(np.float32)
             q8, n, m, s_, st = O.nsn_encode(x, 3)
             pages = cache.block_table[b, :nb[b]].long().cpu()
-            codes = pool["codes"][:, pages]
-            if pool.get("paired"):  # the block records keep V codes as paired rows
-                codes = w.unpair_rows(codes, 3)
+            # the block records keep K as paired halves and V as paired rows
+            codes = w.from_code_order(pool["codes"][:, pages], 3, pool.get("code_order", 0))
             got = codes.cpu().numpy().reshape(-1, 3072)
             want = np.stack([O.pack3(blk) for blk in q8.reshape(-1, 64, 128)])
             assert np.array_equal(got, want), (b, kv)

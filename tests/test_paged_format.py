@@ -122,5 +122,14 @@ def test_pair_rows_layout_and_round_trip(bits):
     j, k = 5, 7
     want = (rows[..., 2 * j, k].to(torch.int32) & 0xFFFF) | (rows[..., 2 * j + 1, k].to(torch.int32) << 16)
     assert torch.equal(words[..., j, k], want)
+    ph = w.pair_halves(codes, bits)
+    assert torch.equal(w.unpair_halves(ph, bits), codes)
+    halves = codes.view(torch.int16).reshape(2, 3, 64, 4, 2 * bits)  # [row, group, half]
+    hw = ph.view(torch.int32).reshape(2, 3, 64, 4, bits)
+    r, gi, m = 9, 2, bits - 1
+    want = (halves[..., r, gi, m].to(torch.int32) & 0xFFFF) | (halves[..., r, gi, bits + m].to(torch.int32) << 16)
+    assert torch.equal(hw[..., r, gi, m], want)
+    for order in (0, 1, 2):
+        assert torch.equal(w.from_code_order(w.to_code_order(codes, bits, order), bits, order), codes)
     _, kp, vp = block_record_pools(1, 2, 3, "cpu")
-    assert vp.get("paired") is True and not kp.get("paired")
+    assert kp["code_order"] == 2 and vp["code_order"] == 1
