@@ -660,8 +660,8 @@ def main():
                        "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
             "roofline": {"bound": "hbm",
-                         "kernel": ("nsnkv_decode_attn_alpha (attn_sealed3_kernel + attn_partial_kernel on the tails "
-                                    "+ attn_merge_kernel)") if cache.uses_alpha_path() else
+                         "kernel": ("nsnkv_decode_attn_alpha (attn_sealed3_kernel + attn_native_rows_kernel on the "
+                                    "tails + attn_merge_kernel)") if cache.uses_alpha_path() else
                                    "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn, cache.uses_alpha_path()),

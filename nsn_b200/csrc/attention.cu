@@ -99,6 +99,15 @@ struct AttnSmem {
   uint64_t full[kStages];
 };
 
+// Shared memory of a CTA that only handles native rows (the tensor-core path's tail grid):
+// no TMA ring, so several such CTAs fit into the slot of one finished sealed CTA.
+struct RawSmem {
+  union {
+    uint16_t v16[kWarps][16][kVRow];
+    MergeSmem merge;
+  } u;
+};
+
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ int meta_index(int c) { return c + (c >> 5) * 4; }
 
@@ -363,10 +372,12 @@ __device__ __forceinline__ void warp_softmax_pv(WarpState &ws, const float (&raw
   }
 }
 
-template <int BITS, typename T>
+// RAW: the CTA only ever takes native-row chunks (raw_only launches), with RawSmem.
+template <int BITS, typename T, bool RAW = false>
 __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *smem_raw) {
   constexpr int CB = code_bytes(BITS);
-  AttnSmem<BITS> &S = *reinterpret_cast<AttnSmem<BITS> *>(smem_raw);
+  using SmemT = typename std::conditional<RAW, RawSmem, AttnSmem<BITS>>::type;
+  SmemT &S = *reinterpret_cast<SmemT *>(smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3, cbase = 32 * tig, mi = meta_index(cbase);
@@ -401,96 +412,7 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *sme
   uint16_t (*v16)[kVRow] = S.u.v16[warp];
   const bool all_valid[4] = {true, true, true, true};
 
-  if (!is_raw) {
-    const int blk0 = chunk * a.chunk_blocks;
-    const int nloc = min(nb, blk0 + a.chunk_blocks) - blk0;
-    auto issue = [&](int i, int s) {
-      const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
-      const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
-      Stage<BITS> &sg = S.stage[s];
-      mbar_expect_tx(&S.full[s], 2 * CB + 2 * (kBlock * 2 + 2 * kDim * 2));
-      bulk_g2s(sg.kc, a.kc + bi * a.cs, CB, &S.full[s]);
-      bulk_g2s(sg.vc, a.vc + bi * a.cs, CB, &S.full[s]);
-      bulk_g2s(sg.kn, a.kn + bi * kBlock, kBlock * 2, &S.full[s]);
-      bulk_g2s(sg.km, blk_ptr(a.km, bi, a.ms), kDim * 2, &S.full[s]);
-      bulk_g2s(sg.ks, blk_ptr(a.ks, bi, a.ms), kDim * 2, &S.full[s]);
-      bulk_g2s(sg.vn, a.vn + bi * kBlock, kBlock * 2, &S.full[s]);
-      bulk_g2s(sg.vm, blk_ptr(a.vm, bi, a.ms), kDim * 2, &S.full[s]);
-      bulk_g2s(sg.vs, blk_ptr(a.vs, bi, a.ms), kDim * 2, &S.full[s]);
-    };
-    if (tid == 0) {
-#pragma unroll
-      for (int i = 0; i < kStages; ++i) mbar_init(&S.full[i], 1);
-      fence_mbar_init();
-      for (int i = 0; i < kStages && i < nloc; ++i) issue(blk0 + i, i);
-    }
-    __syncthreads();  // no thread may poll a barrier before thread 0 has initialised it
-    const float fac = static_cast<float>(1 << (23 - code_pos<BITS>(tid & 31)));
-    for (int li = 0; li < nloc; ++li) {
-      const int s = li % kStages;
-      const bool ok = mbar_wait_bounded(&S.full[s], (li / kStages) & 1, a.status);
-      const Stage<BITS> &sg = S.stage[s];
-      MetaF &mf = S.meta[li & 1];
-      if (ok) {  // fp32 metadata of this block, one channel per thread
-        const int ci = meta_index(tid);
-        const float km = half_bits_to_f(sg.km[tid]), ks = half_bits_to_f(sg.ks[tid]);
-        const float vm = half_bits_to_f(sg.vm[tid]), vs = half_bits_to_f(sg.vs[tid]);
-        const float kb_ = ks * fac, vb_ = vs * fac;
-        mf.ka[ci] = km - kb_;
-        mf.kb[ci] = kb_;
-        mf.va[ci] = vm - vb_;
-        mf.vb[ci] = vb_;
-        bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
-        if (tid < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[tid])) || !isfinite(half_bits_to_f(sg.vn[tid]));
-        if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
-      }
-      if (__syncthreads_or(!ok)) {
-        // A staged copy never landed: give the later copies a bounded chance to
-        // finish, then leave; the timeout status tells the host.
-        if (tid == 0)
-          for (int k = li + 1; k < nloc && k < li + kStages; ++k)
-            mbar_wait_bounded(&S.full[k % kStages], (k / kStages) & 1, a.status);
-        return;
-      }
-      // every warp has finished block li-1: its stage takes block li-1+kStages
-      if (tid == 0 && li >= 1 && li - 1 + kStages < nloc) issue(blk0 + li - 1 + kStages, (li - 1) % kStages);
-      // ---- V rows t0, t1: restore, renormalise, round to the bridge dtype (the value
-      // restore_group stores) into this warp's V tile
-      {
-        uint32_t u0[16], u1[16];
-        restore_two_rows<BITS, T>(sg.vc, mf.va, mf.vb, mi, t0, t1, tig, half_bits_to_f(sg.vn[t0]),
-                                  half_bits_to_f(sg.vn[t1]), u0, u1);
-        store_row32(&v16[g][cbase], u0);
-        store_row32(&v16[g + 8][cbase], u1);
-      }
-      // ---- K rows t0, t1: the same restore, then the scores of both rows
-      float sraw[4];
-      {
-        uint32_t k0[16], k1[16];
-        restore_two_rows<BITS, T>(sg.kc, mf.ka, mf.kb, mi, t0, t1, tig, half_bits_to_f(sg.kn[t0]),
-                                  half_bits_to_f(sg.kn[t1]), k0, k1);
-        // four independent accumulation chains per row (two slices each) shorten the
-        // dependent MMA sequence; their sum is the score
-        float s0[4][4], s1[4][4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) s0[c][i] = s1[c][i] = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          mma16816<T>(s0[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k0[2 * j], k0[2 * j + 1]);
-          mma16816<T>(s1[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k1[2 * j], k1[2 * j + 1]);
-        }
-        sraw[0] = (s0[0][0] + s0[1][0]) + (s0[2][0] + s0[3][0]);
-        sraw[1] = (s0[0][1] + s0[1][1]) + (s0[2][1] + s0[3][1]);
-        sraw[2] = (s1[0][0] + s1[1][0]) + (s1[2][0] + s1[3][0]);
-        sraw[3] = (s1[0][1] + s1[1][1]) + (s1[2][1] + s1[3][1]);
-      }
-      __syncwarp();
-      warp_softmax_pv<T>(ws, sraw, v16, all_valid, G, lane, st);
-      __syncwarp();
-    }
-  } else {
+  auto native_rows = [&]() {
     // ---- native rows (tail, appended token, or materialised K/V), per warp 16 rows of each 64-row tile
     const T *ktb = static_cast<const T *>(a.kt) + (b * a.tss + h * a.tsh) * kDim;
     const T *vtb = static_cast<const T *>(a.vt) + (b * a.tss + h * a.tsh) * kDim;
@@ -545,6 +467,103 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *sme
       warp_softmax_pv<T>(ws, sraw, v16, valid, G, lane, st);
       __syncwarp();
     }
+  
+  };
+  if constexpr (!RAW) {
+    if (!is_raw) {
+      const int blk0 = chunk * a.chunk_blocks;
+      const int nloc = min(nb, blk0 + a.chunk_blocks) - blk0;
+      auto issue = [&](int i, int s) {
+        const int32_t page = a.table ? a.table[b * a.table_stride + i] : i;
+        const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
+        Stage<BITS> &sg = S.stage[s];
+        mbar_expect_tx(&S.full[s], 2 * CB + 2 * (kBlock * 2 + 2 * kDim * 2));
+        bulk_g2s(sg.kc, a.kc + bi * a.cs, CB, &S.full[s]);
+        bulk_g2s(sg.vc, a.vc + bi * a.cs, CB, &S.full[s]);
+        bulk_g2s(sg.kn, a.kn + bi * kBlock, kBlock * 2, &S.full[s]);
+        bulk_g2s(sg.km, blk_ptr(a.km, bi, a.ms), kDim * 2, &S.full[s]);
+        bulk_g2s(sg.ks, blk_ptr(a.ks, bi, a.ms), kDim * 2, &S.full[s]);
+        bulk_g2s(sg.vn, a.vn + bi * kBlock, kBlock * 2, &S.full[s]);
+        bulk_g2s(sg.vm, blk_ptr(a.vm, bi, a.ms), kDim * 2, &S.full[s]);
+        bulk_g2s(sg.vs, blk_ptr(a.vs, bi, a.ms), kDim * 2, &S.full[s]);
+      };
+      if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < kStages; ++i) mbar_init(&S.full[i], 1);
+        fence_mbar_init();
+        for (int i = 0; i < kStages && i < nloc; ++i) issue(blk0 + i, i);
+      }
+      __syncthreads();  // no thread may poll a barrier before thread 0 has initialised it
+      const float fac = static_cast<float>(1 << (23 - code_pos<BITS>(tid & 31)));
+      for (int li = 0; li < nloc; ++li) {
+        const int s = li % kStages;
+        const bool ok = mbar_wait_bounded(&S.full[s], (li / kStages) & 1, a.status);
+        const Stage<BITS> &sg = S.stage[s];
+        MetaF &mf = S.meta[li & 1];
+        if (ok) {  // fp32 metadata of this block, one channel per thread
+          const int ci = meta_index(tid);
+          const float km = half_bits_to_f(sg.km[tid]), ks = half_bits_to_f(sg.ks[tid]);
+          const float vm = half_bits_to_f(sg.vm[tid]), vs = half_bits_to_f(sg.vs[tid]);
+          const float kb_ = ks * fac, vb_ = vs * fac;
+          mf.ka[ci] = km - kb_;
+          mf.kb[ci] = kb_;
+          mf.va[ci] = vm - vb_;
+          mf.vb[ci] = vb_;
+          bool bad = !isfinite(km) || !isfinite(ks) || !isfinite(vm) || !isfinite(vs);
+          if (tid < kBlock) bad |= !isfinite(half_bits_to_f(sg.kn[tid])) || !isfinite(half_bits_to_f(sg.vn[tid]));
+          if (bad) st |= NSNKV_ST_INPUT_NONFINITE;
+        }
+        if (__syncthreads_or(!ok)) {
+          // A staged copy never landed: give the later copies a bounded chance to
+          // finish, then leave; the timeout status tells the host.
+          if (tid == 0)
+            for (int k = li + 1; k < nloc && k < li + kStages; ++k)
+              mbar_wait_bounded(&S.full[k % kStages], (k / kStages) & 1, a.status);
+          return;
+        }
+        // every warp has finished block li-1: its stage takes block li-1+kStages
+        if (tid == 0 && li >= 1 && li - 1 + kStages < nloc) issue(blk0 + li - 1 + kStages, (li - 1) % kStages);
+        // ---- V rows t0, t1: restore, renormalise, round to the bridge dtype (the value
+        // restore_group stores) into this warp's V tile
+        {
+          uint32_t u0[16], u1[16];
+          restore_two_rows<BITS, T>(sg.vc, mf.va, mf.vb, mi, t0, t1, tig, half_bits_to_f(sg.vn[t0]),
+                                    half_bits_to_f(sg.vn[t1]), u0, u1);
+          store_row32(&v16[g][cbase], u0);
+          store_row32(&v16[g + 8][cbase], u1);
+        }
+        // ---- K rows t0, t1: the same restore, then the scores of both rows
+        float sraw[4];
+        {
+          uint32_t k0[16], k1[16];
+          restore_two_rows<BITS, T>(sg.kc, mf.ka, mf.kb, mi, t0, t1, tig, half_bits_to_f(sg.kn[t0]),
+                                    half_bits_to_f(sg.kn[t1]), k0, k1);
+          // four independent accumulation chains per row (two slices each) shorten the
+          // dependent MMA sequence; their sum is the score
+          float s0[4][4], s1[4][4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s0[c][i] = s1[c][i] = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            mma16816<T>(s0[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k0[2 * j], k0[2 * j + 1]);
+            mma16816<T>(s1[j & 3], aq[2 * j], 0u, aq[2 * j + 1], 0u, k1[2 * j], k1[2 * j + 1]);
+          }
+          sraw[0] = (s0[0][0] + s0[1][0]) + (s0[2][0] + s0[3][0]);
+          sraw[1] = (s0[0][1] + s0[1][1]) + (s0[2][1] + s0[3][1]);
+          sraw[2] = (s1[0][0] + s1[1][0]) + (s1[2][0] + s1[3][0]);
+          sraw[3] = (s1[0][1] + s1[1][1]) + (s1[2][1] + s1[3][1]);
+        }
+        __syncwarp();
+        warp_softmax_pv<T>(ws, sraw, v16, all_valid, G, lane, st);
+        __syncwarp();
+      }
+    } else {
+      native_rows();
+    }
+  } else {
+    native_rows();
   }
 
   // ---- combine the four warps' partials and write this chunk's partial
@@ -601,6 +620,17 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
   extern __shared__ __align__(128) uint8_t smem_raw[];
   pdl_launch_dependents();  // the merge grid may be resident (and waiting) before this one ends
   attn_partial_cta<BITS, T>(a, smem_raw);
+  pdl_wait();
+}
+
+// The tensor-core path's tail grid: the native-row chunks only (raw_only), with the small
+// RawSmem.  Launched after attn_sealed3_kernel with a programmatic dependency, it fills
+// slots freed in the sealed grid's last wave; the final wait keeps this grid from
+// completing before the sealed grid, so the merge launched next sees both.
+__global__ void __launch_bounds__(kThreads, 4) attn_native_rows_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  pdl_launch_dependents();
+  attn_partial_cta<3, __half, true>(a, smem_raw);
   pdl_wait();
 }
 
@@ -1425,7 +1455,18 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
     if (cudaGetLastError() != cudaSuccess) return NSNKV_ERR_LAUNCH;
     if (any_tail) {  // native-row chunks, overlapping the sealed grid's last wave
       a.raw_only = 1;
-      rc = launch_attn<3, __half>(a, dim3(a.max_chunks - sealed_chunks, h, static_cast<unsigned>(batch)), st, true);
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(a.max_chunks - sealed_chunks, h, static_cast<unsigned>(batch));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = sizeof(RawSmem);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, attn_native_rows_kernel, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
+      rc = cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
     }
   } else {
     dim3 grid(a.max_chunks, h, static_cast<unsigned>(batch));
