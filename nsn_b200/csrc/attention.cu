@@ -612,9 +612,10 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint8_t *sme
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// The restore-path CTA.  Launched after attn_sealed3_kernel with a programmatic
-// dependency (native-row chunks only), it overlaps that kernel's last wave; the final
-// wait keeps this grid from completing before it, so the merge launched next sees both.
+// The restore-path CTA (every shape without the tensor-core path, and the reference-layout
+// entry points).  launch_dependents lets the merge grid, launched next with a programmatic
+// dependency, become resident early; it waits for this grid on entry.  Launched normally,
+// this grid has no programmatic predecessor, so its final wait returns at once.
 template <int BITS, typename T>
 __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1291,29 +1292,13 @@ static int max_chunks_for(int32_t max_blocks, int32_t max_tail, int32_t ch) {
   return static_cast<int>((max_blocks + ch - 1) / ch + (raw + static_cast<int64_t>(ch) * kBlock - 1) / (static_cast<int64_t>(ch) * kBlock));
 }
 
-// after_sealed: launched with a programmatic dependency on the attn_sealed3_kernel grid
-// just before it in the stream.
 template <int BITS, typename T>
-static int launch_attn(const AttnArgs &a, dim3 grid, cudaStream_t st, bool after_sealed = false) {
+static int launch_attn(const AttnArgs &a, dim3 grid, cudaStream_t st) {
   auto k = attn_partial_kernel<BITS, T>;
   const size_t smem = sizeof(AttnSmem<BITS>);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return NSNKV_ERR_CUDA;
-  if (!after_sealed) {
-    k<<<grid, kThreads, smem, st>>>(a);
-  } else {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, k, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
-  }
+  k<<<grid, kThreads, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
