@@ -46,13 +46,13 @@ def peaks():
     return HBM_FALLBACK, "fallback"
 
 
-def traffic_for(bytes_attn, sealed3=True):
-    """DRAM bytes per attention launch: the ncu capture's traffic/algorithmic ratio times this launch's bytes."""
-    p = ROOT / "profiles" / ("attn_sealed3_cfg2_traffic.json" if sealed3 else "attn_partial_cfg2_traffic.json")
-    if not p.exists():
-        return None
-    d = json.loads(p.read_text())
-    return d["traffic_bytes_per_launch"] / d["algorithmic_bytes_that_launch"] * bytes_attn
+# Algorithmic bytes of the hot path (per decode call): per (sequence, kv head) each sealed
+# INT3 K or V block is 3072 code bytes + 128 norm + 512 min / scale = 3712 B (headers are
+# never read), each native tail token 256 B for K and for V, q and out 256 B per query
+# head.  The tensor-core kernels read fp32 renorm factors (256 B per block) in place of
+# the fp16 norms (128 B): 128 B per K or V block of the kernel's own overhead.
+BLOCK_BYTES = 3712
+FACTOR_OVERHEAD = 128
 
 
 # ------------------------------------------------------------------ clocks sampling
@@ -124,12 +124,13 @@ def shard_sequences(blocks, tails, world, rank):
     return sorted(i for i in range(len(blocks)) if owner[i] == rank)
 
 
-def build_cache(seqs, blocks, tails, steps, device, hq=32, h=8):
+def build_cache(seqs, blocks, tails, steps, device, hq=32, h=8, rounding="exact"):
     from nsn_b200 import workloads
     from nsn_b200.paged import PagedKVCache
     c = workloads.CONFIGS[2]
     max_blocks = int(max(blocks[i] for i in seqs)) + (steps + 64) // 64 + 2
-    cache = PagedKVCache(len(seqs), h, max_blocks, bits=3, dtype=torch.float16, device=device, hq=hq)
+    cache = PagedKVCache(len(seqs), h, max_blocks, bits=3, dtype=torch.float16, device=device, hq=hq,
+                         restore_rounding=rounding)
     for j, i in enumerate(seqs):
         T = int(blocks[i]) * 64 + int(tails[i])
         gen = torch.Generator(device=device).manual_seed(c["seed"] * 100003 + i)
@@ -151,64 +152,92 @@ def step_inputs(n_seq, steps, device, hq=32, h=8, seed=2):
 
 
 # ------------------------------------------------------------------ CPU baseline (reference bridge port)
-def cpu_bridge_rate(n_seq_sample=2, budget_s=12.0, impl_label="port"):
-    """Decode tokens/s of the reference's CPU bridge (torch port) on a bounded cfg2 sample."""
+def bridge_sample(n_seq=4, device="cpu"):
+    """Four cfg2 sequences for the CPU bridge (the 1/8, 3/8, 5/8 and 7/8 quantiles of the
+    batch's lengths, mean close to the batch mean), encoded with the port's own encoder.
+    Returns (sequences, description)."""
     from oracle import bridge_torch as B
-    from oracle import nsn_oracle as O
     from nsn_b200 import workloads
-    import numpy as np
+    c = workloads.CONFIGS[2]
+    blocks, tails = workloads.np_cfg2_lengths()
+    order = sorted(range(len(blocks)), key=lambda i: (int(blocks[i]), i))
+    picks = [order[int(len(order) * (2 * j + 1) / (2 * n_seq))] for j in range(n_seq)]
+    seqs = []
+    for i in picks:
+        nb, t = int(blocks[i]), int(tails[i])
+        gen = torch.Generator(device=device).manual_seed(c["seed"] * 100003 + i)
+        k = workloads.torch_kv(gen, (1, 8, nb * 64 + t, 128), c["k_outliers"], 0.5, device=device)
+        v = workloads.torch_kv(gen, (1, 8, nb * 64 + t, 128), (), c["v_sigma"], device=device)
+        kc, km = B.encode_group(k[:, :, :nb * 64].reshape(1, 8, nb, 64, 128))
+        vc, vm = B.encode_group(v[:, :, :nb * 64].reshape(1, 8, nb, 64, 128))
+        seqs.append(B.BridgeSequence(kc, km, k[:, :, nb * 64:].contiguous(), vc, vm, v[:, :, nb * 64:].contiguous()))
+    desc = (f"cfg2 sequences {picks} ({', '.join(str(int(blocks[i])) for i in picks)} sealed blocks; batch mean "
+            f"{float(blocks.mean()):.1f}), one sequence per step in turn")
+    return seqs, desc
+
+
+def bridge_steps(seqs, n_steps, seed=11):
+    """Run n_steps single-sequence decode steps (round robin over seqs); returns seconds per step."""
+    gen = torch.Generator().manual_seed(seed)
+    times = []
+    for i in range(n_steps):
+        q = (torch.randn((1, 32, 1, 128), generator=gen) / math.sqrt(128)).half()
+        kn = torch.randn((1, 8, 1, 128), generator=gen).half()
+        vn = torch.randn((1, 8, 1, 128), generator=gen).half()
+        t0 = time.perf_counter()
+        seqs[i % len(seqs)].step(q, kn, vn)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def cpu_bridge_rate(budget_s=12.0):
+    """The cpu_baseline record: the reference's CPU bridge (torch port, all host threads)
+    on a bounded sample of cfg2 decode steps."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    blocks, tails = workloads.np_cfg2_lengths()
-    idx = list(range(n_seq_sample))
-    rng = np.random.default_rng(2)
-    cases = []
-    for i in idx:
-        nb, t = int(blocks[i]), int(tails[i])
-        k = workloads.np_kv(rng, (1, 8, nb * 64 + t, 128), workloads.K_OUTLIERS_4, 0.5)
-        v = workloads.np_kv(rng, (1, 8, nb * 64 + t, 128), (), 0.5)
-        parts = []
-        for src in (k, v):
-            qc, n, m, s, _ = O.nsn_encode(src[:, :, :nb * 64].astype(np.float32).reshape(1, 8, nb, 64, 128), 3)
-            codes = torch.from_numpy(np.frombuffer(O.pack_codes(qc, 3), np.uint8).copy().reshape(1, 8, nb, 3072))
-            parts.append((codes, tuple(torch.from_numpy(x) for x in (n, m, s)), torch.from_numpy(src[:, :, nb * 64:])))
-        q = torch.from_numpy((rng.standard_normal((1, 32, 1, 128)) / math.sqrt(128)).astype(np.float16))
-        cases.append((q, parts))
-    B.bridge_decode(cases[0][0], *cases[0][1][0], *cases[0][1][1])  # warm-up
-    done = 0
-    t0 = time.perf_counter()
-    samples = []
-    while time.perf_counter() - t0 < budget_s or done < 5:
-        for q, parts in cases:
-            s0 = time.perf_counter()
-            B.bridge_decode(q, *parts[0], *parts[1])
-            samples.append(time.perf_counter() - s0)
-            done += 1
-        if done >= 200:
-            break
-    med = statistics.median(samples)
-    return {"value": 1.0 / med, "unit": "tokens/s", "cores": threads, "kind": impl_label,
-            "sample": f"reference CPU bridge (torch port: restore_group fp16 + cat + repeat_kv + SDPA) on "
-                      f"{len(cases)} cfg2 sequences ({int(blocks[0])},{int(blocks[1])} blocks), median of {done} "
-                      f"single-sequence decodes, torch threads={threads}"}
+    seqs, desc = bridge_sample()
+    bridge_steps(seqs, len(seqs))  # warm-up
+    n, t0, times = 0, time.perf_counter(), []
+    while (time.perf_counter() - t0 < budget_s or n < 8) and n < 400:
+        times += bridge_steps(seqs, len(seqs), seed=100 + n)
+        n += len(seqs)
+    ms = 1000.0 * sum(times) / len(times)
+    return {"value": 1000.0 / ms, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "ms_per_sample_step": ms, "timed_s": sum(times),
+            "sample": f"reference CPU bridge (oracle/bridge_torch port: append by torch.cat, restore_group fp16 + "
+                      f"cat + repeat_kv + SDPA, seal-at-64 by encode_group + torch.cat) over {len(times)} "
+                      f"single-sequence decode steps of {desc}; torch threads={threads}"}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU bridge on the host cores (rank 0 only)."""
+    """--impl reference: the reference's CPU bridge on the host cores, rank 0 only.
+
+    A step is one decode step of one sequence from a fixed sample of four cfg2 sequences
+    (append, bridge attention, seal at 64), taken in turn; W untimed steps, then K timed
+    steps.  value = decoded tokens/s = 1 / mean step time, the rate the CPU path would
+    sustain over the whole batch (it decodes one sequence at a time);
+    ms_per_step * steps is the timed region."""
     if rank != 0:
         return
-    for _ in range(max(args.warmup, 0)):
-        pass
-    res = cpu_bridge_rate(budget_s=min(30.0, 3.0 * max(args.steps, 1)), impl_label="port")
-    v = res["value"]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    seqs, desc = bridge_sample()
+    bridge_steps(seqs, max(args.warmup, 1), seed=1)
+    times = bridge_steps(seqs, args.steps, seed=2)
+    ms = 1000.0 * sum(times) / len(times)
+    v = 1000.0 / ms
     line = {"metric": "decode tokens/s (batched packed-KV decode, cfg2)", "value": v, "unit": "tokens/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * 64 / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "cfg2-batched-64 (bridge: restore_group + cat + repeat_kv + SDPA on CPU)",
-                       "batch": 64, "hq": 32, "h": 8, "bits": 3},
-            "cpu_baseline": res, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                         "d2h_bytes_per_step": 0}}
+            "config": {"workload": "cfg2-batched-64 decode step (append + bridge attention + seal at 64) on the CPU: "
+                                   "restore_group + cat + repeat_kv + SDPA per sequence",
+                       "batch": 64, "hq": 32, "h": 8, "bits": 3,
+                       "step": "one sequence's decode step (a bounded sample of the batched step)",
+                       "timed_region_s": sum(times), "sample": desc},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} single-sequence decode steps of {desc}"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -519,12 +548,20 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="2: batched decode (the default bench line); 3: looped model; 4: split-KV long context + encode")
     ap.add_argument("--cfg3-steps", type=int, default=256, help="teacher-forced decode steps per sequence (cfg3)")
+    ap.add_argument("--restore-rounding", default="exact", choices=["exact", "k", "kv"],
+                    help="PagedKVCache restore_rounding of the timed cache (cfg2): exact (the headline: exact fp32 "
+                         "restore, the fastest kernel), k (the library default: K rounded like the bridge), kv "
+                         "(restore kernel, K and V rounded)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # CPU only: rank 0 runs, the other ranks exit at once (no process group, no GPU work)
+        run_reference(args, rank, world)
+        return
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -532,13 +569,6 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-
     if args.config in (1, 3, 4):
         torch.cuda.set_device(local)
         {1: run_cfg1, 3: run_cfg3, 4: run_cfg4}[args.config](args, rank, world, local, dist)
@@ -554,19 +584,20 @@ def main():
     blocks, tails = workloads.np_cfg2_lengths(args.batch)
     seqs = shard_sequences(blocks, tails, world, rank)
     total_steps = args.warmup + args.steps
-    cache = build_cache(seqs, blocks, tails, total_steps + 1, device)
+    cache = build_cache(seqs, blocks, tails, total_steps + 1, device, rounding=args.restore_rounding)
     n_seq = len(seqs)
     q, kn, vn = step_inputs(n_seq, total_steps + 1, device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
-    # bytes one attention launch reads (measured at the step it runs; sealing changes them)
+    # algorithmic bytes of one attention call (at the step it runs; sealing changes them) and
+    # the kernel's own extra reads (fp32 factors in place of fp16 norms)
     def attn_bytes():
         nb = cache.n_blocks.long()
         tl = cache.tail_len.long() + 1  # + the appended token
-        # codes + min/scale + per-token factors (fp32 renorm factors on the sealed INT3 kernel, fp16 norms otherwise)
-        per_block = 3072 + 64 * (4 if cache.uses_alpha_path() else 2) + 128 * 4
-        return int((2 * 8 * (nb * per_block + tl * 256)).sum() + 2 * n_seq * 32 * 256 + n_seq * 8 * 2 * 256)
+        algo = int((2 * 8 * (nb * BLOCK_BYTES + tl * 256)).sum() + 2 * n_seq * 32 * 256)
+        over = int((2 * 8 * nb).sum()) * FACTOR_OVERHEAD if cache.uses_alpha_path() else 0
+        return algo, over
 
     for i in range(args.warmup):
         cache.step(q[i], kn[i], vn[i])
@@ -602,7 +633,46 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     mean_step, mean_attn_max = t.tolist()
     known = [b for b in bytes_per if b is not None]
-    bytes_attn = sum(known) / len(known)
+    bytes_attn = sum(b[0] for b in known) / len(known)
+    bytes_over = sum(b[1] for b in known) / len(known)
+
+    # ---- both tensor-core kernels on the same blocks, attention only (no append): the
+    # library default (K rounded like the bridge) and the exact restore
+    kernels = None
+    if cache.uses_alpha_path() and cache.hq // cache.h <= 4:
+        from nsn_b200.kernel import decode_attention
+        from nsn_b200 import primitives as P
+        kw = dict(h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1, n_blocks=cache.n_blocks,
+                  max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
+                  tail_stride_seq=cache.h * P.BLOCK, tail_stride_head=P.BLOCK, tail_len=cache.tail_len,
+                  max_tail=P.BLOCK - 1, block_table=cache.block_table, status=cache.status, ws=cache.ws,
+                  blk_bytes=cache.blk_bytes)
+        res = {}
+        for name, ex in (("default", False), ("exact", True)):
+            for _ in range(3):
+                decode_attention(q[0], cache.k_pool, cache.v_pool, exact=ex, **kw)
+            ts = []
+            for i in range(min(args.steps, 16)):
+                flush.zero_()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                decode_attention(q[i], cache.k_pool, cache.v_pool, exact=ex, **kw)
+                a1.record(stream)
+                torch.cuda.synchronize(device)
+                ts.append(a0.elapsed_time(a1))
+            res[name] = sum(ts) / len(ts)
+        cache.check()
+        nb = cache.n_blocks.long()
+        algo = int((2 * 8 * (nb * BLOCK_BYTES + cache.tail_len.long() * 256)).sum() + 2 * n_seq * 32 * 256)
+        kernels = {"what": "attention only (no append) on the same cache state, L2 flushed, rank 0",
+                   "default_k_rounded": {"attn_ms": res["default"],
+                                         "frac": algo / (res["default"] / 1000.0) / 1e9 / peaks()[0],
+                                         "contract": "K rounded to fp16 as restore_group rounds it, V exact: "
+                                                     "within the parity bar of the reference bridge on every "
+                                                     "input (golden cases incl. unscaled cfg0 queries)"},
+                   "exact": {"attn_ms": res["exact"], "frac": algo / (res["exact"] / 1000.0) / 1e9 / peaks()[0],
+                             "contract": "exact fp32 restore of K and V: within the parity bar of the bridge "
+                                         "on this workload's 1/sqrt(128)-scaled queries (full-size cfg2 test)"}}
 
     # ---- end to end through the public API with host buffers (pinned), rank-local
     e2e = None
@@ -636,7 +706,22 @@ def main():
         e2e = {"value": args.batch / (e2e_ms / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": int(qd.numel() * 2 + knd.numel() * 2 + vnd.numel() * 2),
                "d2h_bytes_per_step": int(outh.numel() * 2), "ms_per_step": e2e_ms,
-               "path": "PagedKVCache.step (public API), pinned host q|k_new|v_new in (one copy), output out, per rank"}
+               "path": "PagedKVCache.step (public API), pinned host q|k_new|v_new in (one copy), output out, per rank; "
+                       "steps enqueued back to back (throughput)"}
+        # latency: the same step with the host waiting for each step's output
+        lat = []
+        for i in range(min(args.steps, 16)):
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            ind.copy_(inh[i % 4], non_blocking=True)
+            o = cache.step(qd, knd, vnd)
+            outh.copy_(o, non_blocking=True)
+            l1.record(stream)
+            l1.synchronize()
+            lat.append(l0.elapsed_time(l1))
+        lat.sort()
+        e2e["latency_ms_per_step"] = lat[len(lat) // 2]
+        e2e["latency_what"] = "median of device time from the input copy to the output copy, the host waiting each step"
         cache.check()
 
     hbm, peak_kind = peaks()
@@ -654,20 +739,32 @@ def main():
             "ms_per_step": mean_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "cfg2-batched-64: append 1 token + fused INT3 decode attention + seal, "
-                                   "GQA 32:8, head_dim 128, ctx U{32..256} blocks + tail U[0,63]",
+                                   "GQA 32:8, head_dim 128, ctx U{32..256} blocks + tail U[0,63], "
+                                   f"q N(0,1)/sqrt(128); PagedKVCache restore_rounding={args.restore_rounding!r}",
                        "global_batch": args.batch, "hq": 32, "h": 8, "bits": 3, "parallelism": f"batch-shard{world}",
                        "l2": "flushed (256 MiB write) before every timed step, outside the events",
                        "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
             "roofline": {"bound": "hbm",
-                         "kernel": ("nsnkv_decode_attn_alpha (attn_sealed3_kernel + attn_native_rows_kernel on the "
-                                    "tails + attn_merge_kernel)") if cache.uses_alpha_path() else
-                                   "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)",
+                         "kernel": {"exact": "nsnkv_decode_attn_alpha with NSNKV_ATTN_EXACT (PagedKVCache "
+                                             "restore_rounding='exact'): attn_sealed3_kernel + "
+                                             "attn_native_rows_kernel on the tails + attn_merge_kernel",
+                                    "k": "nsnkv_decode_attn_alpha, library default (PagedKVCache "
+                                         "restore_rounding='k'): attn_sealed_kernel (K rounded like the bridge) "
+                                         "+ attn_native_rows_kernel + attn_merge_kernel",
+                                    "kv": "nsnkv_decode_attn (attn_partial_kernel + attn_merge_kernel)"}[
+                                        args.restore_rounding],
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_kind": peak_kind, "traffic": traffic_for(bytes_attn, cache.uses_alpha_path()),
-                         "traffic_note": "ncu dram read+write of the dominant kernel at one full-size bench launch "
-                                         "(profiles/attn_sealed3_cfg2.md), scaled to this launch's algorithmic bytes",
-                         "bytes_per_launch": bytes_attn},
+                         "peak_kind": peak_kind, "traffic": None,
+                         "traffic_note": "not captured in this run (ncu figures are in the committed profile summaries)",
+                         "bytes_per_launch": bytes_attn,
+                         "bytes_what": "algorithmic: 3712 B per sealed K or V block (codes + fp16 norm + min/scale), "
+                                       "256 B per tail token of K and V (with the appended one), q and out",
+                         "overhead_bytes": bytes_over,
+                         "overhead_what": "the kernel's own extra reads: fp32 renorm factors (256 B) in place of the "
+                                          "fp16 norms (128 B) per K or V block"},
+            "restore_rounding": args.restore_rounding,
+            "kernels": kernels,
             "e2e": e2e,
             # attend: sealed kernel + tail kernel + merge (restore kernel + merge without the renorm
             # path); seal: one launch (encode + renorm + counters), two without the renorm path

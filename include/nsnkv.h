@@ -182,20 +182,27 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
  *                      k_scale = k_codes + CB + 256, k_alpha = k_codes + CB + 512,
  *                      v_codes = k_codes + CB + 768, the same offsets from v_codes, and
  *                      blk_bytes = 2 * (CB + 768)), a block moves in one copy.
- *   rec_order          1: K and V codes in the records' orders (K paired halves, V paired
- *                      rows); only the tensor-core path reads them (NSNKV_ERR_UNSUPPORTED
- *                      otherwise).
- * INT3 fp16 caches with hq / h <= 4 then run the sealed blocks on the tensor cores
- * without restoring any K or V value (the codes are the MMA operands); the norms are
- * not read.  Other shapes take the nsnkv_decode_attn path.  The result matches
- * nsnkv_decode_attn within fp32 accumulation error, not bit for bit: this path
- * skips the bridge's rounding of the restored rows to fp16.  Same workspace.
+ *   flags              NSNKV_ATTN_RECORD_ORDER: K and V codes in the records' orders (K
+ *                      paired halves, V paired rows); only the tensor-core kernels read
+ *                      them (NSNKV_ERR_UNSUPPORTED otherwise).
+ *                      NSNKV_ATTN_EXACT: attend over the exact fp32 restore instead of K
+ *                      rounded like the bridge (INT3 fp16, hq / h <= 4 only).
+ * Default (flags = NSNKV_ATTN_RECORD_ORDER, one block record per block, INT3, fp16 or
+ * bf16, hq / h <= 8): the sealed blocks run on the tensor cores.  K rows are restored
+ * and rounded to dtype as restore_group(g, dtype) rounds them
+ * (loop_kv_nb06_codec.py:36-38), so the scores are those of the reference bridge; V is
+ * applied as the exact fp32 restore with the codes as MMA operands (its rounding moves
+ * an output by about 2^-12 of its size).  NSNKV_ATTN_EXACT applies K exactly as well.
+ * The norms are not read.  Other shapes take the nsnkv_decode_attn path, which rounds
+ * both K and V.  Same workspace.
  */
+#define NSNKV_ATTN_RECORD_ORDER 1
+#define NSNKV_ATTN_EXACT 2
 int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale,
-                            const float *k_alpha, const float *v_alpha, int64_t blk_bytes, int rec_order,
+                            const float *k_alpha, const float *v_alpha, int64_t blk_bytes, int flags,
                             int64_t blk_stride_head, int64_t blk_stride_page,
                             const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,

@@ -29,6 +29,9 @@ ST_OUTPUT_NONFINITE = 8
 ST_TIMEOUT = 32
 ST_CAPACITY = 64
 
+ATTN_RECORD_ORDER = 1  # nsnkv_decode_attn_alpha flags
+ATTN_EXACT = 2
+
 F16, BF16, F32 = 0, 1, 2
 DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 

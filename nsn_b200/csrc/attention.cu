@@ -628,10 +628,11 @@ __global__ void __launch_bounds__(kThreads, 3) attn_partial_kernel(const AttnArg
 // RawSmem.  Launched after attn_sealed3_kernel with a programmatic dependency, it fills
 // slots freed in the sealed grid's last wave; the final wait keeps this grid from
 // completing before the sealed grid, so the merge launched next sees both.
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 4) attn_native_rows_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   pdl_launch_dependents();
-  attn_partial_cta<3, __half, true>(a, smem_raw);
+  attn_partial_cta<3, T, true>(a, smem_raw);
   pdl_wait();
 }
 
@@ -814,8 +815,29 @@ __host__ __device__ constexpr int vpos(int i) { return 3 * i - 8 * vwin(i); }
 __host__ __device__ constexpr uint32_t vsel(int k) {
   return k == 0 ? 0x5410u : (k == 1 || k == 3) ? 0x6521u : (k == 2 || k == 4) ? 0x7632u : 0x7733u;
 }
+// V operand of channel i (0..15 of a lane's field): codes at window positions 0..3 become
+// normal fp16 code * 2^pos (OR 1024, subtract 1024: exact), the rest stay fp16 subnormals
+// code * 2^(pos - 24).  Measured on B200: the P.V sums over the smallest subnormal operands
+// lose precision in proportion to 2^-pos (about 2^-12 of the channel's value at position 0
+// when one token carries most of the softmax weight); normal operands do not.  vunit(i) is
+// the exponent of the operand's unit, so D and the per-channel accumulators count in 2^vunit.
+constexpr int kVNormal = 3;  // highest window position given a normal operand
+__host__ __device__ constexpr int vunit(int i) { return vpos(i) <= kVNormal ? vpos(i) : vpos(i) - 24; }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+constexpr uint32_t kMagic2 = 0x64006400u;  // fp16 1024 in both halves
+
+// The V operand of channel i from window x (two tokens, one per half): see vunit.
+__device__ __forceinline__ uint32_t vop(uint32_t x, int i) {
+  const uint32_t c = x & (0x00070007u << vpos(i));
+  return vpos(i) <= kVNormal ? hsub2u(c | kMagic2, kMagic2) : c;
+}
 
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -1172,30 +1194,25 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
         }
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          constexpr uint32_t one = 0x00070007u;
           const int i0 = 2 * mt, i1 = 2 * mt + 1;
-          mma16816<__half>(D[mt], P[0][vwin(i0)] & (one << vpos(i0)), P[0][vwin(i1)] & (one << vpos(i1)),
-                           P[1][vwin(i0)] & (one << vpos(i0)), P[1][vwin(i1)] & (one << vpos(i1)), PB[ks][0],
-                           PB[ks][1]);
+          mma16816<__half>(D[mt], vop(P[0][vwin(i0)], i0), vop(P[0][vwin(i1)], i1), vop(P[1][vwin(i0)], i0),
+                           vop(P[1][vwin(i1)], i1), PB[ks][0], PB[ks][1]);
         }
       }
     }
-    // ---- epilogue: acc' += scale_c * D + min_c * 2^(pos_c - 24) * sum_t p_t alpha_t
+    // ---- epilogue: acc' += scale_c * D + min_c * 2^vunit(c) * sum_t p_t alpha_t
     {
       const uint4 *vsv = reinterpret_cast<const uint4 *>(sg.vs + 16 * g);
       const uint4 *vmv = reinterpret_cast<const uint4 *>(sg.vm + 16 * g);
       const uint4 s0 = vsv[0], s1 = vsv[1], n0 = vmv[0], n1 = vmv[1];
       const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
       const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-      float wp[8];
-#pragma unroll
-      for (int p = 0; p < 8; ++p) wp[p] = wsum * pow2(p - 24);
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         const float2 bs = Elem<__half>::to_f2(sw[mt]), ms = Elem<__half>::to_f2(nw[mt]);
-        acc[mt][0] = fmaf(bs.x, D[mt][0], fmaf(ms.x, wp[vpos(2 * mt)], acc[mt][0]));
+        acc[mt][0] = fmaf(bs.x, D[mt][0], fmaf(ms.x, wsum * pow2(vunit(2 * mt)), acc[mt][0]));
         acc[mt][1] = fmaf(bs.x, D[mt][1], acc[mt][1]);
-        acc[mt][2] = fmaf(bs.y, D[mt][2], fmaf(ms.y, wp[vpos(2 * mt + 1)], acc[mt][2]));
+        acc[mt][2] = fmaf(bs.y, D[mt][2], fmaf(ms.y, wsum * pow2(vunit(2 * mt + 1)), acc[mt][2]));
         acc[mt][3] = fmaf(bs.y, D[mt][3], acc[mt][3]);
       }
     }
@@ -1226,8 +1243,395 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int c = 16 * g + 2 * mt;
-      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * pow2(24 - vpos(2 * mt));
-      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * pow2(24 - vpos(2 * mt + 1));
+      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * pow2(-vunit(2 * mt));
+      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * pow2(-vunit(2 * mt + 1));
+    }
+  }
+  __syncthreads();
+  if (tid < G) {  // one thread per head: the warps' weights, the chunk's max and sum
+    const int n = tid;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
+      S.u.merge.wt[w][n] = wt;
+      l += wt * M.l[w][n];
+    }
+    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
+    a.part_ml[row * 2] = mx;
+    a.part_ml[row * 2 + 1] = l;
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) o += S.u.merge.wt[w][n] * M.acc[w][n][c];
+    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
+    a.part_o[row * kDim + c] = o;
+  }
+  if (st) set_status(a.status, st);
+}
+
+// ----------------------------------------------------------------- sealed INT3 blocks, K rounded like the bridge
+// attn_sealed_kernel<T, NT>: the paged cache's default path (INT3 block records with
+// per-token renorm factors, q / tails / output in T = fp16 or bf16, G <= 4 * NT query heads
+// per kv head).  The reference bridge (restore_group(g, T), then SDPA) attends over
+// restored rows rounded to T.  Rounding K moves a logit by up to ~2^-12 sum_c |q_c k_c| /
+// sqrt(128), which with unscaled N(0,1) queries moves outputs by several 1e-3; rounding V
+// moves an output by about 2^-12 of its own size.  So K is restored and rounded to T as
+// the bridge rounds it, and V stays the exact fp32 restore:
+//   K  per 16-token m-tile and register r (channels 32 tig + r and 32 tig + 16 + r of
+//      tokens g and g + 8, both at position p = (3 r) mod 8 of their 16-bit windows): one
+//      LOP3 turns the two codes into fp16 1024 + code * 2^p, one HSUB2 leaves code * 2^p
+//      (exact), and one mma.m16n8k16 with A = [code * 2^p | 2^p] and a diagonal
+//      B = [scale ; min] (both fp16, every product exact) gives 2^p * (min + scale * code)
+//      in fp32.  Times alpha_t * 2^-p and rounded to T, that is the row restore_group stores
+//      (its y = n * (d / ||d||) and this alpha_t * d differ in the order of two fp32
+//      roundings, so a rounded value can differ by one unit of T in rare ties).  The
+//      rounded pairs are the A fragments of the Q.K mma, B = q with each head in two
+//      adjacent columns, so lane (g, tig) receives head tig's score in the layout the V
+//      side of attn_sealed3_kernel consumes.
+//   V  as in attn_sealed3_kernel: codes as fp16-subnormal operands against
+//      B = p * alpha split into hi | lo, and an fp32 epilogue per block.
+// NT = 2 serves G in 5..8: two head columns tiles, the K restore shared by both.
+namespace s3 {
+
+// d = A * B with fp32 accumulation from zero (m16n8k16, fp16 operands).
+__device__ __forceinline__ void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+template <typename T> __device__ __forceinline__ uint32_t round2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t round2<__half>(float lo, float hi) {
+  __half2 p = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
+template <> __device__ __forceinline__ uint32_t round2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
+
+constexpr int kQf = 16;  // words of a lane's q fragments per head tile: 8 k-steps x (b0, b1)
+
+template <int NT>
+struct KSmem {
+  union {
+    SStage stage[kRing];
+    SMerge merge;  // after the last block of every warp
+  } u;
+  uint32_t qf[32][NT * kQf + 2];  // per lane: Q.K B fragments; stride 2 * odd words (conflict-free 64-bit loads)
+  uint16_t qs[kHeads][kDim];      // this kv head's query rows (G <= 8), raw bits of T
+  int32_t pages[kMaxChunk];
+  uint64_t full[kRing][2];        // as in SSmem
+  int32_t nissued[kRing][2];
+  int32_t failed;
+};
+
+}  // namespace s3
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(const AttnArgs a) {
+  using namespace s3;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  KSmem<NT> &S = *reinterpret_cast<KSmem<NT> *>(smem_raw);
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+  pdl_wait();               // launched with a programmatic dependency on the kernel before it
+  pdl_launch_dependents();  // the native-row chunks (next grid) may fill this grid's last wave
+  const int chunk = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = a.hq / a.h;
+  const int nb = a.nblk ? a.nblk[b] : a.nblk_const;
+  const int blk0 = chunk * a.chunk_blocks;
+  if (blk0 >= nb) return;
+  const int nloc = min(nb - blk0, a.chunk_blocks);
+  const uint16_t *qb = static_cast<const uint16_t *>(a.q) + (b * a.hq + static_cast<int64_t>(h) * G) * kDim;
+
+  // Block li of the chunk goes to warp li % 4 and stage li % kRing (one copy of the block
+  // record); the warp that finishes block li starts the copy of block li + kRing.
+  auto issue = [&](int li, int32_t page) {
+    const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
+    SStage &sg = S.u.stage[li % kRing];
+    uint64_t *bar = &S.full[li % kRing][(li / kRing) & 1];
+    S.nissued[li % kRing][(li / kRing) & 1] += 1;
+    mbar_expect_tx(bar, sizeof(SStage));
+    bulk_g2s(sg.kc, a.kc + bi * a.cs, sizeof(SStage), bar);
+  };
+  // q (8 bytes per thread and pass) and the chunk's pages staged in shared memory
+  uint2 qv[2] = {make_uint2(0u, 0u), make_uint2(0u, 0u)};
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (tid + i * kThreads < G * kDim / 4) qv[i] = reinterpret_cast<const uint2 *>(qb)[tid + i * kThreads];
+  if (warp == 0) {
+    int32_t pg = 0;
+    if (lane < nloc) pg = a.table ? a.table[b * a.table_stride + blk0 + lane] : blk0 + lane;
+    S.pages[lane] = pg;
+    if (lane == 0) {
+      S.failed = 0;
+#pragma unroll
+      for (int s = 0; s < kRing; ++s)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          mbar_init(&S.full[s][x], 1);
+          S.nissued[s][x] = 0;
+        }
+      fence_mbar_init();
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (tid + i * kThreads < G * kDim / 4) reinterpret_cast<uint2 *>(&S.qs[0][0])[tid + i * kThreads] = qv[i];
+  __syncthreads();  // q and the pages staged; the ring initialised before any copy or wait
+  if (lane == 0)
+    for (int li = warp; li < kRing && li < nloc; li += kWarps) issue(li, S.pages[li]);
+  __syncwarp();
+
+  // ---- Q.K B fragments of every lane (the same in every warp, each warp writing a quarter):
+  // k-step p pairs registers r0 = 3p mod 8 and r0 + 8 (both at window position p);
+  // b0 = q[hd][32 tig + r0 | 32 tig + 16 + r0], b1 = the same for r0 + 8, column g -> head
+  // hd = 4 nt + g / 2 (zero beyond G)
+#pragma unroll
+  for (int e = 0; e < NT * 8; ++e) {
+    if ((e & 3) != warp) continue;
+    const int nt = e >> 3, p = e & 7, r0 = (3 * p) & 7;
+    const int hd = 4 * nt + (g >> 1);
+    uint32_t w0 = 0u, w1 = 0u;
+    if (hd < G) {
+      const uint16_t *qr = S.qs[hd] + 32 * tig;
+      w0 = qr[r0] | (static_cast<uint32_t>(qr[16 + r0]) << 16);
+      w1 = qr[r0 + 8] | (static_cast<uint32_t>(qr[24 + r0]) << 16);
+    }
+    S.qf[lane][nt * kQf + 2 * p] = w0;
+    S.qf[lane][nt * kQf + 2 * p + 1] = w1;
+  }
+  __syncthreads();  // fragments written
+
+  // diagonal entries of the restore MMA's B: lane (g, tig) with tig == g / 2 holds the scale
+  // and min of channel dbase + r in half (g & 1); every other lane holds zeros
+  const int dbase = 32 * (g >> 1) + 16 * (g & 1);
+  const bool diag = tig == (g >> 1);
+  const uint32_t selE = !diag ? 0x4444u : (g & 1) ? 0x1044u : 0x4410u;  // r even: low half of the pair word
+  const uint32_t selO = !diag ? 0x4444u : (g & 1) ? 0x3244u : 0x4432u;  // r odd: high half
+  const uint32_t *qfl = S.qf[lane];
+  uint32_t qreg[NT][16];  // this lane's Q.K B fragments, kept for the whole chunk
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qreg[nt][i] = qfl[nt * kQf + i];
+
+  float m_run[NT], l_run[NT];
+  // acc[nt][mt][i]: channel 16 g + 2 mt + i of head 4 nt + tig, in units of 2^vunit
+  // (the hi and lo weight columns summed every block)
+  float acc[NT][8][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt] = -INFINITY;
+    l_run[nt] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[nt][i][0] = acc[nt][i][1] = 0.f;
+  }
+  int st = 0;
+
+  for (int li = warp; li < nloc; li += kWarps) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&S.full[li % kRing][(li / kRing) & 1], (li / (2 * kRing)) & 1,
+                                                   a.status))) {
+      if (lane == 0) S.failed = 1;
+      break;
+    }
+    const SStage &sg = S.u.stage[li % kRing];
+
+    // ---- K: restore, round to T, scores of tokens 16m+g and 16m+g+8 for head 4 nt + tig
+    uint32_t bS[16], bM[16];  // register r's diagonal B fragments (scale, min) for this block
+    {
+      const uint4 s0 = *reinterpret_cast<const uint4 *>(sg.ks + dbase);
+      const uint4 s1 = *reinterpret_cast<const uint4 *>(sg.ks + dbase + 8);
+      const uint4 n0 = *reinterpret_cast<const uint4 *>(sg.km + dbase);
+      const uint4 n1 = *reinterpret_cast<const uint4 *>(sg.km + dbase + 8);
+      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const uint32_t mw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        bS[r] = prmt(sw[r >> 1], 0u, (r & 1) ? selO : selE);
+        bM[r] = prmt(mw[r >> 1], 0u, (r & 1) ? selO : selE);
+      }
+    }
+    float s[NT][4][2];
+    {
+      const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t X0[6], X1[6];
+        {
+          const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
+          const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
+          X0[0] = u0, X0[1] = prmt(u0, u1, 0x6341u), X0[2] = u1;
+          X0[3] = prmt(u1, u2, 0x6341u), X0[4] = u2, X0[5] = prmt(u2, u2, 0x3311u);
+          X1[0] = v0, X1[1] = prmt(v0, v1, 0x6341u), X1[2] = v1;
+          X1[3] = prmt(v1, v2, 0x6341u), X1[4] = v2, X1[5] = prmt(v2, v2, 0x3311u);
+        }
+        // alpha * 2^-p of tokens 16m+g (mg) and 16m+g+8 (mh), both halves alike, p = 0 first
+        float2 mg = make_float2(sg.ka[16 * m + g], 0.f), mh = make_float2(sg.ka[16 * m + g + 8], 0.f);
+        mg.y = mg.x, mh.y = mh.x;
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          const uint32_t pw = 0x3C003C00u + static_cast<uint32_t>(p) * 0x04000400u;  // fp16 2^p in both halves
+          uint32_t klo[2], khi[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int r = ((3 * p) & 7) + 8 * e;
+            constexpr uint32_t seven = 0x00070007u;
+            const uint32_t msk = seven << p;  // vpos(r) == p
+            const uint32_t a0 = hsub2u((X0[vwin(r)] & msk) | kMagic2, kMagic2);
+            const uint32_t a1 = hsub2u((X1[vwin(r)] & msk) | kMagic2, kMagic2);
+            float d[4];
+            mma16816_z(d, a0, a1, pw, pw, bS[r], bM[r]);
+            const float2 y01 = __fmul2_rn(make_float2(d[0], d[1]), mg);
+            const float2 y23 = __fmul2_rn(make_float2(d[2], d[3]), mh);
+            klo[e] = round2<T>(y01.x, y01.y);
+            khi[e] = round2<T>(y23.x, y23.y);
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            mma16816<T>(sc[nt], klo[0], khi[0], klo[1], khi[1], qreg[nt][2 * p], qreg[nt][2 * p + 1]);
+          }
+          mg = __fmul2_rn(mg, make_float2(0.5f, 0.5f));
+          mh = __fmul2_rn(mh, make_float2(0.5f, 0.5f));
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          s[nt][m][0] = sc[nt][0] * kScale;
+          s[nt][m][1] = sc[nt][2] * kScale;
+        }
+      }
+    }
+
+    // ---- per head tile: softmax, then V: D[mt] (channel slots 16g+2mt | 16g+2mt+1, head
+    // 4 nt + tig hi | lo) over the 64 tokens with B = p * alpha_V split into fp16 hi | lo
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      uint32_t PB[4][2];
+      float wsum = 0.f;
+      {
+        float bm = -INFINITY;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) bm = fmaxf(bm, fmaxf(s[nt][m][0], s[nt][m][1]));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+        const float m_new = fmaxf(m_run[nt], bm);
+        const float r = m_run[nt] == -INFINITY ? 0.f : ex2_neg((m_run[nt] - m_new) * kLog2e);
+        const float mb = m_new * kLog2e;
+        float psum = 0.f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const float p = ex2_neg(fmaf(s[nt][m][i], kLog2e, -mb));
+            const float pv = p * sg.va[16 * m + g + 8 * i];
+            psum += p;
+            wsum += pv;
+            PB[m][i] = movtrans(split_hilo(pv));
+          }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+        l_run[nt] = l_run[nt] * r + psum;  // this lane's tokens only: the head's sum is formed at the end
+        m_run[nt] = m_new;
+        if (!__all_sync(0xffffffffu, r == 1.f)) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[nt][i][0] *= r, acc[nt][i][1] *= r;
+        }
+      }
+      float D[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k]
+        uint32_t P[2][6];
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int j = 8 * ks + tig + 4 * pr;
+          const uint32_t w0 = vw[24 * j], w1 = vw[24 * j + 1], w2 = vw[24 * j + 2];
+          P[pr][0] = w0;
+          P[pr][1] = prmt(w0, w1, 0x6341u);
+          P[pr][2] = w1;
+          P[pr][3] = prmt(w1, w2, 0x6341u);
+          P[pr][4] = w2;
+          P[pr][5] = prmt(w2, w2, 0x3311u);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int i0 = 2 * mt, i1 = 2 * mt + 1;
+          mma16816<__half>(D[mt], vop(P[0][vwin(i0)], i0), vop(P[0][vwin(i1)], i1), vop(P[1][vwin(i0)], i0),
+                           vop(P[1][vwin(i1)], i1), PB[ks][0], PB[ks][1]);
+        }
+      }
+      // epilogue: acc' += scale_c * D + min_c * 2^vunit(c) * sum_t p_t alpha_t
+      const uint4 *vsv = reinterpret_cast<const uint4 *>(sg.vs + 16 * g);
+      const uint4 *vmv = reinterpret_cast<const uint4 *>(sg.vm + 16 * g);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint4 sv = vsv[half], mv = vmv[half];
+        const uint32_t sw4[4] = {sv.x, sv.y, sv.z, sv.w}, mw4[4] = {mv.x, mv.y, mv.z, mv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int mt = 4 * half + q;
+          const float2 bs = Elem<__half>::to_f2(sw4[q]), ms = Elem<__half>::to_f2(mw4[q]);
+          const float w0 = wsum * __int_as_float((127 + vunit(2 * mt)) << 23);
+          const float w1 = wsum * __int_as_float((127 + vunit(2 * mt + 1)) << 23);
+          acc[nt][mt][0] = fmaf(bs.x, D[mt][0] + D[mt][1], fmaf(ms.x, w0, acc[nt][mt][0]));
+          acc[nt][mt][1] = fmaf(bs.y, D[mt][2] + D[mt][3], fmaf(ms.y, w1, acc[nt][mt][1]));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && li + kRing < nloc) issue(li + kRing, S.pages[li + kRing]);
+  }
+  __syncthreads();
+  if (S.failed) {  // a copy never landed: give every started copy a bounded chance to finish
+    if (tid == 0)
+      for (int s2 = 0; s2 < kRing; ++s2)
+        for (int x = 0; x < 2; ++x)
+          if (S.nissued[s2][x] > 0) mbar_wait_bounded(&S.full[s2][x], (S.nissued[s2][x] - 1) & 1, a.status);
+    __syncthreads();  // the stages are reused below
+  }
+
+  // ---- combine the four warps and write this chunk's partial
+  MergeSmem &M = S.u.merge.part;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float l = l_run[nt];
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    const int hd = 4 * nt + tig;
+    // a non-finite score or weight leaves the running sum non-finite (checked once per chunk;
+    // the merge kernel also checks every output)
+    if (hd < G && !isfinite(l)) st |= NSNKV_ST_OUTPUT_NONFINITE;
+    if (hd < G) {
+      if (g == 0) {
+        M.m[warp][hd] = m_run[nt];
+        M.l[warp][hd] = l;
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int c = 16 * g + 2 * mt;
+        M.acc[warp][hd][c] = acc[nt][mt][0] * __int_as_float((127 - vunit(2 * mt)) << 23);
+        M.acc[warp][hd][c + 1] = acc[nt][mt][1] * __int_as_float((127 - vunit(2 * mt + 1)) << 23);
+      }
     }
   }
   __syncthreads();
@@ -1273,11 +1677,11 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   return static_cast<int>(ch);
 }
 
-// The sealed INT3 kernel's chunks: about one CTA per resident slot (148 SMs x 4), in
+// The sealed INT3 kernels' chunks: about one CTA per resident slot (148 SMs x per_sm), in
 // multiples of 4 blocks (one round of its four warps), up to 32 blocks.
-static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail) {
+static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail, int per_sm) {
   const int64_t units = batch * h;
-  const int64_t target = 148 * 4;
+  const int64_t target = 148 * per_sm;
   const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
   const int64_t per_unit = (target + units - 1) / units;
   int64_t ch = (work + per_unit - 1) / per_unit;
@@ -1334,7 +1738,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint16_t *k_norm, const uint16_t *k_min, const uint16_t *k_scale,
                             const uint8_t *v_codes, const uint16_t *v_norm, const uint16_t *v_min,
                             const uint16_t *v_scale, const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
-                            int rec_order, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
+                            int flags, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
                             int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
                             void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
                             const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new,
@@ -1359,7 +1763,8 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   if (batch > 65535 || h > 65535) return NSNKV_ERR_ARG;
   const int64_t cb = code_bytes(bits);
   if (blk_bytes != 0 && (blk_bytes < cb || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
-  if (rec_order != 0 && rec_order != 1) return NSNKV_ERR_ARG;
+  if (flags & ~(NSNKV_ATTN_RECORD_ORDER | NSNKV_ATTN_EXACT)) return NSNKV_ERR_ARG;
+  const bool rec_order = (flags & NSNKV_ATTN_RECORD_ORDER) != 0, exact = (flags & NSNKV_ATTN_EXACT) != 0;
 
   AttnArgs a{};
   a.cs = blk_bytes ? blk_bytes : cb;
@@ -1406,20 +1811,37 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   const int G = hq / h;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = NSNKV_OK;
-  const bool sealed_path = k_alpha && v_alpha && bits == 3 && dtype == NSNKV_F16 && G <= 4;
-  if (rec_order && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // record orders: tensor-core kernel only
+  // Sealed blocks with renorm factors go to a tensor-core kernel: exact restore
+  // (attn_sealed3_kernel: fp16, G <= 4, either code order) or, by default, K rounded to the
+  // cache dtype as the bridge rounds it (attn_sealed_kernel: record orders, G <= 8).
+  const bool sealed_exact = k_alpha && v_alpha && exact && bits == 3 && dtype == NSNKV_F16 && G <= 4;
+  const bool sealed_round = k_alpha && v_alpha && !exact && rec_order && bits == 3 && G <= kHeads;
+  const bool sealed_path = sealed_exact || sealed_round;
+  if (rec_order && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // record orders: tensor-core kernels only
+  if (exact && max_blocks > 0 && !sealed_exact) return NSNKV_ERR_UNSUPPORTED;
   if (sealed_path && max_blocks > 0) {
-    // sealed chunks on the tensor-core kernel, native-row chunks on attn_partial_kernel
+    // sealed chunks on a tensor-core kernel, native-row chunks on attn_native_rows_kernel
     if (!aligned16(k_alpha) || !aligned16(v_alpha)) return NSNKV_ERR_ARG;
+    if (sealed_round && !a.one_copy) return NSNKV_ERR_ARG;  // the rounding kernel moves whole block records
     a.ka = k_alpha;
     a.va = v_alpha;
-    const size_t smem = sizeof(s3::SSmem);
-    const auto kern = rec_order ? attn_sealed3_kernel<true> : attn_sealed3_kernel<false>;
+    size_t smem = sizeof(s3::SSmem);
+    void (*kern)(const AttnArgs) = rec_order ? attn_sealed3_kernel<true> : attn_sealed3_kernel<false>;
+    int per_sm = 4;
+    if (sealed_round) {
+      const bool wide = G > 4;
+      per_sm = wide ? 2 : 3;
+      smem = wide ? sizeof(s3::KSmem<2>) : sizeof(s3::KSmem<1>);
+      if (dtype == NSNKV_F16)
+        kern = wide ? attn_sealed_kernel<__half, 2> : attn_sealed_kernel<__half, 1>;
+      else
+        kern = wide ? attn_sealed_kernel<__nv_bfloat16, 2> : attn_sealed_kernel<__nv_bfloat16, 1>;
+    }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return NSNKV_ERR_CUDA;
     // whole chunks of up to 32 blocks (8 per warp) amortise the per-CTA set-up; fewer chunks
     // than nsnkv_decode_attn_workspace_bytes() sized for, so the same workspace holds them
-    a.chunk_blocks = s3_chunk_blocks(batch, h, max_blocks, max_tail);
+    a.chunk_blocks = s3_chunk_blocks(batch, h, max_blocks, max_tail, per_sm);
     a.max_chunks = max_chunks_for(max_blocks, max_tail, a.chunk_blocks);
     a.part_ml = a.part_o + batch * hq * static_cast<int64_t>(a.max_chunks) * kDim;
     // sealed chunks here, native-row chunks on attn_partial_kernel, then the merge kernel
@@ -1450,7 +1872,8 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, attn_native_rows_kernel, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
+      const auto tails = dtype == NSNKV_F16 ? attn_native_rows_kernel<__half> : attn_native_rows_kernel<__nv_bfloat16>;
+      if (cudaLaunchKernelEx(&cfg, tails, a) != cudaSuccess) return NSNKV_ERR_LAUNCH;
       rc = cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
     }
   } else {
@@ -1502,7 +1925,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint8_t *k_codes, const uint16_t *k_norm, const uint16_t *k_min,
                             const uint16_t *k_scale, const uint8_t *v_codes, const uint16_t *v_norm,
                             const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
-                            const float *v_alpha, int64_t blk_bytes, int rec_order, int64_t blk_stride_head,
+                            const float *v_alpha, int64_t blk_bytes, int flags, int64_t blk_stride_head,
                             int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail,
                             void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
@@ -1511,7 +1934,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             int32_t *status, void *stream) {
   if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
-                          v_scale, k_alpha, v_alpha, blk_bytes, rec_order, blk_stride_head, blk_stride_page,
+                          v_scale, k_alpha, v_alpha, blk_bytes, flags, blk_stride_head, blk_stride_page,
                           block_table, table_stride, n_blocks, n_blocks_const, max_blocks, k_tail, v_tail,
                           tail_stride_seq, tail_stride_head, tail_len, tail_len_const, max_tail, k_new, v_new, out,
                           out_f32, lse, workspace, workspace_bytes, status, stream);

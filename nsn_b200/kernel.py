@@ -34,8 +34,16 @@ _workspace_cache: dict = {}
 
 
 def workspace(nbytes: int, device) -> torch.Tensor:
-    """Reusable per-device scratch for the split-KV partials (grown on demand)."""
-    key = (str(device),)
+    """Reusable scratch for the split-KV partials, one buffer per (device, current stream).
+
+    Calls on one stream run in order, so they can share a buffer; calls on different
+    streams get different buffers and never race on the partials.  A buffer that grows is
+    replaced on its own stream only, where every earlier call has been ordered before the
+    caching allocator can hand the old memory out again.
+    """
+    device = torch.device(device)
+    stream = torch.cuda.current_stream(device)
+    key = (str(device), stream.cuda_stream)
     buf = _workspace_cache.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -46,7 +54,7 @@ def workspace(nbytes: int, device) -> torch.Tensor:
 def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_page, n_blocks, max_blocks,
                      k_tail=None, v_tail=None, tail_stride_seq=0, tail_stride_head=0, tail_len=0, max_tail=0,
                      block_table=None, k_new=None, v_new=None, out=None, out_f32=None, lse=None, status=None,
-                     ws=None, blk_bytes=None):
+                     ws=None, blk_bytes=None, exact=False):
     """Direct binding of nsnkv_decode_attn (nsnkv_decode_attn_alpha when both pools carry
     "alpha" or their arrays are fields of block records).
 
@@ -55,6 +63,8 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     (or None when max_blocks == 0); n_blocks/tail_len either ints (same for every
     sequence) or int32 CUDA tensors [B].  blk_bytes: the block stride of the
     codes / min / scale / alpha arrays (None: read from the tensors' strides, 0: dense).
+    With renorm factors, K rows are rounded to the cache dtype as the reference bridge
+    rounds them unless ``exact`` (then K and V are both the exact fp32 restore).
     Returns (out, status).
     """
     L.require_cuda()
@@ -84,10 +94,12 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     w.require(orders in ((0, 0), (2, 1)), "pool code orders (K paired halves with V paired rows, or neither)")
     rec_order = int(orders == (2, 1))
     w.require(not rec_order or has_alpha, "the block records' code orders need the renorm-factor path")
+    w.require(not exact or has_alpha, "exact attention needs the renorm factors")
     if has_alpha or blk_bytes:
         entry, name = lib.nsnkv_decode_attn_alpha, "nsnkv_decode_attn_alpha"
         alphas = (L.ptr(kp["alpha"]), L.ptr(vp["alpha"])) if has_alpha else (L.ptr(None), L.ptr(None))
-        blocks = blocks + alphas + (int(blk_bytes), rec_order)
+        flags = (L.ATTN_RECORD_ORDER if rec_order else 0) | (L.ATTN_EXACT if exact else 0)
+        blocks = blocks + alphas + (int(blk_bytes), flags)
     else:
         entry, name = lib.nsnkv_decode_attn, "nsnkv_decode_attn"
     rc = entry(

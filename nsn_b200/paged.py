@@ -22,7 +22,7 @@ Layout (head-major pools so one sequence's blocks of one head are contiguous):
   whenever a block is (sealed, prefilled or imported) so attention does not recompute
   ||d|| per step; derived data, not part of the reference's format or of the exports
   block (sequence b, head j, block i) = pool row j, page block_table[b, i]
-  For caches on the tensor-core path (INT3, fp16, hq / h <= 4) codes / min / scale /
+  For caches on the tensor-core path (INT3, hq / h <= 8) codes / min / scale /
   alpha of K and then of V are fields of one block record per (head, page),
   records [h, pages, 7680] uint8, so the attention kernel moves a block with one copy;
   the pool dicts hold views of those fields (norms stay dense).
@@ -145,33 +145,48 @@ def block_record_pools(h: int, pages: int, bits: int, device):
     return rec, kp, vp
 
 
+ROUNDING_MODES = ("k", "kv", "exact")
+
+
 class PagedKVCache:
     def __init__(self, batch: int, h: int, max_blocks: int, bits: int = 3, dtype=torch.float16, device="cuda",
-                 hq: int | None = None, bridge_rounding: bool = False):
-        """``bridge_rounding=True`` attends through the restore kernel, which rounds every
-        restored K/V row to the cache dtype exactly as the reference bridge
-        (restore_group + SDPA) does.  The default keeps per-token renorm factors and, for
-        INT3 fp16 caches with hq / h <= 4, attends over the codes directly on the tensor
-        cores: the exact fp32 restore, with no rounding of restored rows."""
+                 hq: int | None = None, bridge_rounding: bool = False, restore_rounding: str | None = None):
+        """How attention treats the restored rows (``restore_rounding``):
+
+        ``"k"`` (default): K rows rounded to the cache dtype exactly as the reference
+            bridge (restore_group(g, dtype) + SDPA) rounds them, V applied as the exact fp32
+            restore.  INT3 caches with hq / h <= 8 keep per-token renorm factors in block
+            records and attend over them on the tensor cores; other shapes use the restore
+            kernel, which rounds K and V.
+        ``"kv"`` (or ``bridge_rounding=True``): the restore kernel, K and V rounded as the
+            bridge rounds them.
+        ``"exact"``: K and V both the exact fp32 restore, nothing rounded (INT3 fp16
+            caches with hq / h <= 4): the fastest kernel, a stricter contract than the
+            bridge's, whose fp16 rounding of K moves outputs by up to a few 1e-3 when the
+            queries are not scaled down.
+        """
         w.require(batch > 0 and h > 0 and max_blocks > 0 and bits in (3, 4, 5), "paged cache shape")
         w.require(dtype in (torch.float16, torch.bfloat16), "paged cache dtype")
+        mode = restore_rounding if restore_rounding is not None else ("kv" if bridge_rounding else "k")
+        w.require(mode in ROUNDING_MODES, "paged cache restore_rounding")
         L.require_cuda()
         self.batch, self.h, self.max_blocks, self.bits, self.dtype = batch, h, max_blocks, bits, dtype
         self.hq = hq or h
-        self.bridge_rounding = bridge_rounding
+        w.require(self.hq % h == 0 and self.hq // h <= 8, "paged cache head grouping")
+        self.restore_rounding = mode
+        self.bridge_rounding = mode == "kv"
+        w.require(mode != "exact" or (bits == 3 and dtype == torch.float16 and self.hq // h <= 4),
+                  "exact attention needs an INT3 fp16 cache with hq / h <= 4")
         self.device = torch.device(device)
         self.pages = batch * max_blocks
         cb = w.code_bytes(bits)
         dev = self.device
 
         def pool():
-            p = dict(codes=torch.zeros((h, self.pages, cb), dtype=torch.uint8, device=dev),
-                     norm=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float16, device=dev),
-                     min=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
-                     scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev))
-            if not bridge_rounding:
-                p["alpha"] = torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float32, device=dev)
-            return p
+            return dict(codes=torch.zeros((h, self.pages, cb), dtype=torch.uint8, device=dev),
+                        norm=torch.zeros((h, self.pages, w.BLOCK), dtype=torch.float16, device=dev),
+                        min=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev),
+                        scale=torch.zeros((h, self.pages, w.DIM), dtype=torch.float16, device=dev))
 
         self.records = None
         self.blk_bytes = 0
@@ -294,11 +309,11 @@ class PagedKVCache:
             tail_stride_seq=self.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=self.tail_len,
             max_tail=w.BLOCK - 1, block_table=self.block_table, k_new=k_new, v_new=v_new,
             out=self.out if out is None else out, out_f32=out_f32, lse=lse, status=self.status, ws=self.ws,
-            blk_bytes=self.blk_bytes)[0]
+            blk_bytes=self.blk_bytes, exact=self.restore_rounding == "exact")[0]
 
     def seal(self, pending_append: int = 1):
         lib = L.load()
-        if self.bridge_rounding:
+        if self.records is None:
             rc = lib.nsnkv_seal_full_tails(
                 self.batch, self.h, self.bits, L.DTYPE_CODE[self.dtype], L.ptr(self.k_tail), L.ptr(self.v_tail),
                 self.h * w.BLOCK, w.BLOCK, L.ptr(self.tail_len), L.ptr(self.n_blocks), pending_append,
@@ -316,8 +331,7 @@ class PagedKVCache:
             L.ptr(self.k_pool["codes"]), L.ptr(self.k_pool["norm"]), L.ptr(self.k_pool["min"]),
             L.ptr(self.k_pool["scale"]), L.ptr(self.v_pool["codes"]), L.ptr(self.v_pool["norm"]),
             L.ptr(self.v_pool["min"]), L.ptr(self.v_pool["scale"]), L.ptr(self.k_pool["alpha"]),
-            L.ptr(self.v_pool["alpha"]), self.blk_bytes, int(self.records is not None),
-            L.ptr(self.seal_counters), self.pages, 1,
+            L.ptr(self.v_pool["alpha"]), self.blk_bytes, 1, L.ptr(self.seal_counters), self.pages, 1,
             L.ptr(self.status), L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")
 
@@ -334,16 +348,26 @@ class PagedKVCache:
 
     # ------------------------------------------------------------ accounting
     def kv_bytes(self):
-        """Bytes held for K and V: codes + fp16 metadata + 12-byte headers + fp16 tail tokens."""
+        """Bytes held for K and V: what the reference's planned_bytes counts (codes, fp16
+        metadata, 12-byte headers, native tail tokens; loop_kv_nb06_primitives.py:72-81)
+        plus this cache's own derived data, the fp32 renorm factors (64 per K or V block)."""
+        return self.reference_kv_bytes() + self.factor_bytes()
+
+    def reference_kv_bytes(self):
+        """planned_bytes of the cached tokens: codes + fp16 metadata + headers + tails."""
         nb = int(self.n_blocks.sum())
         t = int(self.tail_len.sum())
         per_block = w.code_bytes(self.bits) + w.BLOCK * 2 + w.DIM * 4 + 12
         return 2 * self.h * (nb * per_block + t * w.DIM * 2)
 
+    def factor_bytes(self):
+        """Bytes of the per-token renorm factors kept beside the sealed blocks (0 without)."""
+        return 2 * self.h * int(self.n_blocks.sum()) * w.BLOCK * 4 if self.records is not None else 0
+
     def uses_alpha_path(self):
-        """True when attend() runs the sealed blocks through the renorm-factor kernel."""
-        return (not self.bridge_rounding and self.bits == 3 and self.dtype == torch.float16
-                and self.hq // self.h <= 4)
+        """True when attend() runs the sealed blocks on the tensor-core kernels (block
+        records with per-token renorm factors)."""
+        return self.restore_rounding != "kv" and self.bits == 3 and self.hq // self.h <= 8
 
     def read_bytes_per_step(self):
         """Algorithmic bytes one attend() reads: sealed blocks (codes + metadata) and tails, q and out.

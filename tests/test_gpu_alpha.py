@@ -1,13 +1,14 @@
 """GPU tests of the renorm-factor path (nsnkv_block_renorm, nsnkv_seal_full_tails_alpha,
-nsnkv_decode_attn_alpha).
+nsnkv_decode_attn_alpha) in its exact mode.
 
 * alpha = n / max(||min + scale * code||, 1e-12) per token against the oracle's decode.
-* Attention through the paged cache (sealed blocks on attn_sealed3_kernel, tails on
-  attn_partial_kernel) against fp64 attention over the exact fp32 restore of the
-  same blocks (nsn_decode without the final cast), with a tight bar, and against the
-  reference bridge (rows rounded to fp16) with the parity bar.
+* Attention through a paged cache built with restore_rounding="exact" (sealed blocks on
+  attn_sealed3_kernel, tails on attn_native_rows_kernel) against fp64 attention over
+  the exact fp32 restore of the same blocks (nsn_decode without the final cast), with a
+  tight bar, and against the reference bridge (rows rounded to fp16) with the parity bar.
 * GQA groups 1..4, q magnitudes that need the exponent shift, zero-norm tokens,
   constant blocks, chunk sizes that leave warps idle, appended tokens and seals.
+The default mode (K rounded like the bridge) is tested in test_gpu_sealed.py.
 """
 import numpy as np
 import pytest
@@ -23,10 +24,10 @@ TIGHT = (1e-4, 2e-5)  # (rtol, atol) against the exact fp32 restore: fp32 accumu
 def mma_bar(q, k, v):
     """Extra absolute bar for the tensor-core dot products over codes.
 
-    The codes enter mma.sync as fp16 subnormals, for which the tensor core keeps about
-    2^-18.5 of sum |products| per k-group (a B200 probe; normal fp16 operands keep 2^-23).
-    A logit therefore carries up to ~2^-16 * sum_c |q_c k_c| / sqrt(128), and the output
-    moves by at most that times max |v|.  With 1/sqrt(128)-scaled queries this is ~1e-5."""
+    The K codes enter mma.sync as fp16 subnormals, whose sums the tensor core keeps to
+    less than fp32 precision.  The bar allows each logit an error of 2^-16 * sum_c |q_c k_c|
+    / sqrt(128), which moves an output by at most that times max |v|; every case in this
+    file stays inside it.  With 1/sqrt(128)-scaled queries the bar is about 1e-5."""
     rep = q.shape[0] // k.shape[0]
     sabs = np.einsum("jd,jtd->jt", np.abs(q), np.abs(np.repeat(k, rep, 0))).max() / np.sqrt(128.0)
     return 2.0 ** -16 * sabs * np.abs(v).max()
@@ -70,13 +71,13 @@ def history_oracle(hk, hv, nb, rows="exact"):
     return np.concatenate(parts_k, 1), np.concatenate(parts_v, 1)
 
 
-def make_cache(rng, lens, h, hq, max_blocks, q_scale=1.0, bridge_rounding=False):
+def make_cache(rng, lens, h, hq, max_blocks, q_scale=1.0, mode="exact"):
     from nsn_b200 import workloads
     from nsn_b200.paged import PagedKVCache
     hk = [workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5) for L in lens]
     hv = [workloads.np_kv(rng, (h, L, 128), (), 0.5) for L in lens]
     cache = PagedKVCache(len(lens), h, max_blocks=max_blocks, bits=3, dtype=torch.float16, hq=hq,
-                         bridge_rounding=bridge_rounding)
+                         restore_rounding=mode)
     for b in range(len(lens)):
         cache.prefill(b, torch.from_numpy(hk[b]).cuda(), torch.from_numpy(hv[b]).cuda())
     q = (rng.standard_normal((len(lens), hq, 128)) * q_scale / np.sqrt(128)).astype(np.float16)
@@ -162,7 +163,7 @@ def test_alpha_path_zero_and_constant_blocks():
     hv[0, 128:192] = 0.5         # a constant V block: scale 0
     hk[1, 200:203] = 0.0         # zero-norm tokens inside a block
     hv[1, 300] = 0.0
-    cache = PagedKVCache(1, h, max_blocks=8, bits=3, dtype=torch.float16, hq=hq)
+    cache = PagedKVCache(1, h, max_blocks=8, bits=3, dtype=torch.float16, hq=hq, restore_rounding="exact")
     cache.prefill(0, torch.from_numpy(hk).cuda(), torch.from_numpy(hv).cuda())
     q = (rng.standard_normal((1, hq, 128)) / np.sqrt(128)).astype(np.float16)
     out32 = torch.empty((1, hq, 128), dtype=torch.float32, device="cuda")
@@ -176,7 +177,7 @@ def test_alpha_path_zero_and_constant_blocks():
 
 
 def test_alpha_path_agrees_with_restore_path():
-    """The same cache attended through nsnkv_decode_attn (norms, bridge rounding) and the renorm-factor kernel."""
+    """The same cache attended through nsnkv_decode_attn (norms, bridge rounding) and the exact renorm-factor kernel."""
     from nsn_b200.kernel import decode_attention
     from nsn_b200 import primitives as w
     rng = np.random.default_rng(11)
@@ -227,14 +228,13 @@ def test_seal_writes_renorm_factors():
 def test_bridge_rounding_option_matches_bridge_on_unscaled_queries():
     """cfg0-style queries (N(0,1), not scaled by 1/sqrt(128)): the bridge's fp16 rounding of
     restored rows alone moves outputs past the parity bar, so a cache built with
-    bridge_rounding=True (restore kernel, rows rounded like restore_group) is the one that
-    matches the bridge there; the default path matches the exact restore."""
-    rng = np.random.default_rng(9)
+    restore_rounding="kv" (restore kernel, rows rounded like restore_group) matches the
+    bridge there, and the exact mode matches the exact restore."""
     lens = [64 * 15 + 3, 64 * 8]
     for bridge in (True, False):
         r = np.random.default_rng(9)
         cache, hk, hv, q = make_cache(r, lens, 2, 8, max_blocks=16, q_scale=float(np.sqrt(128)),
-                                      bridge_rounding=bridge)
+                                      mode="kv" if bridge else "exact")
         assert cache.uses_alpha_path() == (not bridge)
         out32 = torch.empty((len(lens), 8, 128), dtype=torch.float32, device="cuda")
         out = cache.attend(torch.from_numpy(q).cuda(), out_f32=out32)
@@ -301,8 +301,8 @@ def test_block_records_match_dense_arrays():
     assert w.blk_bytes_of(dense[0], 3) == 0
     fa = torch.empty(q.shape, device="cuda")
     fb = torch.empty(q.shape, device="cuda")
-    a, sa = decode_attention(qt, cache.k_pool, cache.v_pool, out_f32=fa, **common)
-    b, sb = decode_attention(qt, dense[0], dense[1], out_f32=fb, **common)
+    a, sa = decode_attention(qt, cache.k_pool, cache.v_pool, out_f32=fa, exact=True, **common)
+    b, sb = decode_attention(qt, dense[0], dense[1], out_f32=fb, exact=True, **common)
     torch.cuda.synchronize()
     assert int(sa.item()) == 0 and int(sb.item()) == 0
     assert torch.allclose(fa, fb, rtol=TIGHT[0], atol=TIGHT[1]), (fa - fb).abs().max().item()

@@ -132,6 +132,83 @@ def test_bridge_attention_oracle(name):
     assert ok, (name, err)
 
 
+# ---------------------------------------------------------------- the timed CPU bridge port
+def _golden_attention_inputs(name):
+    e = G.index()["attention"][name]
+    dt = e["dtype"]
+    if name == "cfg0":
+        from nsn_b200 import workloads
+        k, v, _, _, _ = workloads.np_config(0)
+        kin, vin = k.astype(np.float32), v.astype(np.float32)
+    else:
+        kin = G.bits_to_float32(G.get(f"attn_{name}_k_in"), dt)
+        vin = G.bits_to_float32(G.get(f"attn_{name}_v_in"), dt)
+    q = G.bits_to_float32(G.get(f"attn_{name}_q"), dt)
+    return e, kin.reshape(1, e["h"], -1, 128), vin.reshape(1, e["h"], -1, 128), q.reshape(1, e["hq"], 1, 128)
+
+
+@pytest.mark.parametrize("name", sorted(G.index()["attention"]))
+def test_bridge_port_reproduces_reference_sdpa(name):
+    """oracle/bridge_torch.bridge_decode (the timed CPU baseline) gives the reference's
+    recorded SDPA output bit for bit, with groups from the port's own encoder."""
+    import torch
+    from oracle import bridge_torch as B
+    e, kin, vin, q = _golden_attention_inputs(name)
+    dt = {"float16": torch.float16, "bfloat16": torch.bfloat16}[e["dtype"]]
+    nb, h = e["blocks"], e["h"]
+    parts = []
+    for src in (kin, vin):
+        x = torch.from_numpy(src).to(dt)
+        codes, metas = B.encode_group(x[:, :, :nb * 64].reshape(1, h, nb, 64, 128))
+        parts.append((codes, metas, x[:, :, nb * 64:].contiguous()))
+    out = B.bridge_decode(torch.from_numpy(q).to(dt), *parts[0], *parts[1])
+    want = G.get(f"attn_{name}_sdpa")
+    assert out.contiguous().view(torch.int16).numpy().view(np.uint16).tobytes() == want.tobytes(), name
+
+
+@pytest.mark.parametrize("name", sorted(G.index()["encode"]))
+def test_bridge_port_encoder_bit_exact(name):
+    """The port's nsn_encode + pack3 (its seal step) give the reference's recorded codes and metas."""
+    import torch
+    from oracle import bridge_torch as B
+    x, strided, entry = G.encode_input(name)
+    rec = entry["bits"].get("3")
+    if strided or rec is None or "raises" in rec:
+        pytest.skip("channel-strided or rejected input: the port takes contiguous rows")
+    dt = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}[entry["dtype"]]
+    q, metas = B.nsn_encode(torch.from_numpy(x).to(dt), 3)
+    assert G.matches(rec["key"] + "_packed", B.pack3(q).numpy())
+    for tag, t in zip(("n", "m", "s"), metas):
+        assert G.matches(f"{rec['key']}_{tag}", t.contiguous().view(torch.int16).numpy().view(np.uint16)), tag
+
+
+def test_bridge_sequence_step_and_seal():
+    """BridgeSequence.step equals bridge_decode over the history plus the new token, and
+    a tail reaching 64 tokens is encoded into one more block."""
+    import torch
+    from oracle import bridge_torch as B
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(4)
+    h, hq, nb, t = 2, 8, 2, 62
+    k = torch.from_numpy(workloads.np_kv(rng, (1, h, nb * 64 + t + 3, 128), workloads.K_OUTLIERS_4, 0.5))
+    v = torch.from_numpy(workloads.np_kv(rng, (1, h, nb * 64 + t + 3, 128), (), 0.5))
+    kc, km = B.encode_group(k[:, :, :nb * 64].reshape(1, h, nb, 64, 128))
+    vc, vm = B.encode_group(v[:, :, :nb * 64].reshape(1, h, nb, 64, 128))
+    seq = B.BridgeSequence(kc, km, k[:, :, nb * 64:nb * 64 + t], vc, vm, v[:, :, nb * 64:nb * 64 + t])
+    for i in range(3):
+        T = nb * 64 + t + i + 1
+        q = torch.from_numpy(rng.standard_normal((1, hq, 1, 128)).astype(np.float16))
+        kk, vv = k[:, :, T - 1:T], v[:, :, T - 1:T]
+        sealed = seq.k[0].shape[2]
+        want = B.bridge_decode(q, seq.k[0], seq.k[1], torch.cat((seq.k[2], kk), 2),
+                               seq.v[0], seq.v[1], torch.cat((seq.v[2], vv), 2))
+        assert torch.equal(seq.step(q, kk, vv), want)
+        assert seq.k[0].shape[2] == sealed + (1 if T - 64 * sealed == 64 else 0)
+    assert seq.k[0].shape[2] == nb + 1 and seq.k[2].shape[2] == 1
+    codes, metas = B.encode_group(k[:, :, nb * 64:(nb + 1) * 64].reshape(1, h, 1, 64, 128))
+    assert torch.equal(seq.k[0][:, :, nb:], codes) and all(torch.equal(a[:, :, nb:], b) for a, b in zip(seq.k[1], metas))
+
+
 # ---------------------------------------------------------------- library INT3 container
 def _asym_input(case):
     """float32 values in the input's logical order (a transposed input was recorded through its view)."""
