@@ -1,8 +1,8 @@
 """Model adapter: single-query decode of an HF attention module over the packed cache.
 
-Mirrors experiments/nb06/source/loop_kv_nb06_attention.py:13-88. ``make_cache`` is a
-PackedCache with deferred restoration (``append_for_attention`` appends and seals
-without materialising K/V). ``decode`` runs the projections, RoPE and the fused packed
+Serves the role of experiments/nb06/source/loop_kv_nb06_attention.py:13-88. ``make_cache``
+is a PackedCache whose ``append_for_attention`` appends a decode token without
+restoring the slot's K/V. ``decode`` runs the projections, RoPE and the fused packed
 attention of one query. ``install`` patches every layer's ``self_attn.forward`` and
 returns a ``restore`` callable.
 
@@ -62,6 +62,14 @@ class ListCacheBase:
 
 
 def make_cache(base=ListCacheBase):
+    """The connection cache class: a PackedCache over `base` as the patched layers use it.
+
+    Besides the packed cache it carries the arm, the check granularity and per-slot
+    counters, and ``append_for_attention``, which appends a decode token to a slot
+    without restoring it: the fused arm reads the sealed blocks and the tail directly,
+    and the bridge arm restores them itself (experiments/nb06/source/loop_kv_nb06_attention.py:13-31
+    defers the restoration the same way; skipped_k / skipped_v count the restorations
+    saved, as there)."""
     parent = make_packed_cache(base)
 
     class ConnectionCache(parent):
@@ -74,17 +82,16 @@ def make_cache(base=ListCacheBase):
             # "step": fused calls OR their device status into one word that post_decode reads
             self.checks = checks
             self.status = None
-            self._defer = False
-            self.connections = Counter()
-            self.skipped_k = Counter()
+            self.connections = Counter()  # attention calls per slot
+            self.skipped_k = Counter()    # restorations saved per slot
             self.skipped_v = Counter()
-            self.capture = None
+            self.capture = None           # optional callable(slot, data, out) after each decode call
 
-        def materialize(self, slot, kv):
-            if self._defer:
-                (self.skipped_k if kv == "K" else self.skipped_v)[slot] += 1
-                return None
-            return super().materialize(slot, kv)
+        def append_for_attention(self, key, value, slot, kwargs):
+            w.require(self.restore_observer is None, "Recursive/decorated restore")
+            if self._append(key, value, slot, kwargs) is None:
+                self.skipped_k[slot] += 1
+                self.skipped_v[slot] += 1
 
         def post_decode(self):
             if self.checks == "step" and self.status is not None:
@@ -93,14 +100,6 @@ def make_cache(base=ListCacheBase):
                     self.status.zero_()
                     K._raise_status(st)
             super().post_decode()
-
-        def append_for_attention(self, key, value, slot, kwargs):
-            w.require(not self._defer and self.restore_observer is None, "Recursive/decorated restore")
-            self._defer = True
-            try:
-                super().update(key, value, slot, kwargs)
-            finally:
-                self._defer = False
 
     return ConnectionCache
 

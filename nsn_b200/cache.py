@@ -62,8 +62,9 @@ class Int3AsymNsepPchanCache:
         rows = math.prod(prefix) if prefix else 1
         dev = self.packed_d.device
         out = torch.empty(tuple(prefix) + (T, D), dtype=torch.float16, device=dev)
-        L.check(L.load().nsnkv_int3asym_decode(L.ptr(self.packed_d.contiguous()), L.ptr(self.norm.contiguous()),
-                                               L.ptr(self.d_min.contiguous()), L.ptr(self.d_step.contiguous()), rows,
+        # contiguous copies stay referenced until the launch is enqueued
+        packed, norm, d_min, d_step = (t.contiguous() for t in (self.packed_d, self.norm, self.d_min, self.d_step))
+        L.check(L.load().nsnkv_int3asym_decode(L.ptr(packed), L.ptr(norm), L.ptr(d_min), L.ptr(d_step), rows,
                                                T, D, L.ptr(out), L.stream_handle(dev)),
                 "nsnkv_int3asym_decode")
         return out

@@ -36,9 +36,31 @@ def group_layout(group, h, dev):
         specs.append((group["headers"], (1, h, n, 12), torch.uint8))
     specs.extend(zip(group["metas"], [(1, h, n, 64, 1), (1, h, n, 1, 128), (1, h, n, 1, 128)], [torch.float16] * 3))
     for x, shape, dtype in specs:
-        w.require(tuple(x.shape) == shape and x.dtype == dtype and x.is_contiguous() and x.device == dev,
-                  "Packed tensor layout/device")
+        w.require(tuple(x.shape) == shape and x.dtype == dtype and x.device == dev, "Packed tensor layout/device")
+    head_stride_blocks(group)
     return n * 64, bits
+
+
+def head_stride_blocks(group) -> int:
+    """Blocks between one head's first block and the next head's in every tensor of a group.
+
+    A group from encode_group is contiguous (n); PackedCache serves views of arrays with
+    spare capacity (the capacity).  Each block must be dense and the blocks of a head
+    consecutive, with the same head stride in every tensor of the group.
+    """
+    tensors = [group["codes"], *group["metas"]] + ([group["headers"]] if group.get("headers") is not None else [])
+    strides = set()
+    for x in tensors:
+        per = 1
+        for d in x.shape[3:]:
+            per *= d
+        inner = x[0, 0, 0] if x.shape[2] else None
+        dense_block = inner is None or inner.is_contiguous()
+        w.require(dense_block and (x.shape[2] <= 1 or x.stride(2) == per) and x.stride(1) % per == 0
+                  and x.stride(1) // per >= x.shape[2], "Packed tensor layout/device")
+        strides.add(x.stride(1) // per if x.shape[1] > 1 else x.shape[2])
+    w.require(len(strides) == 1, "Packed tensor layout/device")
+    return strides.pop()
 
 
 def structural(g, kt, q, vg, vt):

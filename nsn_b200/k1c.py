@@ -29,11 +29,10 @@ def triton_decode_scores(q, tstore, n_q, n_kv, head_dim):
     st = tstore.get("step")
     en = tstore.get("eff_norm")
     out = torch.empty((B, n_q, T), dtype=torch.float32, device=q.device)
-    L.check(L.load().nsnkv_k1c_scores(recipe, B, n_q, n_kv, T, head_dim, L.ptr(q.contiguous()), L.ptr(code),
-                                      L.ptr(None if mn is None else mn.contiguous()),
-                                      L.ptr(None if st is None else st.contiguous()),
-                                      L.ptr(None if en is None else en.contiguous()), L.ptr(out),
-                                      L.stream_handle(q.device)),
+    # contiguous copies stay referenced until the launch is enqueued
+    qc, mn, st, en = (None if t is None else t.contiguous() for t in (q, mn, st, en))
+    L.check(L.load().nsnkv_k1c_scores(recipe, B, n_q, n_kv, T, head_dim, L.ptr(qc), L.ptr(code), L.ptr(mn),
+                                      L.ptr(st), L.ptr(en), L.ptr(out), L.stream_handle(q.device)),
             "nsnkv_k1c_scores")
     return out
 

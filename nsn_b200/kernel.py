@@ -115,7 +115,7 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
 
 
 def group_pool(g, h):
-    """Pool view of a reference-layout group [1, h, n, ...] (block index h*n + i)."""
+    """Pool view of a reference-layout group [1, h, n, ...] (block (j, i) at j * head stride + i)."""
     return dict(codes=g["codes"], norm=g["metas"][0], min=g["metas"][1], scale=g["metas"][2])
 
 
@@ -157,12 +157,19 @@ def launch(g, kt, q, vg, vt, trace=False, check=True, status=None):
     t = kt.shape[2]
     bits = 3 if g is None else g["codes"].shape[-1] * 8 // (w.BLOCK * w.DIM)
     ctx = torch.empty((1, hq, 1, 128), dtype=torch.float32, device=q.device)
+    stride = n
+    if g is not None:  # groups may be views with spare capacity between heads (PackedCache)
+        stride = checks.head_stride_blocks(g)
+        if checks.head_stride_blocks(vg) != stride:
+            g, vg = ({"codes": x["codes"].contiguous(), "metas": tuple(m.contiguous() for m in x["metas"])}
+                     for x in (g, vg))
+            stride = n
     out, status = decode_attention(
         q.reshape(1, hq, 128), group_pool(g, h) if g is not None else None,
-        group_pool(vg, h) if vg is not None else None, h=h, bits=bits, blk_stride_head=n, blk_stride_page=1,
+        group_pool(vg, h) if vg is not None else None, h=h, bits=bits, blk_stride_head=stride, blk_stride_page=1,
         n_blocks=n, max_blocks=n, k_tail=kt if t else None, v_tail=vt if t else None,
         tail_stride_seq=h * t, tail_stride_head=t, tail_len=t, max_tail=t, out_f32=ctx.reshape(1, hq, 128),
-        status=status)
+        status=status, blk_bytes=0)
     if check:
         _raise_status(int(status.item()))
     out = out.reshape(1, 1, hq, 128)

@@ -103,7 +103,8 @@ def unpack_codes(payload, count: int, bits: int):
             "packed payload shape")
     L.require_cuda()
     out = torch.empty(count, dtype=torch.uint8, device=payload.device)
-    L.check(L.load().nsnkv_unpack(L.ptr(payload.contiguous()), count, bits, L.ptr(out),
+    payload = payload.contiguous()  # referenced until the launch is enqueued
+    L.check(L.load().nsnkv_unpack(L.ptr(payload), count, bits, L.ptr(out),
                                   L.stream_handle(payload.device)), "unpack_codes")
     return out.cpu().numpy() if as_np else out
 
@@ -297,9 +298,11 @@ def restore_blocks(codes, metas, dtype, *, bits=3, unpacked=False, tail=None, ch
     status = L.status_tensor(dev)
     if tail is not None:
         require(tail.dtype == dtype and tail.is_contiguous(), "tail dtype/layout")
+    # contiguous copies of strided inputs stay referenced until the launch is enqueued (a
+    # temporary freed earlier could be handed to the next copy before the kernel reads it)
+    codes, n, m, s = (None if x is None else x.contiguous() for x in (codes, n, m, s))
     L.check(L.load().nsnkv_restore(
-        L.ptr(codes.contiguous() if codes is not None else None), int(unpacked), L.ptr(n.contiguous()),
-        L.ptr(m.contiguous()), L.ptr(s.contiguous()), rows, bpr, bits, L.ptr(tail), t, L.DTYPE_CODE[dtype],
+        L.ptr(codes), int(unpacked), L.ptr(n), L.ptr(m), L.ptr(s), rows, bpr, bits, L.ptr(tail), t, L.DTYPE_CODE[dtype],
         L.ptr(out), L.ptr(status), L.stream_handle(dev)), "nsnkv_restore")
     if check:
         _status_to_error(int(status.item()), "Nonfinite NSN reconstruction", meta=False)
