@@ -341,10 +341,15 @@ def run_cfg1(args, rank, world, local, dist):
     print(json.dumps(line), flush=True)
 
 
-def run_cfg4(args, rank, world, local, dist):
-    """One 131072-token INT5 sequence (2047 blocks + 64 tail, GQA 64:8) split across ranks."""
-    from nsn_b200 import codec, workloads
+def cfg4_measure(args, rank, world, local, dist, with_encode=True, steps=None, warmup=None):
+    """cfg4 on `world` ranks: one 131072-token INT5 sequence (2047 blocks + 64 tail, GQA
+    64:8), split by block ranges; optionally the timed full-context encode of each rank's
+    blocks.  Every rank returns the same dict (times are maxima over ranks)."""
+    from nsn_b200 import workloads
     from nsn_b200.splitkv import ShardedSequence, shard_range
+    from nsn_b200 import primitives as P
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     device = torch.device("cuda", local)
     c = workloads.CONFIGS[4]
     nb_total, h, hq, bits = c["blocks"], c["h"], c["hq"], c["bits"]
@@ -372,9 +377,7 @@ def run_cfg4(args, rank, world, local, dist):
     vt = vall[None, :, n * 64:].contiguous() if last else None
     del kall, vall
     stream = torch.cuda.current_stream(device)
-    # full-context encode (prefill quantisation of this rank's K and V blocks), timed
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    from nsn_b200 import primitives as P
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
 
     def encode_kv():
         # the public encoder with its status check deferred, so no host sync splits K from V
@@ -382,19 +385,23 @@ def run_cfg4(args, rank, world, local, dist):
         rv = P.encode_blocks(v, bits, packed=True, headers_start=s * 64, check=False)
         return rk, rv
 
-    for _ in range(3):
-        encode_kv()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    flush.zero_()
-    torch.cuda.synchronize(device)
-    if dist:
-        dist.barrier()
-        torch.cuda.synchronize(device)  # the barrier's own device work stays outside the events
-    e0.record(stream)
-    rk, rv = encode_kv()
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    enc_ms = e0.elapsed_time(e1)
+    enc_ms = 0.0
+    if with_encode:
+        for _ in range(3):
+            encode_kv()
+        flush.zero_()
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+            torch.cuda.synchronize(device)  # the barrier's own device work stays outside the events
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        rk, rv = encode_kv()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        enc_ms = e0.elapsed_time(e1)
+    else:
+        rk, rv = encode_kv()
     for r_ in (rk, rv):
         P._status_to_error(int(r_["status"].item()), "Nonfinite input to NSN")
     g = dict(codes=rk["codes"], metas=tuple(rk["metas"]), headers=rk["headers"])
@@ -402,12 +409,12 @@ def run_cfg4(args, rank, world, local, dist):
     del k, v
     sh = ShardedSequence(g, vg, kt, vt, h, hq, bits)
     gen = torch.Generator(device=device).manual_seed(4 * 7919)
-    qs = (torch.randn((args.warmup + args.steps, 1, hq, 1, 128), generator=gen, device=device) / math.sqrt(128)).half()
+    qs = (torch.randn((warmup + steps, 1, hq, 1, 128), generator=gen, device=device) / math.sqrt(128)).half()
     # one decode step (local attention, one all-gather of the (o, lse) records, merge) is
     # captured once as a CUDA graph and replayed, so the step carries no host launch gaps
     static_q = qs[0].clone()
     static_out = torch.empty((hq, 128), dtype=torch.float16, device=device)
-    for i in range(args.warmup):
+    for i in range(warmup):
         static_q.copy_(qs[i])
         sh.decode(static_q, out=static_out)
     torch.cuda.synchronize(device)
@@ -415,52 +422,73 @@ def run_cfg4(args, rank, world, local, dist):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         sh.decode(static_q, out=static_out)
+    local_graph = torch.cuda.CUDAGraph()  # the same step's local attention alone
+    with torch.cuda.graph(local_graph):
+        sh.local(static_q)
     torch.cuda.synchronize(device)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if dist:
-        dist.barrier()
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
+
+    def timed(gr, n_steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_steps)]
+        for i in range(n_steps):
             flush.zero_()
-            static_q.copy_(qs[args.warmup + i])
+            static_q.copy_(qs[warmup + i])
             if dist:
                 dist.barrier()
                 torch.cuda.synchronize(device)
             ev[i][0].record(stream)
-            graph.replay()
+            gr.replay()
             ev[i][1].record(stream)
         torch.cuda.synchronize(device)
+        return sum(a.elapsed_time(b) for a, b in ev) / n_steps
+
+    if dist:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        step_ms = timed(graph, steps)
+        local_ms = timed(local_graph, steps)
     sh.check()
-    del graph  # a graph holding NCCL work is released before the process group
+    del graph, local_graph  # graphs holding NCCL work are released before the process group
     torch.cuda.synchronize(device)
-    step_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
-    t = torch.tensor([step_ms, enc_ms], dtype=torch.float64, device=device)
+    t = torch.tensor([step_ms, enc_ms, local_ms], dtype=torch.float64, device=device)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, enc_ms_max = t.tolist()
+    step_ms, enc_ms_max, local_ms = t.tolist()
     total_bytes = 2 * 8 * (nb_total * 5760 + 64 * 256) + 2 * hq * 256
     total_enc_bytes = 2 * (nb_total * 8 * 64 * 128 * 2 + nb_total * 8 * 5760)
     hbm, peak_kind = peaks()
+    return {"n_gpus": world, "step_ms": step_ms, "tokens_per_s": 1000.0 / step_ms,
+            "local_attention_ms": local_ms, "gather_merge_ms": max(step_ms - local_ms, 0.0),
+            "decode_gbs_whole_job": total_bytes / (step_ms / 1000.0) / 1e9,
+            "frac_per_gpu": total_bytes / (step_ms / 1000.0) / 1e9 / world / hbm, "peak": hbm, "peak_kind": peak_kind,
+            "bytes_per_step": total_bytes, "blocks_per_rank": n,
+            "encode_ms": enc_ms_max if with_encode else None, "encode_bytes": total_enc_bytes,
+            "clocks": clk.summary()}
+
+
+def run_cfg4(args, rank, world, local, dist):
+    """One 131072-token INT5 sequence (2047 blocks + 64 tail, GQA 64:8) split across ranks."""
+    r = cfg4_measure(args, rank, world, local, dist, with_encode=True)
     if rank == 0:
-        line = {"metric": "decode tokens/s (split-KV long-context decode, cfg4)", "value": 1000.0 / step_ms,
+        hbm = r["peak"]
+        line = {"metric": "decode tokens/s (split-KV long-context decode, cfg4)", "value": r["tokens_per_s"],
                 "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "ms_per_step": r["step_ms"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "fp16", "data": "synthetic",
                 "config": {"workload": "cfg4-long-131k-int5: 2047 INT5 blocks + 64 tail, GQA 64:8, split-KV "
                                        "(local fused attention + one NCCL all-gather of the (o, lse) records + "
                                        "merge kernel, replayed as a CUDA graph)",
                            "global_batch": 1, "context": 131072, "parallelism": f"seq-split{world}",
                            "l2": "flushed before every timed step"},
-                "decode_gbs_whole_job": total_bytes / (step_ms / 1000.0) / 1e9,
-                "encode": {"ms_max_over_ranks": enc_ms_max, "bytes_total": total_enc_bytes,
-                           "gbs_whole_job": total_enc_bytes / (enc_ms_max / 1000.0) / 1e9,
-                           "what": "nsnkv_encode_blocks of the 131008 sealed tokens (2047 blocks) x 8 kv heads, K and V (read fp16, "
-                                   "write INT5 codes + fp16 metadata + headers), L2 flushed before"},
-                "roofline": {"bound": "hbm", "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
-                             "achieved": total_bytes / (step_ms / 1000.0) / 1e9 / world,
-                             "frac": total_bytes / (step_ms / 1000.0) / 1e9 / world / hbm,
+                "decode_gbs_whole_job": r["decode_gbs_whole_job"],
+                "local_attention_ms": r["local_attention_ms"], "gather_merge_ms": r["gather_merge_ms"],
+                "encode": {"ms_max_over_ranks": r["encode_ms"], "bytes_total": r["encode_bytes"],
+                           "gbs_whole_job": r["encode_bytes"] / (r["encode_ms"] / 1000.0) / 1e9,
+                           "what": "nsnkv_encode_blocks of the 131008 sealed tokens (2047 blocks) x 8 kv heads, K "
+                                   "and V (read fp16, write INT5 codes + fp16 metadata + headers), L2 flushed before"},
+                "roofline": {"bound": "hbm", "peak": hbm, "peak_kind": r["peak_kind"], "unit": "GB/s",
+                             "achieved": r["decode_gbs_whole_job"] / world, "frac": r["frac_per_gpu"],
                              "note": "per GPU: whole-job packed bytes / step time / GPUs"},
-                "clocks": clk.summary()}
+                "clocks": r["clocks"]}
         print(json.dumps(line), flush=True)
 
 
@@ -545,6 +573,7 @@ def main():
     ap.add_argument("--impl", default="nsn", choices=["nsn", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the cfg4 split-KV sub-record of the cfg2 line")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="2: batched decode (the default bench line); 3: looped model; 4: split-KV long context + encode")
     ap.add_argument("--cfg3-steps", type=int, default=256, help="teacher-forced decode steps per sequence (cfg3)")
@@ -727,6 +756,17 @@ def main():
     hbm, peak_kind = peaks()
     achieved = bytes_attn / (mean_attn / 1000.0) / 1e9  # this rank
     clocks = clk.summary()
+
+    # ---- cfg4 split-KV on the same ranks (every rank takes part in its all-gathers)
+    cfg4 = None
+    if not args.no_cfg4:
+        del cache, q, kn, vn
+        torch.cuda.empty_cache()
+        cfg4 = cfg4_measure(args, rank, world, local, dist, with_encode=False, steps=min(args.steps, 20), warmup=3)
+        cfg4["what"] = ("cfg4 split-KV decode step: one 131072-token INT5 sequence (2047 blocks + 64 tail, GQA "
+                        "64:8) split by block ranges over the ranks; local fused attention + one NCCL all-gather "
+                        "of the (o, lse) records + merge kernel, replayed as a CUDA graph, L2 flushed; "
+                        "gather_merge_ms = step - local attention alone (max over ranks)")
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:
@@ -771,6 +811,7 @@ def main():
             "gpu_launches": 4 * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "cfg4_splitkv": cfg4,
         }
         print(json.dumps(line), flush=True)
     if dist:
