@@ -182,6 +182,9 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
  *                      k_scale = k_codes + CB + 256, k_alpha = k_codes + CB + 512,
  *                      v_codes = k_codes + CB + 768, the same offsets from v_codes, and
  *                      blk_bytes = 2 * (CB + 768)), a block moves in one copy.
+ *   blocks_total       sum of n_blocks[b] over the batch when the caller knows it (0: not
+ *                      known), with n_blocks given; it only sizes the tensor-core kernels'
+ *                      chunks (a wrong value costs speed, never correctness).
  *   flags              NSNKV_ATTN_RECORD_ORDER: K and V codes in the records' orders (K
  *                      paired halves, V paired rows); only the tensor-core kernels read
  *                      them (NSNKV_ERR_UNSUPPORTED otherwise).
@@ -206,6 +209,7 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             int64_t blk_stride_head, int64_t blk_stride_page,
                             const int32_t *block_table, int64_t table_stride,
                             const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                            int64_t blocks_total,
                             void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
                             const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail,
                             const void *k_new, const void *v_new,

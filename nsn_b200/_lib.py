@@ -58,7 +58,7 @@ SIGNATURES = [
     ("nsnkv_decode_attn_alpha", c_int, [c_int64, c_int, c_int, c_int, c_int, P,
                                         P, P, P, P, P, P, P, P, P, P, c_int64, c_int,
                                         c_int64, c_int64, P, c_int64,
-                                        P, c_int32, c_int32,
+                                        P, c_int32, c_int32, c_int64,
                                         P, P, c_int64, c_int64,
                                         P, c_int32, c_int32,
                                         P, P, P, P, P, P, c_int64, P, P]),

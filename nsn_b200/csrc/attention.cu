@@ -636,7 +636,11 @@ __global__ void __launch_bounds__(kThreads, 4) attn_native_rows_kernel(const Att
   pdl_wait();
 }
 
-// Combine the chunk partials of one (sequence, query head).
+// Combine the chunk partials of one (sequence, query head): the log-sum-exp merge of the
+// reference (experiments/ac08/source/loop_kv_af01_kernel.py:70-84), as one online pass.
+// Thread c owns output channel c and walks the chunks once, rescaling its running sum
+// whenever a chunk raises the running maximum; the loads of different chunks do not
+// depend on each other, so they overlap instead of forming one dependent round per pass.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G, T *out, float *out_f32,
                                                           float *lse) {
@@ -651,41 +655,23 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G
   const int raw_per_chunk = a.chunk_blocks * kBlock;
   const int n_chunks = (nb + a.chunk_blocks - 1) / a.chunk_blocks + (tail_total + raw_per_chunk - 1) / raw_per_chunk;
   const int64_t row0 = (b * a.hq + hqi) * a.max_chunks;
+  const float *ml = a.part_ml + row0 * 2;
+  const float *po = a.part_o + row0 * kDim + c;
   constexpr float kLog2e = 1.4426950408889634f;
-  // The chunks' (m, l) are read once by the CTA (thread i takes chunk i, i + 128, ...)
-  // and their weights kept in shared memory; each thread then sums its channel over the
-  // chunks with independent loads.  Long single sequences have ~100 chunks per head.
-  constexpr int kMaxW = 512;
-  __shared__ float wgt[kMaxW];
-  __shared__ float red[2][4];
-  float M = -INFINITY;
-  for (int i = c; i < n_chunks; i += kDim) M = fmaxf(M, a.part_ml[(row0 + i) * 2]);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if ((c & 31) == 0) red[0][c >> 5] = M;
-  __syncthreads();
-  M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
-  float L = 0.f;
-  for (int i = c; i < n_chunks; i += kDim) {
-    const float m = a.part_ml[(row0 + i) * 2];
-    const float w = m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e);
-    L += w * a.part_ml[(row0 + i) * 2 + 1];
-    if (i < kMaxW) wgt[i] = w;
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  if ((c & 31) == 0) red[1][c >> 5] = L;
-  __syncthreads();
-  L = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
-  float o = 0.f;
-  if (n_chunks <= kMaxW) {
-#pragma unroll 8
-    for (int i = 0; i < n_chunks; ++i) o += wgt[i] * a.part_o[(row0 + i) * kDim + c];
-  } else {
-    for (int i = 0; i < n_chunks; ++i) {
-      const float m = a.part_ml[(row0 + i) * 2];
-      o += (m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e)) * a.part_o[(row0 + i) * kDim + c];
+  float M = -INFINITY, L = 0.f, o = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < n_chunks; ++i) {
+    const float m = ml[2 * i], l = ml[2 * i + 1], x = po[static_cast<int64_t>(i) * kDim];
+    if (m == -INFINITY) continue;  // a chunk without a finite score contributes nothing
+    if (m > M) {
+      const float r = M == -INFINITY ? 0.f : exp2f((M - m) * kLog2e);
+      L *= r;
+      o *= r;
+      M = m;
     }
+    const float wgt = exp2f((m - M) * kLog2e);
+    L = fmaf(wgt, l, L);
+    o = fmaf(wgt, x, o);
   }
   const float y = __fdiv_rn(o, L);
   const T yt = Elem<T>::from_f(y);
@@ -1677,18 +1663,23 @@ static int chunk_blocks_for(int64_t batch, int h, int32_t max_blocks, int32_t ma
   return static_cast<int>(ch);
 }
 
-// The sealed INT3 kernels' chunks: about one CTA per resident slot (148 SMs x per_sm), in
-// multiples of 4 blocks (one round of its four warps), up to 32 blocks.
-static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail, int per_sm) {
+// The sealed INT3 kernels' chunks: about one CTA per resident slot (148 SMs x per_sm) for
+// the average sequence, in multiples of 4 blocks (one round of its four warps), up to 32
+// blocks and never below the restore kernel's chunks (the workspace is sized for those).
+// blocks_total, the sum of n_blocks when the caller knows it, gives the average; without
+// it the bound max_blocks stands in, which undersizes the grid when lengths differ.
+static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max_tail, int per_sm,
+                           int64_t blocks_total) {
   const int64_t units = batch * h;
   const int64_t target = 148 * per_sm;
-  const int64_t work = max_blocks + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
+  const int64_t avg = blocks_total > 0 ? (blocks_total + batch - 1) / batch : max_blocks;
+  const int64_t work = avg + (static_cast<int64_t>(max_tail) + 1 + kBlock - 1) / kBlock;
   const int64_t per_unit = (target + units - 1) / units;
   int64_t ch = (work + per_unit - 1) / per_unit;
   ch = (ch + 3) / 4 * 4;
   if (ch < 4) ch = 4;
   if (ch > 32) ch = 32;
-  return static_cast<int>(ch);
+  return static_cast<int>(std::max<int64_t>(ch, chunk_blocks_for(batch, h, max_blocks, max_tail)));
 }
 
 static int max_chunks_for(int32_t max_blocks, int32_t max_tail, int32_t ch) {
@@ -1740,7 +1731,8 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint16_t *v_scale, const float *k_alpha, const float *v_alpha, int64_t blk_bytes,
                             int flags, int64_t blk_stride_head, int64_t blk_stride_page, const int32_t *block_table,
                             int64_t table_stride, const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
-                            void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,
+                            int64_t blocks_total, void *k_tail, void *v_tail, int64_t tail_stride_seq,
+                            int64_t tail_stride_head,
                             const int32_t *tail_len, int32_t tail_len_const, int32_t max_tail, const void *k_new,
                             const void *v_new, void *out, float *out_f32, float *lse, void *workspace,
                             int64_t workspace_bytes, int32_t *status, void *stream) {
@@ -1841,7 +1833,7 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
       return NSNKV_ERR_CUDA;
     // whole chunks of up to 32 blocks (8 per warp) amortise the per-CTA set-up; fewer chunks
     // than nsnkv_decode_attn_workspace_bytes() sized for, so the same workspace holds them
-    a.chunk_blocks = s3_chunk_blocks(batch, h, max_blocks, max_tail, per_sm);
+    a.chunk_blocks = s3_chunk_blocks(batch, h, max_blocks, max_tail, per_sm, n_blocks ? blocks_total : 0);
     a.max_chunks = max_chunks_for(max_blocks, max_tail, a.chunk_blocks);
     a.part_ml = a.part_o + batch * hq * static_cast<int64_t>(a.max_chunks) * kDim;
     // sealed chunks here, native-row chunks on attn_partial_kernel, then the merge kernel
@@ -1916,7 +1908,7 @@ int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const v
                       void *stream) {
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
                           v_scale, nullptr, nullptr, 0, 0, blk_stride_head, blk_stride_page, block_table, table_stride,
-                          n_blocks, n_blocks_const, max_blocks, k_tail, v_tail, tail_stride_seq, tail_stride_head,
+                          n_blocks, n_blocks_const, max_blocks, 0, k_tail, v_tail, tail_stride_seq, tail_stride_head,
                           tail_len, tail_len_const, max_tail, k_new, v_new, out, out_f32, lse, workspace,
                           workspace_bytes, status, stream);
 }
@@ -1927,17 +1919,17 @@ int nsnkv_decode_attn_alpha(int64_t batch, int hq, int h, int bits, int dtype, c
                             const uint16_t *v_min, const uint16_t *v_scale, const float *k_alpha,
                             const float *v_alpha, int64_t blk_bytes, int flags, int64_t blk_stride_head,
                             int64_t blk_stride_page, const int32_t *block_table, int64_t table_stride,
-                            const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks, void *k_tail,
-                            void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head, const int32_t *tail_len,
-                            int32_t tail_len_const, int32_t max_tail, const void *k_new, const void *v_new,
-                            void *out, float *out_f32, float *lse, void *workspace, int64_t workspace_bytes,
-                            int32_t *status, void *stream) {
-  if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;
+                            const int32_t *n_blocks, int32_t n_blocks_const, int32_t max_blocks,
+                            int64_t blocks_total, void *k_tail, void *v_tail, int64_t tail_stride_seq,
+                            int64_t tail_stride_head, const int32_t *tail_len, int32_t tail_len_const,
+                            int32_t max_tail, const void *k_new, const void *v_new, void *out, float *out_f32,
+                            float *lse, void *workspace, int64_t workspace_bytes, int32_t *status, void *stream) {
+  if ((k_alpha == nullptr) != (v_alpha == nullptr) || blocks_total < 0) return NSNKV_ERR_ARG;
   return decode_attn_impl(batch, hq, h, bits, dtype, q, k_codes, k_norm, k_min, k_scale, v_codes, v_norm, v_min,
                           v_scale, k_alpha, v_alpha, blk_bytes, flags, blk_stride_head, blk_stride_page,
-                          block_table, table_stride, n_blocks, n_blocks_const, max_blocks, k_tail, v_tail,
-                          tail_stride_seq, tail_stride_head, tail_len, tail_len_const, max_tail, k_new, v_new, out,
-                          out_f32, lse, workspace, workspace_bytes, status, stream);
+                          block_table, table_stride, n_blocks, n_blocks_const, max_blocks, blocks_total, k_tail,
+                          v_tail, tail_stride_seq, tail_stride_head, tail_len, tail_len_const, max_tail, k_new, v_new,
+                          out, out_f32, lse, workspace, workspace_bytes, status, stream);
 }
 
 static int merge_shards_launch(int n_shards, int64_t rows, const float *o, int64_t o_stride, const float *lse,

@@ -54,7 +54,7 @@ def workspace(nbytes: int, device) -> torch.Tensor:
 def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_page, n_blocks, max_blocks,
                      k_tail=None, v_tail=None, tail_stride_seq=0, tail_stride_head=0, tail_len=0, max_tail=0,
                      block_table=None, k_new=None, v_new=None, out=None, out_f32=None, lse=None, status=None,
-                     ws=None, blk_bytes=None, exact=False):
+                     ws=None, blk_bytes=None, exact=False, blocks_total=0):
     """Direct binding of nsnkv_decode_attn (nsnkv_decode_attn_alpha when both pools carry
     "alpha" or their arrays are fields of block records).
 
@@ -64,7 +64,8 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
     sequence) or int32 CUDA tensors [B].  blk_bytes: the block stride of the
     codes / min / scale / alpha arrays (None: read from the tensors' strides, 0: dense).
     With renorm factors, K rows are rounded to the cache dtype as the reference bridge
-    rounds them unless ``exact`` (then K and V are both the exact fp32 restore).
+    rounds them unless ``exact`` (then K and V are both the exact fp32 restore);
+    ``blocks_total`` (the sum of n_blocks, when known) sizes their kernel's chunks.
     Returns (out, status).
     """
     L.require_cuda()
@@ -102,11 +103,13 @@ def decode_attention(q, k_pool, v_pool, *, h, bits, blk_stride_head, blk_stride_
         blocks = blocks + alphas + (int(blk_bytes), flags)
     else:
         entry, name = lib.nsnkv_decode_attn, "nsnkv_decode_attn"
+    counts = (L.ptr(nb_t), 0 if nb_t is not None else int(n_blocks), int(max_blocks))
+    if name == "nsnkv_decode_attn_alpha":
+        counts = counts + (int(blocks_total),)
     rc = entry(
         B, hq, h, bits, L.DTYPE_CODE[q.dtype], L.ptr(q), *blocks,
         blk_stride_head, blk_stride_page, L.ptr(block_table), block_table.shape[-1] if block_table is not None else 0,
-        L.ptr(nb_t), 0 if nb_t is not None else int(n_blocks), int(max_blocks),
-        L.ptr(k_tail), L.ptr(v_tail), tail_stride_seq, tail_stride_head,
+        *counts, L.ptr(k_tail), L.ptr(v_tail), tail_stride_seq, tail_stride_head,
         L.ptr(tl_t), 0 if tl_t is not None else int(tail_len), int(max_tail),
         L.ptr(k_new), L.ptr(v_new), L.ptr(out), L.ptr(out_f32), L.ptr(lse),
         L.ptr(ws), ws.numel(), L.ptr(status), L.stream_handle(dev))

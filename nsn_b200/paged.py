@@ -33,6 +33,7 @@ from __future__ import annotations
 
 import struct
 
+import numpy as np
 import torch
 
 from . import _lib as L
@@ -198,6 +199,11 @@ class PagedKVCache:
         self.block_table = torch.arange(self.pages, dtype=torch.int32, device=dev).reshape(batch, max_blocks)
         self.n_blocks = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.tail_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        # host copies of n_blocks / tail_len, kept without reading the device: every change
+        # to the counters comes from this object's prefill, import and seal (seal-at-64 is
+        # deterministic); they size the attention kernels' work (never their correctness)
+        self.host_blocks = np.zeros(batch, np.int64)
+        self.host_tail = np.zeros(batch, np.int64)
         self.k_tail = torch.zeros((batch, h, w.BLOCK, w.DIM), dtype=dtype, device=dev)
         self.v_tail = torch.zeros_like(self.k_tail)
         self.status = L.status_tensor(dev)
@@ -223,6 +229,7 @@ class PagedKVCache:
                 tail[b, :, :t].copy_(src[:, nb * w.BLOCK:])
         self.n_blocks[b] = nb
         self.tail_len[b] = t
+        self.host_blocks[b], self.host_tail[b] = nb, t
 
     # ------------------------------------------------------------ exchange with the reference layout
     def export_groups(self, b: int):
@@ -287,6 +294,7 @@ class PagedKVCache:
             tail[b, :, :rest].copy_(src[:, extra * w.BLOCK:])
         self.n_blocks[b] = n + extra
         self.tail_len[b] = rest
+        self.host_blocks[b], self.host_tail[b] = n + extra, rest
 
     def to_bytes(self, b: int) -> bytes:
         """Sequence b in the sequence container format (see sequence_to_bytes)."""
@@ -309,9 +317,14 @@ class PagedKVCache:
             tail_stride_seq=self.h * w.BLOCK, tail_stride_head=w.BLOCK, tail_len=self.tail_len,
             max_tail=w.BLOCK - 1, block_table=self.block_table, k_new=k_new, v_new=v_new,
             out=self.out if out is None else out, out_f32=out_f32, lse=lse, status=self.status, ws=self.ws,
-            blk_bytes=self.blk_bytes, exact=self.restore_rounding == "exact")[0]
+            blk_bytes=self.blk_bytes, exact=self.restore_rounding == "exact",
+            blocks_total=int(self.host_blocks.sum()))[0]
 
     def seal(self, pending_append: int = 1):
+        t = self.host_tail + pending_append
+        full = t >= w.BLOCK
+        self.host_blocks += full
+        self.host_tail = t - w.BLOCK * full
         lib = L.load()
         if self.records is None:
             rc = lib.nsnkv_seal_full_tails(
