@@ -856,6 +856,346 @@ __device__ __forceinline__ uint32_t split_hilo(float w) {
 
 }  // namespace s3
 
+// ----------------------------------------------------------------- the exact kernel's shared pieces
+// The per-block arithmetic, the per-lane q records and the chunk combine of the exact
+// sealed INT3 kernel (one CTA per chunk).  REC: the codes are in the paged cache's
+// block-record orders (K paired halves, V paired rows); otherwise the reference's packed
+// rows.
+namespace s3 {
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }  // 2^e, -126 <= e <= 127
+
+// Per-lane constant records for the query rows qs (G <= 4 heads), the same in every warp:
+// each of the four warps writes a quarter, so the caller synchronises the warps before any
+// of them reads recs.  Returns kq of head tig (the exponent shift of its q columns).
+template <bool REC>
+__device__ __forceinline__ int build_records(const __half (*qs)[kDim], int G, uint32_t (*recs)[kRec], int lane,
+                                             int warp) {
+  const int g = lane >> 2, tig = lane & 3;
+  auto pow2 = [](int e) { return pow2f(e); };
+  // ---- per-head q exponent kq_h: |q_h| < 2^(8 + kq_h), so q * 2^(7 - pos - kq_h) is a finite fp16
+  // (each MMA column is one head, so the shift may differ per head); every warp computes all four
+  int kqh[4];
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) {
+    float mx = 0.f;
+    if (hh < G) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(&qs[hh][4 * lane]);
+      const float2 x0 = Elem<__half>::to_f2(u.x), x1 = Elem<__half>::to_f2(u.y);
+      mx = fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x1.x), fabsf(x1.y)));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int e = ((__float_as_int(mx) >> 23) & 0xff) - 126;  // mx < 2^e (frexp exponent)
+    kqh[hh] = e > 8 ? e - 8 : 0;
+  }
+  auto pick = [&](int hh) { return hh == 0 ? kqh[0] : hh == 1 ? kqh[1] : hh == 2 ? kqh[2] : kqh[3]; };
+
+  // ---- per-lane constant records (the same in every warp), each warp writing a quarter
+  {
+    uint32_t *rec = recs[lane];
+    const int hb = g >> 1, pb = g & 1;
+    const int kb = pick(hb);
+#pragma unroll
+    for (int r = 0; r < 18; ++r) {
+      if ((r & 3) != warp) continue;
+      float lo = 0.f, hi = 0.f;
+      if (REC) {  // register r: channels 32 tig + r and 32 tig + 16 + r, both at window position vpos(r)
+        if (r < 16 && hb < G) {
+          lo = __half2float(qs[hb][32 * tig + r]) * pow2(7 - vpos(r) - kb);
+          hi = __half2float(qs[hb][32 * tig + 16 + r]) * pow2(7 - vpos(r) - kb);
+        }
+      } else if (hb < G) {
+        if (ktab(r, 1) >= 0) lo = __half2float(qs[hb][32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
+        if (ktab(r, 3) >= 0) hi = __half2float(qs[hb][32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
+      }
+      __half2 s2 = __floats2half2_rn(lo, hi);
+      const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
+      rec[r] = pb ? su ^ 0x80008000u : su;  // hi lanes: q; lo lanes: -q
+      rec[20 + r] = pb ? su : 0u;           // lo lanes: q; hi lanes: 0
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      if (((ks + 2) & 3) != warp) continue;
+      uint32_t a0 = 0u, a2 = 0u;
+      if (g < G) {
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(&qs[g][32 * tig + 4 * ks]);
+        a0 = qw[0];
+        a2 = qw[1];
+      }
+      rec[40 + 2 * ks] = a0;
+      rec[41 + 2 * ks] = a2;
+    }
+  }
+  return pick(tig);
+}
+
+// One 64-token block: K scores, online softmax and the P.V update of the running state
+// (m_run, l_run, acc) for head tig of this lane.
+template <bool REC>
+__device__ __forceinline__ void block_step(const SStage &sg, const uint32_t *rec, float c1, int vword, uint32_t selL,
+                                           uint32_t selH, int g, int tig, float &m_run, float &l_run,
+                                           float (&acc)[8][4]) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  constexpr float c2 = kScale;
+  auto pow2 = [](int e) { return pow2f(e); };
+  // ---- K weights of this block: W[r] = hi (even g) or lo (odd g) of q * scale * 2^(7-pos-kq)
+  constexpr int KR = REC ? 16 : 18;  // K registers per token row of a lane group
+  uint32_t W[KR];
+  {
+    uint32_t nat[16];
+    const uint4 *ksv = reinterpret_cast<const uint4 *>(sg.ks + 32 * tig);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = ksv[i];
+      nat[4 * i] = v.x;
+      nat[4 * i + 1] = v.y;
+      nat[4 * i + 2] = v.z;
+      nat[4 * i + 3] = v.w;
+    }
+    uint32_t qa[20], qz[20];
+    const uint4 *rq = reinterpret_cast<const uint4 *>(rec);
+#pragma unroll
+    for (int i = 0; i < (KR + 3) / 4; ++i) {
+      const uint4 x = rq[i], y = rq[5 + i];
+      qa[4 * i] = x.x, qa[4 * i + 1] = x.y, qa[4 * i + 2] = x.z, qa[4 * i + 3] = x.w;
+      qz[4 * i] = y.x, qz[4 * i + 1] = y.y, qz[4 * i + 2] = y.z, qz[4 * i + 3] = y.w;
+    }
+#pragma unroll
+    for (int r = 0; r < KR; ++r) {
+      uint32_t b2;
+      if constexpr (REC) {  // scales of channels 32 tig + r and 32 tig + 16 + r
+        b2 = prmt(nat[r >> 1], nat[8 + (r >> 1)], (r & 1) ? 0x7632u : 0x5410u);
+      } else {
+        const uint32_t lo_src = ktab(r, 1) >= 0 ? nat[ktab(r, 1) >> 1] : 0u;
+        const uint32_t hi_src = ktab(r, 3) >= 0 ? nat[ktab(r, 3) >> 1] : 0u;
+        b2 = prmt(lo_src, hi_src, ksel(r));
+      }
+      W[r] = hfma2u(qz[r], b2, hmul2u(qa[r], b2));
+    }
+  }
+  // ---- Delta_h = sum_c q_hc min_c on the tensor cores (rows = heads, every column alike)
+  float dd[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const uint4 *kmv = reinterpret_cast<const uint4 *>(sg.km + 32 * tig);
+    const uint4 *rqd = reinterpret_cast<const uint4 *>(rec + 40);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 mv = kmv[i], qv = rqd[i];
+      mma16816<__half>(dd, qv.x, 0u, qv.y, 0u, mv.x, mv.y);
+      mma16816<__half>(dd, qv.z, 0u, qv.w, 0u, mv.z, mv.w);
+    }
+  }
+  const float dlt = __shfl_sync(0xffffffffu, dd[0], 4 * tig) * c2;
+
+  // ---- K: scores of tokens 16m+g and 16m+g+8 for head tig (two m-tiles at a time)
+  float sc[4][4];
+  {
+    const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t X0[2][6], X1[2][6];
+#pragma unroll
+      for (int mm = 0; mm < 2; ++mm) {
+        const int m = 2 * half + mm;
+        const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
+        const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
+        if constexpr (REC) {  // paired halves: windows of both 48-bit halves of the group at once
+          X0[mm][0] = u0, X0[mm][1] = prmt(u0, u1, 0x6341u), X0[mm][2] = u1;
+          X0[mm][3] = prmt(u1, u2, 0x6341u), X0[mm][4] = u2, X0[mm][5] = prmt(u2, u2, 0x3311u);
+          X1[mm][0] = v0, X1[mm][1] = prmt(v0, v1, 0x6341u), X1[mm][2] = v1;
+          X1[mm][3] = prmt(v1, v2, 0x6341u), X1[mm][4] = v2, X1[mm][5] = prmt(v2, v2, 0x3311u);
+        } else {
+          X0[mm][0] = u0, X0[mm][1] = __funnelshift_r(u0, u1, 8), X0[mm][2] = u1;
+          X0[mm][3] = __funnelshift_r(u1, u2, 8), X0[mm][4] = u2, X0[mm][5] = u2 >> 8;
+          X1[mm][0] = v0, X1[mm][1] = __funnelshift_r(v0, v1, 8), X1[mm][2] = v1;
+          X1[mm][3] = __funnelshift_r(v1, v2, 8), X1[mm][4] = v2, X1[mm][5] = v2 >> 8;
+        }
+        sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < KR / 2; ++k)
+#pragma unroll
+        for (int mm = 0; mm < 2; ++mm) {
+          const int r0 = 2 * k, r1 = 2 * k + 1;
+          if constexpr (REC) {
+            constexpr uint32_t seven = 0x00070007u;
+            const uint32_t m0 = seven << vpos(r0), m1 = seven << vpos(r1);
+            mma16816<__half>(sc[2 * half + mm], X0[mm][vwin(r0)] & m0, X1[mm][vwin(r0)] & m0,
+                             X0[mm][vwin(r1)] & m1, X1[mm][vwin(r1)] & m1, W[r0], W[r1]);
+          } else {
+            mma16816<__half>(sc[2 * half + mm], X0[mm][ktab(r0, 0)] & kmask(r0), X1[mm][ktab(r0, 0)] & kmask(r0),
+                             X0[mm][ktab(r1, 0)] & kmask(r1), X1[mm][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
+          }
+        }
+    }
+  }
+  float s[4][2];
+  float bm = -INFINITY;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    s[m][0] = sg.ka[16 * m + g] * fmaf(sc[m][0] + sc[m][1], c1, dlt);
+    s[m][1] = sg.ka[16 * m + g + 8] * fmaf(sc[m][2] + sc[m][3], c1, dlt);
+    bm = fmaxf(bm, fmaxf(s[m][0], s[m][1]));
+  }
+  bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+  bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+  bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+  const float m_new = fmaxf(m_run, bm);
+  const float r = m_run == -INFINITY ? 0.f : ex2_neg((m_run - m_new) * kLog2e);
+  const float mb = m_new * kLog2e;
+  float psum = 0.f, wsum = 0.f;
+  uint32_t PB[4][2];
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float p = ex2_neg(fmaf(s[m][i], kLog2e, -mb));
+      const float pv = p * sg.va[16 * m + g + 8 * i];
+      psum += p;
+      wsum += pv;
+      PB[m][i] = movtrans(split_hilo(pv));
+    }
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+  l_run = l_run * r + psum;  // this lane's tokens only: the head's sum is formed at the end
+  m_run = m_new;
+  if (!__all_sync(0xffffffffu, r == 1.f)) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] *= r, acc[i][1] *= r, acc[i][2] *= r, acc[i][3] *= r;
+  }
+
+  // ---- V: D[mt] (channel slots 16g+2mt | 16g+2mt+1, head tig hi | lo) over the 64 tokens
+  float D[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
+  {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      // P[pr][k]: window k of this lane's field for tokens 16ks + 2tig + 8pr (low half) and
+      // the token after it (high half)
+      uint32_t P[2][6];
+      if constexpr (REC) {
+        // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k], so both tokens'
+        // windows come from the same three words (conflict-free: banks 24 tig + 3 g + c)
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int j = 8 * ks + tig + 4 * pr;
+          const uint32_t w0 = vw[24 * j], w1 = vw[24 * j + 1], w2 = vw[24 * j + 2];
+          P[pr][0] = w0;
+          P[pr][1] = prmt(w0, w1, 0x6341u);
+          P[pr][2] = w1;
+          P[pr][3] = prmt(w1, w2, 0x6341u);
+          P[pr][4] = w2;
+          P[pr][5] = prmt(w2, w2, 0x3311u);
+        }
+      } else {
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + vword;
+        const int ta = 16 * ks + 2 * tig;
+        uint32_t L[4], H[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = ta + (u & 1) + 8 * (u >> 1);  // ta, ta+1, ta+8, ta+9
+          const uint32_t w0 = vw[12 * t], w1 = vw[12 * t + 1];
+          L[u] = prmt(w0, w1, selL);
+          H[u] = prmt(w0, w1, selH);
+        }
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int x = 2 * pr, y = 2 * pr + 1;
+          P[pr][0] = prmt(L[x], L[y], vsel(0));
+          P[pr][1] = prmt(L[x], L[y], vsel(1));
+          P[pr][2] = prmt(L[x], L[y], vsel(2));
+          P[pr][3] = prmt(H[x], H[y], vsel(3));
+          P[pr][4] = prmt(H[x], H[y], vsel(4));
+          P[pr][5] = prmt(H[x], H[y], vsel(5));
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int i0 = 2 * mt, i1 = 2 * mt + 1;
+        mma16816<__half>(D[mt], vop(P[0][vwin(i0)], i0), vop(P[0][vwin(i1)], i1), vop(P[1][vwin(i0)], i0),
+                         vop(P[1][vwin(i1)], i1), PB[ks][0], PB[ks][1]);
+      }
+    }
+  }
+  // ---- epilogue: acc' += scale_c * D + min_c * 2^vunit(c) * sum_t p_t alpha_t
+  {
+    const uint4 *vsv = reinterpret_cast<const uint4 *>(sg.vs + 16 * g);
+    const uint4 *vmv = reinterpret_cast<const uint4 *>(sg.vm + 16 * g);
+    const uint4 s0 = vsv[0], s1 = vsv[1], n0 = vmv[0], n1 = vmv[1];
+    const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const float2 bs = Elem<__half>::to_f2(sw[mt]), ms = Elem<__half>::to_f2(nw[mt]);
+      acc[mt][0] = fmaf(bs.x, D[mt][0], fmaf(ms.x, wsum * pow2(vunit(2 * mt)), acc[mt][0]));
+      acc[mt][1] = fmaf(bs.x, D[mt][1], acc[mt][1]);
+      acc[mt][2] = fmaf(bs.y, D[mt][2], fmaf(ms.y, wsum * pow2(vunit(2 * mt + 1)), acc[mt][2]));
+      acc[mt][3] = fmaf(bs.y, D[mt][3], acc[mt][3]);
+    }
+  }
+}
+
+// Combine the four warps' states of one chunk and write its partial (o, m, l) rows.
+// row0 = b * hq + h * G (the chunk's first query head row); sync() synchronises the four
+// warps (128 threads), tid is the thread's index among them.
+template <typename Sync>
+__device__ __forceinline__ void combine_chunk(SMerge &SM, int G, int tid, float m_run, float l_run,
+                                              const float (&acc)[8][4], int64_t row0, int max_chunks, int chunk,
+                                              float *part_o, float *part_ml, int &st, Sync sync) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
+  // a non-finite score or weight leaves the running sum non-finite (checked once per chunk;
+  // the merge kernel also checks every output)
+  if (tig < G && !isfinite(l_run)) st |= NSNKV_ST_OUTPUT_NONFINITE;
+  MergeSmem &M = SM.part;
+  sync();  // every warp is past its last block (the merge area may alias the block data)
+  if (tig < G) {
+    if (g == 0) {
+      M.m[warp][tig] = m_run;
+      M.l[warp][tig] = l_run;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int c = 16 * g + 2 * mt;
+      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * pow2f(-vunit(2 * mt));
+      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * pow2f(-vunit(2 * mt + 1));
+    }
+  }
+  sync();
+  if (tid < G) {  // one thread per head: the warps' weights, the chunk's max and sum
+    const int n = tid;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
+      SM.wt[w][n] = wt;
+      l += wt * M.l[w][n];
+    }
+    const int64_t row = (row0 + n) * max_chunks + chunk;
+    part_ml[row * 2] = mx;
+    part_ml[row * 2 + 1] = l;
+  }
+  sync();
+  for (int e = tid; e < G * kDim; e += kThreads) {
+    const int n = e / kDim, c = e % kDim;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) o += SM.wt[w][n] * M.acc[w][n][c];
+    const int64_t row = (row0 + n) * max_chunks + chunk;
+    part_o[row * kDim + c] = o;
+  }
+}
+
+}  // namespace s3
+
 // REC: the codes are in the paged cache's block-record orders: K as paired halves (each
 // 32-code group of a row stored as words [A half m | B half m]), V as paired rows (token
 // rows 2j and 2j+1 interleaved at 16 bits).  Otherwise the reference's packed rows.
@@ -864,7 +1204,6 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
   using namespace s3;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SSmem &S = *reinterpret_cast<SSmem *>(smem_raw);
-  constexpr float kLog2e = 1.4426950408889634f;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
   pdl_wait();               // launched with a programmatic dependency on the kernel before it
   pdl_launch_dependents();  // the native-row chunks (next grid) may fill this grid's last wave
@@ -929,65 +1268,9 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
     for (int li = warp; li < kRing && li < nloc; li += kWarps) issue(li, S.pages[li]);
   __syncwarp();
 
-  // ---- per-head q exponent kq_h: |q_h| < 2^(8 + kq_h), so q * 2^(7 - pos - kq_h) is a finite fp16
-  // (each MMA column is one head, so the shift may differ per head); every warp computes all four
-  int kqh[4];
-#pragma unroll
-  for (int hh = 0; hh < 4; ++hh) {
-    float mx = 0.f;
-    if (hh < G) {
-      const uint2 u = *reinterpret_cast<const uint2 *>(&S.qs[hh][4 * lane]);
-      const float2 x0 = Elem<__half>::to_f2(u.x), x1 = Elem<__half>::to_f2(u.y);
-      mx = fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x1.x), fabsf(x1.y)));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int e = ((__float_as_int(mx) >> 23) & 0xff) - 126;  // mx < 2^e (frexp exponent)
-    kqh[hh] = e > 8 ? e - 8 : 0;
-  }
-  auto pick = [&](int hh) { return hh == 0 ? kqh[0] : hh == 1 ? kqh[1] : hh == 2 ? kqh[2] : kqh[3]; };
-  auto pow2 = [](int e) { return __int_as_float((127 + e) << 23); };  // 2^e, -126 <= e <= 127
-
-  // ---- per-lane constant records (the same in every warp), each warp writing a quarter
-  {
-    uint32_t *rec = S.rec[lane];
-    const int hb = g >> 1, pb = g & 1;
-    const int kb = pick(hb);
-#pragma unroll
-    for (int r = 0; r < 18; ++r) {
-      if ((r & 3) != warp) continue;
-      float lo = 0.f, hi = 0.f;
-      if (REC) {  // register r: channels 32 tig + r and 32 tig + 16 + r, both at window position vpos(r)
-        if (r < 16 && hb < G) {
-          lo = __half2float(S.qs[hb][32 * tig + r]) * pow2(7 - vpos(r) - kb);
-          hi = __half2float(S.qs[hb][32 * tig + 16 + r]) * pow2(7 - vpos(r) - kb);
-        }
-      } else if (hb < G) {
-        if (ktab(r, 1) >= 0) lo = __half2float(S.qs[hb][32 * tig + ktab(r, 1)]) * pow2(7 - ktab(r, 2) - kb);
-        if (ktab(r, 3) >= 0) hi = __half2float(S.qs[hb][32 * tig + ktab(r, 3)]) * pow2(7 - ktab(r, 4) - kb);
-      }
-      __half2 s2 = __floats2half2_rn(lo, hi);
-      const uint32_t su = *reinterpret_cast<uint32_t *>(&s2);
-      rec[r] = pb ? su ^ 0x80008000u : su;  // hi lanes: q; lo lanes: -q
-      rec[20 + r] = pb ? su : 0u;           // lo lanes: q; hi lanes: 0
-    }
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      if (((ks + 2) & 3) != warp) continue;
-      uint32_t a0 = 0u, a2 = 0u;
-      if (g < G) {
-        const uint32_t *qw = reinterpret_cast<const uint32_t *>(&S.qs[g][32 * tig + 4 * ks]);
-        a0 = qw[0];
-        a2 = qw[1];
-      }
-      rec[40 + 2 * ks] = a0;
-      rec[41 + 2 * ks] = a2;
-    }
-  }
+  const int kq = build_records<REC>(S.qs, G, S.rec, lane, warp);
   __syncthreads();  // records written
-  const int kq = pick(tig);
-
-  const float c1 = kScale * pow2(17 + kq), c2 = kScale;
+  const float c1 = kScale * pow2f(17 + kq);
   const int vword = (3 * g - (g & 1)) >> 1;  // first word holding this lane's V field
   const uint32_t selL = (g & 1) ? 0x5432u : 0x3210u, selH = (g & 1) ? 0x7654u : 0x5432u;
   const uint32_t *rec = S.rec[lane];
@@ -1003,205 +1286,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       if (lane == 0) S.failed = 1;
       break;
     }
-    const SStage &sg = S.u.stage[li % kRing];
-
-    // ---- K weights of this block: W[r] = hi (even g) or lo (odd g) of q * scale * 2^(7-pos-kq)
-    constexpr int KR = REC ? 16 : 18;  // K registers per token row of a lane group
-    uint32_t W[KR];
-    {
-      uint32_t nat[16];
-      const uint4 *ksv = reinterpret_cast<const uint4 *>(sg.ks + 32 * tig);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = ksv[i];
-        nat[4 * i] = v.x;
-        nat[4 * i + 1] = v.y;
-        nat[4 * i + 2] = v.z;
-        nat[4 * i + 3] = v.w;
-      }
-      uint32_t qa[20], qz[20];
-      const uint4 *rq = reinterpret_cast<const uint4 *>(rec);
-#pragma unroll
-      for (int i = 0; i < (KR + 3) / 4; ++i) {
-        const uint4 x = rq[i], y = rq[5 + i];
-        qa[4 * i] = x.x, qa[4 * i + 1] = x.y, qa[4 * i + 2] = x.z, qa[4 * i + 3] = x.w;
-        qz[4 * i] = y.x, qz[4 * i + 1] = y.y, qz[4 * i + 2] = y.z, qz[4 * i + 3] = y.w;
-      }
-#pragma unroll
-      for (int r = 0; r < KR; ++r) {
-        uint32_t b2;
-        if constexpr (REC) {  // scales of channels 32 tig + r and 32 tig + 16 + r
-          b2 = prmt(nat[r >> 1], nat[8 + (r >> 1)], (r & 1) ? 0x7632u : 0x5410u);
-        } else {
-          const uint32_t lo_src = ktab(r, 1) >= 0 ? nat[ktab(r, 1) >> 1] : 0u;
-          const uint32_t hi_src = ktab(r, 3) >= 0 ? nat[ktab(r, 3) >> 1] : 0u;
-          b2 = prmt(lo_src, hi_src, ksel(r));
-        }
-        W[r] = hfma2u(qz[r], b2, hmul2u(qa[r], b2));
-      }
-    }
-    // ---- Delta_h = sum_c q_hc min_c on the tensor cores (rows = heads, every column alike)
-    float dd[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const uint4 *kmv = reinterpret_cast<const uint4 *>(sg.km + 32 * tig);
-      const uint4 *rqd = reinterpret_cast<const uint4 *>(rec + 40);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 mv = kmv[i], qv = rqd[i];
-        mma16816<__half>(dd, qv.x, 0u, qv.y, 0u, mv.x, mv.y);
-        mma16816<__half>(dd, qv.z, 0u, qv.w, 0u, mv.z, mv.w);
-      }
-    }
-    const float dlt = __shfl_sync(0xffffffffu, dd[0], 4 * tig) * c2;
-
-    // ---- K: scores of tokens 16m+g and 16m+g+8 for head tig (two m-tiles at a time)
-    float sc[4][4];
-    {
-      const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t X0[2][6], X1[2][6];
-#pragma unroll
-        for (int mm = 0; mm < 2; ++mm) {
-          const int m = 2 * half + mm;
-          const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
-          const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
-          if constexpr (REC) {  // paired halves: windows of both 48-bit halves of the group at once
-            X0[mm][0] = u0, X0[mm][1] = prmt(u0, u1, 0x6341u), X0[mm][2] = u1;
-            X0[mm][3] = prmt(u1, u2, 0x6341u), X0[mm][4] = u2, X0[mm][5] = prmt(u2, u2, 0x3311u);
-            X1[mm][0] = v0, X1[mm][1] = prmt(v0, v1, 0x6341u), X1[mm][2] = v1;
-            X1[mm][3] = prmt(v1, v2, 0x6341u), X1[mm][4] = v2, X1[mm][5] = prmt(v2, v2, 0x3311u);
-          } else {
-            X0[mm][0] = u0, X0[mm][1] = __funnelshift_r(u0, u1, 8), X0[mm][2] = u1;
-            X0[mm][3] = __funnelshift_r(u1, u2, 8), X0[mm][4] = u2, X0[mm][5] = u2 >> 8;
-            X1[mm][0] = v0, X1[mm][1] = __funnelshift_r(v0, v1, 8), X1[mm][2] = v1;
-            X1[mm][3] = __funnelshift_r(v1, v2, 8), X1[mm][4] = v2, X1[mm][5] = v2 >> 8;
-          }
-          sc[m][0] = sc[m][1] = sc[m][2] = sc[m][3] = 0.f;
-        }
-#pragma unroll
-        for (int k = 0; k < KR / 2; ++k)
-#pragma unroll
-          for (int mm = 0; mm < 2; ++mm) {
-            const int r0 = 2 * k, r1 = 2 * k + 1;
-            if constexpr (REC) {
-              constexpr uint32_t seven = 0x00070007u;
-              const uint32_t m0 = seven << vpos(r0), m1 = seven << vpos(r1);
-              mma16816<__half>(sc[2 * half + mm], X0[mm][vwin(r0)] & m0, X1[mm][vwin(r0)] & m0,
-                               X0[mm][vwin(r1)] & m1, X1[mm][vwin(r1)] & m1, W[r0], W[r1]);
-            } else {
-              mma16816<__half>(sc[2 * half + mm], X0[mm][ktab(r0, 0)] & kmask(r0), X1[mm][ktab(r0, 0)] & kmask(r0),
-                               X0[mm][ktab(r1, 0)] & kmask(r1), X1[mm][ktab(r1, 0)] & kmask(r1), W[r0], W[r1]);
-            }
-          }
-      }
-    }
-    float s[4][2];
-    float bm = -INFINITY;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      s[m][0] = sg.ka[16 * m + g] * fmaf(sc[m][0] + sc[m][1], c1, dlt);
-      s[m][1] = sg.ka[16 * m + g + 8] * fmaf(sc[m][2] + sc[m][3], c1, dlt);
-      bm = fmaxf(bm, fmaxf(s[m][0], s[m][1]));
-    }
-    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
-    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
-    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
-    const float m_new = fmaxf(m_run, bm);
-    const float r = m_run == -INFINITY ? 0.f : ex2_neg((m_run - m_new) * kLog2e);
-    const float mb = m_new * kLog2e;
-    float psum = 0.f, wsum = 0.f;
-    uint32_t PB[4][2];
-#pragma unroll
-    for (int m = 0; m < 4; ++m)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const float p = ex2_neg(fmaf(s[m][i], kLog2e, -mb));
-        const float pv = p * sg.va[16 * m + g + 8 * i];
-        psum += p;
-        wsum += pv;
-        PB[m][i] = movtrans(split_hilo(pv));
-      }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
-    l_run = l_run * r + psum;  // this lane's tokens only: the head's sum is formed at the end
-    m_run = m_new;
-    if (!__all_sync(0xffffffffu, r == 1.f)) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i][0] *= r, acc[i][1] *= r, acc[i][2] *= r, acc[i][3] *= r;
-    }
-
-    // ---- V: D[mt] (channel slots 16g+2mt | 16g+2mt+1, head tig hi | lo) over the 64 tokens
-    float D[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
-    {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        // P[pr][k]: window k of this lane's field for tokens 16ks + 2tig + 8pr (low half) and
-        // the token after it (high half)
-        uint32_t P[2][6];
-        if constexpr (REC) {
-          // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k], so both tokens'
-          // windows come from the same three words (conflict-free: banks 24 tig + 3 g + c)
-          const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
-#pragma unroll
-          for (int pr = 0; pr < 2; ++pr) {
-            const int j = 8 * ks + tig + 4 * pr;
-            const uint32_t w0 = vw[24 * j], w1 = vw[24 * j + 1], w2 = vw[24 * j + 2];
-            P[pr][0] = w0;
-            P[pr][1] = prmt(w0, w1, 0x6341u);
-            P[pr][2] = w1;
-            P[pr][3] = prmt(w1, w2, 0x6341u);
-            P[pr][4] = w2;
-            P[pr][5] = prmt(w2, w2, 0x3311u);
-          }
-        } else {
-          const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + vword;
-          const int ta = 16 * ks + 2 * tig;
-          uint32_t L[4], H[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int t = ta + (u & 1) + 8 * (u >> 1);  // ta, ta+1, ta+8, ta+9
-            const uint32_t w0 = vw[12 * t], w1 = vw[12 * t + 1];
-            L[u] = prmt(w0, w1, selL);
-            H[u] = prmt(w0, w1, selH);
-          }
-#pragma unroll
-          for (int pr = 0; pr < 2; ++pr) {
-            const int x = 2 * pr, y = 2 * pr + 1;
-            P[pr][0] = prmt(L[x], L[y], vsel(0));
-            P[pr][1] = prmt(L[x], L[y], vsel(1));
-            P[pr][2] = prmt(L[x], L[y], vsel(2));
-            P[pr][3] = prmt(H[x], H[y], vsel(3));
-            P[pr][4] = prmt(H[x], H[y], vsel(4));
-            P[pr][5] = prmt(H[x], H[y], vsel(5));
-          }
-        }
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int i0 = 2 * mt, i1 = 2 * mt + 1;
-          mma16816<__half>(D[mt], vop(P[0][vwin(i0)], i0), vop(P[0][vwin(i1)], i1), vop(P[1][vwin(i0)], i0),
-                           vop(P[1][vwin(i1)], i1), PB[ks][0], PB[ks][1]);
-        }
-      }
-    }
-    // ---- epilogue: acc' += scale_c * D + min_c * 2^vunit(c) * sum_t p_t alpha_t
-    {
-      const uint4 *vsv = reinterpret_cast<const uint4 *>(sg.vs + 16 * g);
-      const uint4 *vmv = reinterpret_cast<const uint4 *>(sg.vm + 16 * g);
-      const uint4 s0 = vsv[0], s1 = vsv[1], n0 = vmv[0], n1 = vmv[1];
-      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const float2 bs = Elem<__half>::to_f2(sw[mt]), ms = Elem<__half>::to_f2(nw[mt]);
-        acc[mt][0] = fmaf(bs.x, D[mt][0], fmaf(ms.x, wsum * pow2(vunit(2 * mt)), acc[mt][0]));
-        acc[mt][1] = fmaf(bs.x, D[mt][1], acc[mt][1]);
-        acc[mt][2] = fmaf(bs.y, D[mt][2], fmaf(ms.y, wsum * pow2(vunit(2 * mt + 1)), acc[mt][2]));
-        acc[mt][3] = fmaf(bs.y, D[mt][3], acc[mt][3]);
-      }
-    }
+    block_step<REC>(S.u.stage[li % kRing], rec, c1, vword, selL, selH, g, tig, m_run, l_run, acc);
     __syncwarp();
     if (lane == 0 && li + kRing < nloc) issue(li + kRing, S.pages[li + kRing]);
   }
@@ -1211,56 +1296,13 @@ __global__ void __launch_bounds__(kThreads, 4) attn_sealed3_kernel(const AttnArg
       for (int s = 0; s < kRing; ++s)
         for (int x = 0; x < 2; ++x)
           if (S.nissued[s][x] > 0) mbar_wait_bounded(&S.full[s][x], (S.nissued[s][x] - 1) & 1, a.status);
-    __syncthreads();  // the stages are reused below
   }
-
-  // ---- combine the four warps and write this chunk's partial
-#pragma unroll
-  for (int o = 4; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
-  // a non-finite score or weight leaves the running sum non-finite (checked once per chunk;
-  // the merge kernel also checks every output)
-  if (tig < G && !isfinite(l_run)) st |= NSNKV_ST_OUTPUT_NONFINITE;
-  MergeSmem &M = S.u.merge.part;
-  if (tig < G) {
-    if (g == 0) {
-      M.m[warp][tig] = m_run;
-      M.l[warp][tig] = l_run;
-    }
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int c = 16 * g + 2 * mt;
-      M.acc[warp][tig][c] = (acc[mt][0] + acc[mt][1]) * pow2(-vunit(2 * mt));
-      M.acc[warp][tig][c + 1] = (acc[mt][2] + acc[mt][3]) * pow2(-vunit(2 * mt + 1));
-    }
-  }
-  __syncthreads();
-  if (tid < G) {  // one thread per head: the warps' weights, the chunk's max and sum
-    const int n = tid;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, M.m[w][n]);
-    float l = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float wt = M.m[w][n] == -INFINITY ? 0.f : exp2f((M.m[w][n] - mx) * kLog2e);
-      S.u.merge.wt[w][n] = wt;
-      l += wt * M.l[w][n];
-    }
-    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
-    a.part_ml[row * 2] = mx;
-    a.part_ml[row * 2 + 1] = l;
-  }
-  __syncthreads();
-  for (int e = tid; e < G * kDim; e += kThreads) {
-    const int n = e / kDim, c = e % kDim;
-    float o = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) o += S.u.merge.wt[w][n] * M.acc[w][n][c];
-    const int64_t row = (b * a.hq + static_cast<int64_t>(h) * G + n) * a.max_chunks + chunk;
-    a.part_o[row * kDim + c] = o;
-  }
+  combine_chunk(S.u.merge, G, tid, m_run, l_run, acc, b * a.hq + static_cast<int64_t>(h) * G, a.max_chunks, chunk,
+                a.part_o, a.part_ml, st, [] { __syncthreads(); });
   if (st) set_status(a.status, st);
 }
+
+
 
 // ----------------------------------------------------------------- sealed INT3 blocks, K rounded like the bridge
 // attn_sealed_kernel<T, NT>: the paged cache's default path (INT3 block records with
