@@ -637,10 +637,15 @@ __global__ void __launch_bounds__(kThreads, 4) attn_native_rows_kernel(const Att
 }
 
 // Combine the chunk partials of one (sequence, query head): the log-sum-exp merge of the
-// reference (experiments/ac08/source/loop_kv_af01_kernel.py:70-84), as one online pass.
-// Thread c owns output channel c and walks the chunks once, rescaling its running sum
-// whenever a chunk raises the running maximum; the loads of different chunks do not
-// depend on each other, so they overlap instead of forming one dependent round per pass.
+// reference (experiments/ac08/source/loop_kv_af01_kernel.py:70-84).  Thread c owns output
+// channel c.  Up to kOnlineChunks chunks (batched decode) it walks them once, rescaling its
+// running sum whenever a chunk raises the maximum: one round of independent loads and no
+// block barrier.  Longer lists (one long sequence split into ~100 chunks) take two
+// parallel passes instead: the chunks' (m, l) are read once by the CTA (thread i takes
+// chunk i, i + 128, ...), their weights kept in shared memory, then every thread sums its
+// channel with independent loads -- a serial online pass over that many chunks is a long
+// dependent chain.
+constexpr int kOnlineChunks = 16;
 template <typename T>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G, T *out, float *out_f32,
                                                           float *lse) {
@@ -659,19 +664,51 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const AttnArgs a, int G
   const float *po = a.part_o + row0 * kDim + c;
   constexpr float kLog2e = 1.4426950408889634f;
   float M = -INFINITY, L = 0.f, o = 0.f;
+  if (n_chunks <= kOnlineChunks) {
 #pragma unroll 4
-  for (int i = 0; i < n_chunks; ++i) {
-    const float m = ml[2 * i], l = ml[2 * i + 1], x = po[static_cast<int64_t>(i) * kDim];
-    if (m == -INFINITY) continue;  // a chunk without a finite score contributes nothing
-    if (m > M) {
-      const float r = M == -INFINITY ? 0.f : exp2f((M - m) * kLog2e);
-      L *= r;
-      o *= r;
-      M = m;
+    for (int i = 0; i < n_chunks; ++i) {
+      const float m = ml[2 * i], l = ml[2 * i + 1], x = po[static_cast<int64_t>(i) * kDim];
+      if (m == -INFINITY) continue;  // a chunk without a finite score contributes nothing
+      if (m > M) {
+        const float r = M == -INFINITY ? 0.f : exp2f((M - m) * kLog2e);
+        L *= r;
+        o *= r;
+        M = m;
+      }
+      const float wgt = exp2f((m - M) * kLog2e);
+      L = fmaf(wgt, l, L);
+      o = fmaf(wgt, x, o);
     }
-    const float wgt = exp2f((m - M) * kLog2e);
-    L = fmaf(wgt, l, L);
-    o = fmaf(wgt, x, o);
+  } else {
+    constexpr int kMaxW = 512;
+    __shared__ float wgt[kMaxW];
+    __shared__ float red[2][4];
+    for (int i = c; i < n_chunks; i += kDim) M = fmaxf(M, ml[2 * i]);
+#pragma unroll
+    for (int s = 16; s; s >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, s));
+    if ((c & 31) == 0) red[0][c >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+    for (int i = c; i < n_chunks; i += kDim) {
+      const float m = ml[2 * i];
+      const float w = m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e);
+      L += w * ml[2 * i + 1];
+      if (i < kMaxW) wgt[i] = w;
+    }
+#pragma unroll
+    for (int s = 16; s; s >>= 1) L += __shfl_xor_sync(0xffffffffu, L, s);
+    if ((c & 31) == 0) red[1][c >> 5] = L;
+    __syncthreads();
+    L = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+    if (n_chunks <= kMaxW) {
+#pragma unroll 8
+      for (int i = 0; i < n_chunks; ++i) o += wgt[i] * po[static_cast<int64_t>(i) * kDim];
+    } else {
+      for (int i = 0; i < n_chunks; ++i) {
+        const float m = ml[2 * i];
+        o += (m == -INFINITY ? 0.f : exp2f((m - M) * kLog2e)) * po[static_cast<int64_t>(i) * kDim];
+      }
+    }
   }
   const float y = __fdiv_rn(o, L);
   const T yt = Elem<T>::from_f(y);
