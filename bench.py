@@ -30,6 +30,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -612,18 +613,20 @@ def main():
     from nsn_b200 import _lib as L
     blocks, tails = workloads.np_cfg2_lengths(args.batch)
     seqs = shard_sequences(blocks, tails, world, rank)
-    total_steps = args.warmup + args.steps
-    cache = build_cache(seqs, blocks, tails, total_steps + 1, device, rounding=args.restore_rounding)
+    total_steps = args.warmup + args.steps + min(args.steps, 16)
+    # (+ the end-to-end and latency steps below)
+    cache = build_cache(seqs, blocks, tails, total_steps + 1 + 48, device, rounding=args.restore_rounding)
+    lib = L.load()
     n_seq = len(seqs)
     q, kn, vn = step_inputs(n_seq, total_steps + 1, device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
-    # algorithmic bytes of one attention call (at the step it runs; sealing changes them) and
-    # the kernel's own extra reads (fp32 factors in place of fp16 norms)
+    # algorithmic bytes of the next step's attention (sealing changes them) and the kernel's
+    # own extra reads (fp32 factors in place of fp16 norms), from the cache's host counters
     def attn_bytes():
-        nb = cache.n_blocks.long()
-        tl = cache.tail_len.long() + 1  # + the appended token
+        nb = cache.host_blocks.astype(np.int64)
+        tl = cache.host_tail.astype(np.int64) + 1  # + the appended token
         algo = int((2 * 8 * (nb * BLOCK_BYTES + tl * 256)).sum() + 2 * n_seq * 32 * 256)
         over = int((2 * 8 * nb).sum()) * FACTOR_OVERHEAD if cache.uses_alpha_path() else 0
         return algo, over
@@ -633,37 +636,48 @@ def main():
     torch.cuda.synchronize(device)
     cache.check()
 
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    bytes_per = []
+    E = lambda: torch.cuda.Event(enable_timing=True)
+    ev = [(E(), E()) for _ in range(args.steps)]
+    launches = 0
     if dist:
         dist.barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clk:
+        # the timed steps: L2 flushed before each, one event pair around each step
         for i in range(args.steps):
-            bytes_per.append(attn_bytes() if i < 4 or i == args.steps - 1 else None)
             flush.zero_()
             s = args.warmup + i
             ev[i][0].record(stream)
-            cache.attend(q[s], kn[s], vn[s])
+            cache.step(q[s], kn[s], vn[s])
             ev[i][1].record(stream)
-            cache.seal(1)
-            ev[i][2].record(stream)
+            launches += lib.nsnkv_paged_plan_last_launches(cache._plan)
         torch.cuda.synchronize(device)
     if dist:
         dist.barrier()
     cache.check()
-    attn_ms = [a.elapsed_time(b) for a, b, _ in ev]
-    step_ms = [a.elapsed_time(c) for a, _, c in ev]
+    step_ms = [a.elapsed_time(b) for a, b in ev]
     mean_step = sum(step_ms) / len(step_ms)
-    mean_attn = sum(attn_ms) / len(attn_ms)
+    # the attention launches of further steps, timed apart from their seal by an event the
+    # step records between them (that event costs the seal its overlap, so these steps are
+    # not the timed ones); their algorithmic bytes from the host counters
+    n_attn = min(args.steps, 16)
+    aev = [(E(), E()) for _ in range(n_attn)]
+    bytes_per = []
+    for i in range(n_attn):
+        bytes_per.append(attn_bytes())
+        flush.zero_()
+        s = args.warmup + args.steps + i
+        aev[i][0].record(stream)
+        cache.step(q[s], kn[s], vn[s], attn_event=aev[i][1])
+    torch.cuda.synchronize(device)
+    cache.check()
+    mean_attn = sum(a.elapsed_time(b) for a, b in aev) / n_attn
     t = torch.tensor([mean_step, mean_attn], dtype=torch.float64, device=device)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     mean_step, mean_attn_max = t.tolist()
-    known = [b for b in bytes_per if b is not None]
-    bytes_attn = sum(b[0] for b in known) / len(known)
-    bytes_over = sum(b[1] for b in known) / len(known)
+    bytes_attn = sum(b[0] for b in bytes_per) / n_attn
+    bytes_over = sum(b[1] for b in bytes_per) / n_attn
 
     # ---- both tensor-core kernels on the same blocks, attention only (no append): the
     # library default (K rounded like the bridge) and the exact restore
@@ -806,9 +820,9 @@ def main():
             "restore_rounding": args.restore_rounding,
             "kernels": kernels,
             "e2e": e2e,
-            # attend: sealed kernel + tail kernel + merge (restore kernel + merge without the renorm
-            # path); seal: one launch (encode + renorm + counters), two without the renorm path
-            "gpu_launches": 4 * args.steps,
+            # this library's kernels in the timed steps, as nsnkv_paged_plan_last_launches counted
+            # them: attention (chunk grid, tail grid, merge unless fused) and the seal
+            "gpu_launches": launches,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "cfg4_splitkv": cfg4,

@@ -153,7 +153,13 @@ int nsnkv_unpack(const uint8_t *payload, int64_t count, int bits, uint8_t *out, 
  *   max_blocks   upper bound of n_blocks[b] (sizes the launch grid)
  *   out          [batch][hq][128] of dtype; out_f32 (may be NULL) fp32 copy;
  *   lse          [batch][hq] log-sum-exp of the scaled scores (may be NULL)
- *   workspace    device scratch of nsnkv_decode_attn_workspace_bytes() bytes
+ *   workspace    device scratch of nsnkv_decode_attn_workspace_bytes() bytes, 16-byte
+ *                aligned, any contents; calls that may run at the same time need
+ *                separate ones.
+ *                It holds the chunk partials and, first, one 64-bit word per
+ *                (sequence, kv head) in which the chunk CTAs count their arrival under
+ *                a per-call epoch; with at most 32 chunks per sequence the last CTA to
+ *                arrive merges the sequence's partials, and no merge kernel runs.
  * Scores use scale 1/sqrt(128); softmax and accumulation are fp32.
  */
 int nsnkv_decode_attn(int64_t batch, int hq, int h, int bits, int dtype, const void *q,
@@ -299,6 +305,61 @@ int nsnkv_seal_full_tails_alpha(int64_t batch, int h, int bits, int dtype,
                                 uint8_t *v_codes, uint16_t *v_norm, uint16_t *v_min, uint16_t *v_scale,
                                 float *k_alpha, float *v_alpha, int64_t blk_bytes, int rec_order, int32_t *seq_counters,
                                 int64_t blk_stride_head, int64_t blk_stride_page, int32_t *status, void *stream);
+
+/*
+ * Decode-step plan over a paged cache with the seal-at-64 policy.  One step is
+ * nsnkv_decode_attn_alpha (append k_new / v_new, attend with q; max_tail 63,
+ * blocks_total from the host counters) followed by nsnkv_seal_full_tails_alpha
+ * (pending_append 1; nsnkv_seal_full_tails when the pools carry no renorm factors),
+ * over the pointers of the descriptor, which the plan copies.  Together they replace
+ * the reference's per-step append + attention + post_decode
+ * (experiments/nb06/source/loop_kv_nb06_attention.py:33-88,
+ * experiments/nb06/source/loop_kv_nb06_packed.py:54-56).
+ *   struct_bytes     sizeof(nsnkv_paged_desc) as the caller laid it out
+ *   flags            nsnkv_decode_attn_alpha flags (they need k_alpha / v_alpha)
+ *   tail buffers     64 rows per (sequence, kv head): tail_stride_head >= 64
+ *   workspace        >= nsnkv_decode_attn_workspace_bytes(batch, hq, h, max_blocks, 63)
+ *   seq_counters     as for nsnkv_seal_full_tails_alpha (may be NULL)
+ *   host_n_blocks / host_tail_len  int32 [batch] in host memory, equal to the device
+ *                    counters when the plan is made; the plan reads them for the
+ *                    chunk sizing and advances them in place after every step, so they
+ *                    stay equal to the device counters without a device read.  They
+ *                    must outlive the plan.
+ * attn_event (a cudaEvent_t, may be NULL) is recorded on the stream between the attention
+ * launches and the seal, for timing the two apart.
+ * nsnkv_paged_step returns NSNKV_ERR_TOO_LARGE, launching nothing, when a sequence
+ * would need a page beyond max_blocks.  A plan is used by one thread at a time; all
+ * the memory it names stays owned by the caller.
+ */
+typedef struct nsnkv_paged_desc {
+  int64_t struct_bytes;
+  int64_t batch;
+  int32_t hq, h, bits, dtype;
+  int32_t flags, max_blocks;
+  uint8_t *k_codes;
+  uint16_t *k_norm, *k_min, *k_scale;
+  float *k_alpha;
+  uint8_t *v_codes;
+  uint16_t *v_norm, *v_min, *v_scale;
+  float *v_alpha;
+  int64_t blk_bytes, blk_stride_head, blk_stride_page;
+  const int32_t *block_table;
+  int64_t table_stride;
+  int32_t *n_blocks, *tail_len;
+  void *k_tail, *v_tail;
+  int64_t tail_stride_seq, tail_stride_head;
+  int32_t *seq_counters;
+  void *workspace;
+  int64_t workspace_bytes;
+  int32_t *status;
+  int32_t *host_n_blocks, *host_tail_len;
+} nsnkv_paged_desc;
+int nsnkv_paged_plan_create(const nsnkv_paged_desc *desc, void **plan);
+int nsnkv_paged_step(void *plan, const void *q, const void *k_new, const void *v_new, void *out,
+                     void *attn_event, void *stream);
+/* Kernels the plan's last successful step launched (0 before the first step). */
+int nsnkv_paged_plan_last_launches(void *plan);
+int nsnkv_paged_plan_destroy(void *plan);
 
 /*
  * Combine per-shard attention partials (one row per shard) into the final

@@ -75,6 +75,10 @@ SIGNATURES = [
     ("nsnkv_seal_full_tails_alpha", c_int, [c_int64, c_int, c_int, c_int, P, P, c_int64, c_int64, P, P, c_int, P,
                                             c_int64, P, P, P, P, P, P, P, P, P, P, c_int64, c_int, P, c_int64,
                                             c_int64, P, P]),
+    ("nsnkv_paged_plan_create", c_int, [P, P]),
+    ("nsnkv_paged_step", c_int, [P, P, P, P, P, P, P]),
+    ("nsnkv_paged_plan_last_launches", c_int, [P]),
+    ("nsnkv_paged_plan_destroy", c_int, [P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),
@@ -82,6 +86,23 @@ SIGNATURES = [
     ("nsnkv_int3asym_decode", c_int, [P, P, P, P, c_int64, c_int64, c_int, P, P]),
     ("nsnkv_k1c_scores", c_int, [c_int, c_int64, c_int, c_int, c_int64, c_int, P, P, P, P, P, P, P]),
 ]
+
+
+class PagedDesc(ctypes.Structure):
+    """nsnkv_paged_desc (include/nsnkv.h), field for field."""
+    _fields_ = [("struct_bytes", c_int64), ("batch", c_int64),
+                ("hq", c_int32), ("h", c_int32), ("bits", c_int32), ("dtype", c_int32),
+                ("flags", c_int32), ("max_blocks", c_int32),
+                ("k_codes", P), ("k_norm", P), ("k_min", P), ("k_scale", P), ("k_alpha", P),
+                ("v_codes", P), ("v_norm", P), ("v_min", P), ("v_scale", P), ("v_alpha", P),
+                ("blk_bytes", c_int64), ("blk_stride_head", c_int64), ("blk_stride_page", c_int64),
+                ("block_table", P), ("table_stride", c_int64),
+                ("n_blocks", P), ("tail_len", P),
+                ("k_tail", P), ("v_tail", P),
+                ("tail_stride_seq", c_int64), ("tail_stride_head", c_int64),
+                ("seq_counters", P), ("workspace", P), ("workspace_bytes", c_int64), ("status", P),
+                ("host_n_blocks", P), ("host_tail_len", P)]
+
 
 _lib = None
 

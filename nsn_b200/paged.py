@@ -4,13 +4,15 @@ The reference grows each slot's packed groups with ``torch.cat`` on every seal
 (experiments/nb06/source/loop_kv_nb06_packed.py:36-50, ``append_group``
 loop_kv_nb06_codec.py:40-45), which re-copies the whole packed history and syncs
 the host.  Here the packed blocks live in a fixed page pool addressed through a
-block table, and one decode step is three launches with no host sync:
+block table, and one decode step (``step``) is one native call, nsnkv_paged_step,
+over a plan made once per cache, with no host sync:
 
-  1. nsnkv_decode_attn   appends the new K/V token to each sequence's fp16 tail
+  1. nsnkv_decode_attn_alpha  appends the new K/V token to each sequence's fp16 tail
                          and attends over sealed blocks + tail (split-KV partials
                          + log-sum-exp merge);
-  2. nsnkv_seal_full_tails  encodes every tail that reached 64 tokens into the
-                         sequence's next page and advances n_blocks / tail_len.
+  2. nsnkv_seal_full_tails_alpha  encodes every tail that reached 64 tokens into the
+                         sequence's next page and advances n_blocks / tail_len;
+  3. on the host, the plan advances this object's copies of those counters.
 
 Policy: seal whenever a tail reaches 64 tokens, so tails hold 0..63 tokens
 between steps (the benchmark specification's batched policy; the reference's
@@ -31,6 +33,7 @@ Layout (head-major pools so one sequence's blocks of one head are contiguous):
 """
 from __future__ import annotations
 
+import ctypes
 import struct
 
 import numpy as np
@@ -179,6 +182,9 @@ class PagedKVCache:
         w.require(mode != "exact" or (bits == 3 and dtype == torch.float16 and self.hq // h <= 4),
                   "exact attention needs an INT3 fp16 cache with hq / h <= 4")
         self.device = torch.device(device)
+        w.require(self.device.type == "cuda", "paged cache device (CUDA only)")
+        if self.device.index is None:  # "cuda": the current device, named, so tensors compare equal
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.pages = batch * max_blocks
         cb = w.code_bytes(bits)
         dev = self.device
@@ -202,8 +208,9 @@ class PagedKVCache:
         # host copies of n_blocks / tail_len, kept without reading the device: every change
         # to the counters comes from this object's prefill, import and seal (seal-at-64 is
         # deterministic); they size the attention kernels' work (never their correctness)
-        self.host_blocks = np.zeros(batch, np.int64)
-        self.host_tail = np.zeros(batch, np.int64)
+        # (int32, changed in place only: the step plan advances them through their memory)
+        self.host_blocks = np.zeros(batch, np.int32)
+        self.host_tail = np.zeros(batch, np.int32)
         self.k_tail = torch.zeros((batch, h, w.BLOCK, w.DIM), dtype=dtype, device=dev)
         self.v_tail = torch.zeros_like(self.k_tail)
         self.status = L.status_tensor(dev)
@@ -212,6 +219,40 @@ class PagedKVCache:
         lib = L.load()
         self.ws = torch.empty(lib.nsnkv_decode_attn_workspace_bytes(batch, self.hq, h, max_blocks, w.BLOCK - 1),
                               dtype=torch.uint8, device=dev)
+        self._plan = None
+        self._plan = self._make_plan(lib)
+        self._step_fn = lib.nsnkv_paged_step
+        self._q_shape = (batch, self.hq, w.DIM)
+        self._kv_shape = (batch, h, w.DIM)
+
+    def _make_plan(self, lib):
+        """The native decode-step plan (nsnkv_paged_plan_create) over this cache's buffers."""
+        kp, vp = self.k_pool, self.v_pool
+        alpha = "alpha" in kp
+        flags = 0
+        if alpha:
+            flags = L.ATTN_RECORD_ORDER | (L.ATTN_EXACT if self.restore_rounding == "exact" else 0)
+        p = lambda t: t.data_ptr() if t is not None else None
+        d = L.PagedDesc(
+            struct_bytes=ctypes.sizeof(L.PagedDesc), batch=self.batch, hq=self.hq, h=self.h, bits=self.bits,
+            dtype=L.DTYPE_CODE[self.dtype], flags=flags, max_blocks=self.max_blocks,
+            k_codes=p(kp["codes"]), k_norm=p(kp["norm"]), k_min=p(kp["min"]), k_scale=p(kp["scale"]),
+            k_alpha=p(kp.get("alpha")), v_codes=p(vp["codes"]), v_norm=p(vp["norm"]), v_min=p(vp["min"]),
+            v_scale=p(vp["scale"]), v_alpha=p(vp.get("alpha")), blk_bytes=self.blk_bytes,
+            blk_stride_head=self.pages, blk_stride_page=1, block_table=p(self.block_table),
+            table_stride=self.max_blocks, n_blocks=p(self.n_blocks), tail_len=p(self.tail_len),
+            k_tail=p(self.k_tail), v_tail=p(self.v_tail), tail_stride_seq=self.h * w.BLOCK,
+            tail_stride_head=w.BLOCK, seq_counters=p(self.seal_counters) if alpha else None,
+            workspace=p(self.ws), workspace_bytes=self.ws.numel(), status=p(self.status),
+            host_n_blocks=self.host_blocks.ctypes.data, host_tail_len=self.host_tail.ctypes.data)
+        handle = ctypes.c_void_p()
+        L.check(lib.nsnkv_paged_plan_create(ctypes.byref(d), ctypes.byref(handle)), "nsnkv_paged_plan_create")
+        return handle
+
+    def __del__(self):
+        plan, self._plan = getattr(self, "_plan", None), None
+        if plan is not None and L._lib is not None:
+            L._lib.nsnkv_paged_plan_destroy(plan)
 
     # ------------------------------------------------------------ prefill
     def prefill(self, b: int, k: torch.Tensor, v: torch.Tensor):
@@ -324,7 +365,7 @@ class PagedKVCache:
         t = self.host_tail + pending_append
         full = t >= w.BLOCK
         self.host_blocks += full
-        self.host_tail = t - w.BLOCK * full
+        self.host_tail[:] = t - w.BLOCK * full
         lib = L.load()
         if self.records is None:
             rc = lib.nsnkv_seal_full_tails(
@@ -348,10 +389,30 @@ class PagedKVCache:
             L.ptr(self.status), L.stream_handle(self.device))
         L.check(rc, "nsnkv_seal_full_tails_alpha")
 
-    def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, out=None):
-        """One decode step: append (k_new, v_new) [batch, h, 128], attend with q, seal full tails."""
-        o = self.attend(q, k_new, v_new, out=out)
-        self.seal(1)
+    def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, out=None, attn_event=None):
+        """One decode step: append (k_new, v_new) [batch, h, 128], attend with q [batch, hq, 128],
+        seal full tails.  One native call (nsnkv_paged_step): the attention launches of
+        ``attend`` and the seal of ``seal(1)``, with the host counters advanced in place.
+        ``attn_event`` (a torch.cuda.Event) is recorded between the attention and the seal."""
+        o = self.out if out is None else out
+        dt, dev = self.dtype, self.device
+        ok = (q.shape == self._q_shape and o.shape == self._q_shape and k_new.shape == self._kv_shape
+              and v_new.shape == self._kv_shape and q.dtype == dt and k_new.dtype == dt and v_new.dtype == dt
+              and o.dtype == dt and q.device == dev and k_new.device == dev and v_new.device == dev
+              and o.device == dev and q.is_contiguous() and k_new.is_contiguous() and v_new.is_contiguous()
+              and o.is_contiguous())
+        w.require(ok, "paged step operands: contiguous q / out [batch, hq, 128] and k_new / v_new "
+                      "[batch, h, 128] in the cache dtype, on the cache device")
+        stream = torch.cuda.current_stream(dev)
+        ev = None
+        if attn_event is not None:
+            if not attn_event.cuda_event:  # torch creates the event at its first record
+                attn_event.record(stream)
+            ev = attn_event.cuda_event
+        rc = self._step_fn(self._plan, q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), o.data_ptr(), ev,
+                           stream.cuda_stream)
+        if rc:
+            L.check(rc, "nsnkv_paged_step")
         return o
 
     def check(self):

@@ -66,3 +66,54 @@ def test_argument_errors_return_before_launch():
                                  P(16), 1 << 30, P(16), P(None)) == _lib.ERR_ARG
     # empty work is a no-op
     assert lib.nsnkv_pack(P(None), 0, 3, P(None), P(None), P(None)) == _lib.OK
+
+
+def test_paged_plan_descriptor_and_host_checks():
+    """nsnkv_paged_plan_create validates the descriptor on the host (no device touched), and
+    nsnkv_paged_step rejects a step that would need a page beyond max_blocks before it
+    launches anything."""
+    import numpy as np
+    from nsn_b200 import _lib
+    lib = _lib.load()
+    assert ctypes.sizeof(_lib.PagedDesc) == 256  # the C layout of nsnkv_paged_desc on x86-64
+    batch, hq, h, max_blocks = 3, 8, 2, 4
+    nb = np.array([0, 4, 2], np.int32)
+    tl = np.array([5, 62, 0], np.int32)
+    fake = 1 << 20  # a 16-byte aligned address that is never dereferenced here
+    ws = lib.nsnkv_decode_attn_workspace_bytes(batch, hq, h, max_blocks, 63)
+
+    def desc(**kw):
+        d = dict(struct_bytes=ctypes.sizeof(_lib.PagedDesc), batch=batch, hq=hq, h=h, bits=3, dtype=_lib.F16,
+                 flags=_lib.ATTN_RECORD_ORDER, max_blocks=max_blocks, blk_bytes=7680, blk_stride_head=12,
+                 blk_stride_page=1, table_stride=max_blocks, tail_stride_seq=h * 64, tail_stride_head=64,
+                 workspace_bytes=ws, host_n_blocks=nb.ctypes.data, host_tail_len=tl.ctypes.data)
+        for f in ("k_codes", "k_norm", "k_min", "k_scale", "k_alpha", "v_codes", "v_norm", "v_min", "v_scale",
+                  "v_alpha", "block_table", "n_blocks", "tail_len", "k_tail", "v_tail", "seq_counters", "workspace",
+                  "status"):
+            d[f] = fake
+        d.update(kw)
+        return _lib.PagedDesc(**d)
+
+    def create(**kw):
+        handle = ctypes.c_void_p()
+        return lib.nsnkv_paged_plan_create(ctypes.byref(desc(**kw)), ctypes.byref(handle)), handle
+
+    assert create(struct_bytes=200)[0] == _lib.ERR_ARG
+    assert create(hq=7)[0] == _lib.ERR_ARG
+    assert create(k_alpha=None)[0] == _lib.ERR_ARG  # one factor array without the other
+    assert create(k_alpha=None, v_alpha=None)[0] == _lib.ERR_ARG  # flags need the factors
+    assert create(workspace_bytes=ws - 1)[0] == _lib.ERR_ARG
+    assert create(tail_stride_head=63)[0] == _lib.ERR_ARG
+    tl[2] = 64
+    assert create()[0] == _lib.ERR_ARG  # a host counter out of range
+    tl[2] = 0
+    rc, handle = create()
+    assert rc == _lib.OK and handle.value
+    P = ctypes.c_void_p
+    assert lib.nsnkv_paged_step(handle, P(None), P(fake), P(fake), P(fake), P(None), P(None)) == _lib.ERR_ARG
+    # sequence 1 holds max_blocks pages and a tail of 62: one more token fits, a second would not
+    tl[1] = 63
+    assert lib.nsnkv_paged_step(handle, P(fake), P(fake), P(fake), P(fake), P(None), P(None)) == _lib.ERR_TOO_LARGE
+    assert list(nb) == [0, 4, 2] and list(tl) == [5, 63, 0]  # unchanged by a rejected step
+    assert lib.nsnkv_paged_plan_destroy(handle) == _lib.OK
+    assert lib.nsnkv_paged_plan_destroy(P(None)) == _lib.ERR_ARG
