@@ -13,8 +13,9 @@ at the parity bar of oracle.TOLERANCE.  Checked here:
 * the fp32 context against fp64 attention over K rounded and V exact, the arithmetic the
   kernel implements, with a bar a little above fp32 accumulation;
 * the full-size cfg1 sequence (511 blocks + 64 tail tokens) and the full cfg2 benchmark
-  state (64 sequences, 32-block chunks, 64 decode steps with a seal per step on average),
-  against the fp64 oracle on a sample of sequences and steps; the cfg2 state also through
+  state (64 sequences, 32-block chunks, 64 decode steps through PagedKVCache.step, the
+  native step plan, with a seal per step on average), against the fp64 oracle on a sample
+  of sequences and steps; the cfg2 state also through
   restore_rounding="exact" (the benchmark's headline kernel), whose parity with the bridge
   holds for the benchmark's 1/sqrt(128)-scaled queries.
 """
@@ -218,6 +219,36 @@ def test_default_path_flags_nonfinite_metadata(where):
         cache.check()
 
 
+@pytest.mark.parametrize("mode", ["k", "exact"])
+def test_sequence_without_tokens(mode):
+    """A sequence with neither sealed blocks nor tail rows beside two others: its outputs are
+    the merge of zero partials (0 / 0, flagged as non-finite), the others' match the bridge
+    (small batch: the merge runs fused in the chunk kernels)."""
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(17)
+    h, hq, lens = 2, 8, [0, 64 * 3 + 9, 64 * 2]
+    cache = new_cache(len(lens), h, hq, 4, torch.float16, mode)
+    srcs = []
+    for b, L in enumerate(lens):
+        k = workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5).astype(np.float32)
+        v = workloads.np_kv(rng, (h, L, 128), (), 0.5).astype(np.float32)
+        if L:
+            fill(cache, b, k, v)
+        srcs.append((k, v))
+    q = (rng.standard_normal((len(lens), hq, 128)) / np.sqrt(128)).astype(np.float16)
+    out = cache.attend(torch.from_numpy(q).cuda()).float().cpu().numpy()
+    assert np.isnan(out[0]).all()
+    with pytest.raises(w.NumericalFailure):
+        cache.check()
+    for b in (1, 2):
+        k, v = srcs[b]
+        nb = lens[b] // 64
+        kb, vb = rows(k, nb, "float16", "bridge"), rows(v, nb, "float16", "bridge")
+        ok, err = O.within_tolerance(out[b], attention64(q[b].astype(np.float64), kb, vb), *O.TOLERANCE["float16"])
+        assert ok, (b, err)
+
+
 def test_cfg1_full_size_default_path():
     """cfg1: one 32768-token sequence, 511 sealed INT3 blocks + a 64-token native tail, 32:8."""
     from nsn_b200 import workloads
@@ -276,25 +307,32 @@ def test_cfg2_full_bench_state(mode):
     out32 = torch.empty((B, hq, 128), dtype=torch.float32, device="cuda")
     seals = 0
     for s in range(steps):
+        if s in check_at:  # the fp32 context over the history, before this step's append
+            cache.attend(qs[s], out_f32=out32)
+            ctx = out32.cpu().numpy().copy()
         before = cache.n_blocks.clone()
-        o = cache.attend(qs[s], new_k[:, :, s].contiguous(), new_v[:, :, s].contiguous(), out_f32=out32)
-        cache.seal(1)
+        o = cache.step(qs[s], new_k[:, :, s].contiguous(), new_v[:, :, s].contiguous())  # nsnkv_paged_step
         seals += int((cache.n_blocks - before).sum())
         if s in check_at:
-            outs[s] = (o.float().cpu().numpy(), out32.cpu().numpy().copy())
+            outs[s] = (o.float().cpu().numpy(), ctx)
     cache.check()
     assert seals == B  # every tail of 0..63 tokens reaches 64 exactly once in 64 appends
     for b in sample:
         L0, rk, rv = host[b]
         for s in check_at:
-            T = L0 + s + 1     # attended tokens: the history plus this step's token
-            nb = (T - 1) // 64  # blocks sealed before this step's attention
             q64 = qs[s, b].float().cpu().numpy().astype(np.float64)
-            kb, vb, vx = rk.rows(T, nb, "bridge"), rv.rows(T, nb, "bridge"), rv.rows(T, nb, "exact")
             got, got32 = outs[s]
+            # the step's output: the history plus this step's token, blocks sealed before it
+            T = L0 + s + 1
+            nb = (T - 1) // 64
+            kb, vb = rk.rows(T, nb, "bridge"), rv.rows(T, nb, "bridge")
             ok, err = O.within_tolerance(got[b], attention64(q64, kb, vb), *O.TOLERANCE["float16"])
             assert ok, ("bridge", mode, b, s, err)
-            kk = kb if mode == "k" else rk.rows(T, nb, "exact")
+            # the context before the append, against the mode's own arithmetic
+            T = L0 + s
+            nb = T // 64
+            vx = rv.rows(T, nb, "exact")
+            kk = rk.rows(T, nb, "bridge" if mode == "k" else "exact")
             bar = vexact_bar(q64, kk, vx) + (exact_k_bar(q64, kk, vx) if mode == "exact" else 0.0)
             ok, err = O.within_tolerance(got32[b], attention64(q64, kk, vx), KROUND[0], KROUND[1] + bar)
             assert ok, ("own arithmetic", mode, b, s, err)
