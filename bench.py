@@ -778,8 +778,9 @@ def main():
         torch.cuda.empty_cache()
         cfg4 = cfg4_measure(args, rank, world, local, dist, with_encode=False, steps=min(args.steps, 20), warmup=3)
         cfg4["what"] = ("cfg4 split-KV decode step: one 131072-token INT5 sequence (2047 blocks + 64 tail, GQA "
-                        "64:8) split by block ranges over the ranks; local fused attention + one NCCL all-gather "
-                        "of the (o, lse) records + merge kernel, replayed as a CUDA graph, L2 flushed; "
+                        "64:8) split by block ranges over the ranks; local fused attention (attn_sealed_kernel "
+                        "over INT5 block records, K rounded like the bridge) + one NCCL all-gather of the "
+                        "(o, lse) records + merge kernel, replayed as a CUDA graph, L2 flushed; "
                         "gather_merge_ms = step - local attention alone (max over ranks)")
     if rank == 0:
         cpu = None

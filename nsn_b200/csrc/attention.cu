@@ -1532,10 +1532,63 @@ template <> __device__ __forceinline__ uint32_t round2<__nv_bfloat16>(float lo, 
 
 constexpr int kQf = 16;  // words of a lane's q fragments per head tile: 8 k-steps x (b0, b1)
 
-template <int NT>
+// A block record of BITS-bit codes: K codes, min, scale, factors, then the same for V.
+template <int BITS>
+struct RStage {
+  static constexpr int kCodeBytes = kBlock * kDim * BITS / 8;
+  uint8_t kc[kCodeBytes];
+  uint16_t km[kDim], ks[kDim];
+  float ka[kBlock];
+  uint8_t vc[kCodeBytes];
+  uint16_t vm[kDim], vs[kDim];
+  float va[kBlock];
+};
+static_assert(sizeof(RStage<3>) == sizeof(SStage) && sizeof(RStage<5>) == 11776, "record sizes");
+
+// Code i (0..15) of a 16-code field starting at bit 0 of a 16-bit-window sequence: it sits
+// at bit craw of byte window cwin.  For the fp16 operand forms the code must end at or
+// below bit 10 of its window (code * 2^pos exact as 1024 + code * 2^pos, or as a
+// subnormal); INT5 codes at window bits 6 and 7 are shifted down by 2 first (cshift),
+// which moves the other half's low bits only into bits 14..15, outside the code's mask.
+// For INT3 every shift is 0 and cpos == vpos, cwin == vwin.
+template <int BITS> __host__ __device__ constexpr int cwin(int i) { return (BITS * i) >> 3; }
+template <int BITS> __host__ __device__ constexpr int craw(int i) { return BITS * i - 8 * cwin<BITS>(i); }
+template <int BITS> __host__ __device__ constexpr int cshift(int i) { return craw<BITS>(i) + BITS > 10 ? 2 : 0; }
+template <int BITS> __host__ __device__ constexpr int cpos(int i) { return craw<BITS>(i) - cshift<BITS>(i); }
+template <int BITS> __host__ __device__ constexpr uint32_t cmask(int i) {
+  return ((1u << BITS) - 1u) * 0x00010001u << cpos<BITS>(i);
+}
+template <int BITS> __host__ __device__ constexpr int cunit(int i) {
+  return cpos<BITS>(i) <= kVNormal ? cpos<BITS>(i) : cpos<BITS>(i) - 24;
+}
+static_assert(cwin<3>(13) == vwin(13) && cpos<3>(13) == vpos(13) && cunit<3>(5) == vunit(5), "INT3 forms");
+// The code of register i in window word x (two tokens or two channels, one per half).
+template <int BITS>
+__device__ __forceinline__ uint32_t code2(uint32_t x, int i) {
+  return (cshift<BITS>(i) ? x >> cshift<BITS>(i) : x) & cmask<BITS>(i);
+}
+// V operand of channel i (see vunit): normal fp16 code * 2^cpos up to kVNormal, else subnormal.
+template <int BITS>
+__device__ __forceinline__ uint32_t vopb(uint32_t x, int i) {
+  const uint32_t c = code2<BITS>(x, i);
+  return cpos<BITS>(i) <= kVNormal ? hsub2u(c | kMagic2, kMagic2) : c;
+}
+// The 2 BITS byte windows of a field held in BITS paired words w[0..BITS): window 2m is
+// word m, window 2m+1 its high byte joined with the next word's low byte (per half).
+template <int BITS>
+__device__ __forceinline__ void windows(const uint32_t (&w)[BITS], uint32_t (&x)[2 * BITS]) {
+#pragma unroll
+  for (int m = 0; m < BITS; ++m) {
+    x[2 * m] = w[m];
+    x[2 * m + 1] = m + 1 < BITS ? prmt(w[m], w[m + 1], 0x6341u) : prmt(w[m], w[m], 0x3311u);
+  }
+}
+template <int NT, int BITS> constexpr int kCtasPerSm = NT == 1 && BITS == 3 ? 3 : 2;
+
+template <int NT, int BITS>
 struct KSmem {
   union {
-    SStage stage[kRing];
+    RStage<BITS> stage[kRing];
     SMerge merge;  // after the last block of every warp
   } u;
   uint32_t qf[32][NT * kQf + 2];  // per lane: Q.K B fragments; stride 2 * odd words (conflict-free 64-bit loads)
@@ -1548,11 +1601,12 @@ struct KSmem {
 
 }  // namespace s3
 
-template <typename T, int NT>
-__global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(const AttnArgs a) {
+template <typename T, int NT, int BITS>
+__global__ void __launch_bounds__(kThreads, s3::kCtasPerSm<NT, BITS>) attn_sealed_kernel(const AttnArgs a) {
   using namespace s3;
+  using Stg = RStage<BITS>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  KSmem<NT> &S = *reinterpret_cast<KSmem<NT> *>(smem_raw);
+  KSmem<NT, BITS> &S = *reinterpret_cast<KSmem<NT, BITS> *>(smem_raw);
   constexpr float kLog2e = 1.4426950408889634f;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
   pdl_wait();               // launched with a programmatic dependency on the kernel before it
@@ -1573,11 +1627,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
   // record); the warp that finishes block li starts the copy of block li + kRing.
   auto issue = [&](int li, int32_t page) {
     const int64_t bi = static_cast<int64_t>(h) * a.sh + static_cast<int64_t>(page) * a.sp;
-    SStage &sg = S.u.stage[li % kRing];
+    Stg &sg = S.u.stage[li % kRing];
     uint64_t *bar = &S.full[li % kRing][(li / kRing) & 1];
     S.nissued[li % kRing][(li / kRing) & 1] += 1;
-    mbar_expect_tx(bar, sizeof(SStage));
-    bulk_g2s(sg.kc, a.kc + bi * a.cs, sizeof(SStage), bar);
+    mbar_expect_tx(bar, sizeof(Stg));
+    bulk_g2s(sg.kc, a.kc + bi * a.cs, sizeof(Stg), bar);
   };
   // q (8 bytes per thread and pass) and the chunk's pages staged in shared memory
   uint2 qv[2] = {make_uint2(0u, 0u), make_uint2(0u, 0u)};
@@ -1610,13 +1664,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
   __syncwarp();
 
   // ---- Q.K B fragments of every lane (the same in every warp, each warp writing a quarter):
-  // k-step p pairs registers r0 = 3p mod 8 and r0 + 8 (both at window position p);
+  // k-step p pairs registers r0 = BITS p mod 8 and r0 + 8 (both at window bit p; BITS is its
+  // own inverse mod 8 for 3 and 5);
   // b0 = q[hd][32 tig + r0 | 32 tig + 16 + r0], b1 = the same for r0 + 8, column g -> head
   // hd = 4 nt + g / 2 (zero beyond G)
 #pragma unroll
   for (int e = 0; e < NT * 8; ++e) {
     if ((e & 3) != warp) continue;
-    const int nt = e >> 3, p = e & 7, r0 = (3 * p) & 7;
+    const int nt = e >> 3, p = e & 7, r0 = (BITS * p) & 7;
     const int hd = 4 * nt + (g >> 1);
     uint32_t w0 = 0u, w1 = 0u;
     if (hd < G) {
@@ -1661,7 +1716,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
       if (lane == 0) S.failed = 1;
       break;
     }
-    const SStage &sg = S.u.stage[li % kRing];
+    const Stg &sg = S.u.stage[li % kRing];
 
     // ---- K: restore, round to T, scores of tokens 16m+g and 16m+g+8 for head 4 nt + tig
     uint32_t bS[16], bM[16];  // register r's diagonal B fragments (scale, min) for this block
@@ -1683,36 +1738,44 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
       const uint32_t *kw = reinterpret_cast<const uint32_t *>(sg.kc);
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        uint32_t X0[6], X1[6];
+        // paired halves: token row t holds 4 BITS words, lane group tig's 32 channels in
+        // words BITS tig .. BITS tig + BITS - 1 ([channels 0..15 half | channels 16..31 half])
+        uint32_t X0[2 * BITS], X1[2 * BITS];
         {
-          const uint32_t *p0 = kw + 12 * (16 * m + g) + 3 * tig, *p1 = p0 + 12 * 8;
-          const uint32_t u0 = p0[0], u1 = p0[1], u2 = p0[2], v0 = p1[0], v1 = p1[1], v2 = p1[2];
-          X0[0] = u0, X0[1] = prmt(u0, u1, 0x6341u), X0[2] = u1;
-          X0[3] = prmt(u1, u2, 0x6341u), X0[4] = u2, X0[5] = prmt(u2, u2, 0x3311u);
-          X1[0] = v0, X1[1] = prmt(v0, v1, 0x6341u), X1[2] = v1;
-          X1[3] = prmt(v1, v2, 0x6341u), X1[4] = v2, X1[5] = prmt(v2, v2, 0x3311u);
+          const uint32_t *p0 = kw + 4 * BITS * (16 * m + g) + BITS * tig, *p1 = p0 + 4 * BITS * 8;
+          uint32_t u[BITS], v[BITS];
+#pragma unroll
+          for (int i = 0; i < BITS; ++i) u[i] = p0[i], v[i] = p1[i];
+          windows<BITS>(u, X0);
+          windows<BITS>(v, X1);
         }
-        // alpha * 2^-p of tokens 16m+g (mg) and 16m+g+8 (mh), both halves alike, p = 0 first
-        float2 mg = make_float2(sg.ka[16 * m + g], 0.f), mh = make_float2(sg.ka[16 * m + g + 8], 0.f);
-        mg.y = mg.x, mh.y = mh.x;
+        // alpha * 2^-q of tokens 16m+g (mgq) and 16m+g+8 (mhq), both halves alike, for the
+        // k-step's operand bit q (0 at p = 0), carried along the k-steps as one value each
+        float2 mgq = make_float2(sg.ka[16 * m + g], 0.f), mhq = make_float2(sg.ka[16 * m + g + 8], 0.f);
+        mgq.y = mgq.x, mhq.y = mhq.x;
         float sc[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-          const uint32_t pw = 0x3C003C00u + static_cast<uint32_t>(p) * 0x04000400u;  // fp16 2^p in both halves
+          const int r0 = (BITS * p) & 7;  // registers r0 and r0 + 8: window bit p, operand bit cpos(r0)
+          const int q = cpos<BITS>(r0);
+          const uint32_t pw = 0x3C003C00u + static_cast<uint32_t>(q) * 0x04000400u;  // fp16 2^q in both halves
+          if (p > 0) {
+            const float f = pow2f(cpos<BITS>((BITS * (p - 1)) & 7) - q);  // 0.5 except where INT5 shifts
+            mgq = __fmul2_rn(mgq, make_float2(f, f));
+            mhq = __fmul2_rn(mhq, make_float2(f, f));
+          }
           uint32_t klo[2], khi[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int r = ((3 * p) & 7) + 8 * e;
-            constexpr uint32_t seven = 0x00070007u;
-            const uint32_t msk = seven << p;  // vpos(r) == p
-            const uint32_t a0 = hsub2u((X0[vwin(r)] & msk) | kMagic2, kMagic2);
-            const uint32_t a1 = hsub2u((X1[vwin(r)] & msk) | kMagic2, kMagic2);
+            const int r = r0 + 8 * e;
+            const uint32_t a0 = hsub2u(code2<BITS>(X0[cwin<BITS>(r)], r) | kMagic2, kMagic2);
+            const uint32_t a1 = hsub2u(code2<BITS>(X1[cwin<BITS>(r)], r) | kMagic2, kMagic2);
             float d[4];
             mma16816_z(d, a0, a1, pw, pw, bS[r], bM[r]);
-            const float2 y01 = __fmul2_rn(make_float2(d[0], d[1]), mg);
-            const float2 y23 = __fmul2_rn(make_float2(d[2], d[3]), mh);
+            const float2 y01 = __fmul2_rn(make_float2(d[0], d[1]), mgq);
+            const float2 y23 = __fmul2_rn(make_float2(d[2], d[3]), mhq);
             klo[e] = round2<T>(y01.x, y01.y);
             khi[e] = round2<T>(y23.x, y23.y);
           }
@@ -1720,8 +1783,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
           for (int nt = 0; nt < NT; ++nt) {
             mma16816<T>(sc[nt], klo[0], khi[0], klo[1], khi[1], qreg[nt][2 * p], qreg[nt][2 * p + 1]);
           }
-          mg = __fmul2_rn(mg, make_float2(0.5f, 0.5f));
-          mh = __fmul2_rn(mh, make_float2(0.5f, 0.5f));
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -1772,25 +1833,24 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
       for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        // paired rows: word 24 j + k = [token 2j half k | token 2j+1 half k]
-        uint32_t P[2][6];
-        const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + 3 * g;
+        // paired rows: word 8 BITS j + k = [token 2j half k | token 2j+1 half k]; lane g's
+        // 16 channels are halves BITS g .. BITS g + BITS - 1 of a row
+        uint32_t P[2][2 * BITS];
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(sg.vc) + BITS * g;
 #pragma unroll
         for (int pr = 0; pr < 2; ++pr) {
           const int j = 8 * ks + tig + 4 * pr;
-          const uint32_t w0 = vw[24 * j], w1 = vw[24 * j + 1], w2 = vw[24 * j + 2];
-          P[pr][0] = w0;
-          P[pr][1] = prmt(w0, w1, 0x6341u);
-          P[pr][2] = w1;
-          P[pr][3] = prmt(w1, w2, 0x6341u);
-          P[pr][4] = w2;
-          P[pr][5] = prmt(w2, w2, 0x3311u);
+          uint32_t w[BITS];
+#pragma unroll
+          for (int i = 0; i < BITS; ++i) w[i] = vw[8 * BITS * j + i];
+          windows<BITS>(w, P[pr]);
         }
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int i0 = 2 * mt, i1 = 2 * mt + 1;
-          mma16816<__half>(D[mt], vop(P[0][vwin(i0)], i0), vop(P[0][vwin(i1)], i1), vop(P[1][vwin(i0)], i0),
-                           vop(P[1][vwin(i1)], i1), PB[ks][0], PB[ks][1]);
+          mma16816<__half>(D[mt], vopb<BITS>(P[0][cwin<BITS>(i0)], i0), vopb<BITS>(P[0][cwin<BITS>(i1)], i1),
+                           vopb<BITS>(P[1][cwin<BITS>(i0)], i0), vopb<BITS>(P[1][cwin<BITS>(i1)], i1), PB[ks][0],
+                           PB[ks][1]);
         }
       }
       // epilogue: acc' += scale_c * D + min_c * 2^vunit(c) * sum_t p_t alpha_t
@@ -1804,8 +1864,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
         for (int q = 0; q < 4; ++q) {
           const int mt = 4 * half + q;
           const float2 bs = Elem<__half>::to_f2(sw4[q]), ms = Elem<__half>::to_f2(mw4[q]);
-          const float w0 = wsum * __int_as_float((127 + vunit(2 * mt)) << 23);
-          const float w1 = wsum * __int_as_float((127 + vunit(2 * mt + 1)) << 23);
+          const float w0 = wsum * __int_as_float((127 + cunit<BITS>(2 * mt)) << 23);
+          const float w1 = wsum * __int_as_float((127 + cunit<BITS>(2 * mt + 1)) << 23);
           acc[nt][mt][0] = fmaf(bs.x, D[mt][0] + D[mt][1], fmaf(ms.x, w0, acc[nt][mt][0]));
           acc[nt][mt][1] = fmaf(bs.y, D[mt][2] + D[mt][3], fmaf(ms.y, w1, acc[nt][mt][1]));
         }
@@ -1842,8 +1902,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 3 : 2) attn_sealed_kernel(
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         const int c = 16 * g + 2 * mt;
-        M.acc[warp][hd][c] = acc[nt][mt][0] * __int_as_float((127 - vunit(2 * mt)) << 23);
-        M.acc[warp][hd][c + 1] = acc[nt][mt][1] * __int_as_float((127 - vunit(2 * mt + 1)) << 23);
+        M.acc[warp][hd][c] = acc[nt][mt][0] * __int_as_float((127 - cunit<BITS>(2 * mt)) << 23);
+        M.acc[warp][hd][c + 1] = acc[nt][mt][1] * __int_as_float((127 - cunit<BITS>(2 * mt + 1)) << 23);
       }
     }
   }
@@ -1908,6 +1968,18 @@ static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max
   if (ch < 4) ch = 4;
   if (ch > 32) ch = 32;
   return static_cast<int>(std::max<int64_t>(ch, chunk_blocks_for(batch, h, max_blocks, max_tail)));
+}
+
+// attn_sealed_kernel for BITS, the dtype and the head-tile count, with its shared memory
+// and resident CTAs per SM.
+template <int BITS>
+static void sealed_round_kernel(int dtype, bool wide, void (*&kern)(const AttnArgs), size_t &smem, int &per_sm) {
+  per_sm = wide ? s3::kCtasPerSm<2, BITS> : s3::kCtasPerSm<1, BITS>;
+  smem = wide ? sizeof(s3::KSmem<2, BITS>) : sizeof(s3::KSmem<1, BITS>);
+  if (dtype == NSNKV_F16)
+    kern = wide ? attn_sealed_kernel<__half, 2, BITS> : attn_sealed_kernel<__half, 1, BITS>;
+  else
+    kern = wide ? attn_sealed_kernel<__nv_bfloat16, 2, BITS> : attn_sealed_kernel<__nv_bfloat16, 1, BITS>;
 }
 
 // The workspace starts with the fused merge's arrival words (one per unit), then the partials.
@@ -2061,10 +2133,11 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = NSNKV_OK;
   // Sealed blocks with renorm factors go to a tensor-core kernel: exact restore
-  // (attn_sealed3_kernel: fp16, G <= 4, either code order) or, by default, K rounded to the
-  // cache dtype as the bridge rounds it (attn_sealed_kernel: record orders, G <= 8).
+  // (attn_sealed3_kernel: INT3, fp16, G <= 4, either code order) or, by default, K rounded
+  // to the cache dtype as the bridge rounds it (attn_sealed_kernel: INT3 or INT5 in the
+  // record orders, G <= 8).
   const bool sealed_exact = k_alpha && v_alpha && exact && bits == 3 && dtype == NSNKV_F16 && G <= 4;
-  const bool sealed_round = k_alpha && v_alpha && !exact && rec_order && bits == 3 && G <= kHeads;
+  const bool sealed_round = k_alpha && v_alpha && !exact && rec_order && (bits == 3 || bits == 5) && G <= kHeads;
   const bool sealed_path = sealed_exact || sealed_round;
   if (rec_order && max_blocks > 0 && !sealed_path) return NSNKV_ERR_UNSUPPORTED;  // record orders: tensor-core kernels only
   if (exact && max_blocks > 0 && !sealed_exact) return NSNKV_ERR_UNSUPPORTED;
@@ -2079,12 +2152,10 @@ static int decode_attn_impl(int64_t batch, int hq, int h, int bits, int dtype, c
     int per_sm = 4;
     if (sealed_round) {
       const bool wide = G > 4;
-      per_sm = wide ? 2 : 3;
-      smem = wide ? sizeof(s3::KSmem<2>) : sizeof(s3::KSmem<1>);
-      if (dtype == NSNKV_F16)
-        kern = wide ? attn_sealed_kernel<__half, 2> : attn_sealed_kernel<__half, 1>;
+      if (bits == 3)
+        sealed_round_kernel<3>(dtype, wide, kern, smem, per_sm);
       else
-        kern = wide ? attn_sealed_kernel<__nv_bfloat16, 2> : attn_sealed_kernel<__nv_bfloat16, 1>;
+        sealed_round_kernel<5>(dtype, wide, kern, smem, per_sm);
     }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return NSNKV_ERR_CUDA;

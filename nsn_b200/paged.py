@@ -149,6 +149,23 @@ def block_record_pools(h: int, pages: int, bits: int, device):
     return rec, kp, vp
 
 
+def group_record_pools(k_group, v_group, bits: int):
+    """Block records (see block_record_pools) holding the blocks of reference-layout groups
+    ([1, h, n, ...], as encode_group returns them): codes in the records' orders, fp16
+    metadata, and the renorm factors computed from them.  Returns (records, k_pool, v_pool)
+    with block (j, i) at row j, page i, for nsnkv_decode_attn_alpha's tensor-core kernels."""
+    _, h, n, cb = k_group["codes"].shape
+    w.require(cb == w.code_bytes(bits) and tuple(v_group["codes"].shape) == (1, h, n, cb), "group record shapes")
+    records, kp, vp = block_record_pools(h, n, bits, k_group["codes"].device)
+    for g, pool in ((k_group, kp), (v_group, vp)):
+        pool["codes"].copy_(w.to_code_order(g["codes"][0], bits, pool["code_order"]))
+        pool["norm"].copy_(g["metas"][0].reshape(h, n, w.BLOCK))
+        pool["min"].copy_(g["metas"][1].reshape(h, n, w.DIM))
+        pool["scale"].copy_(g["metas"][2].reshape(h, n, w.DIM))
+        w.block_renorm(pool, bits, h, n, n)
+    return records, kp, vp
+
+
 ROUNDING_MODES = ("k", "kv", "exact")
 
 
@@ -159,9 +176,9 @@ class PagedKVCache:
 
         ``"k"`` (default): K rows rounded to the cache dtype exactly as the reference
             bridge (restore_group(g, dtype) + SDPA) rounds them, V applied as the exact fp32
-            restore.  INT3 caches with hq / h <= 8 keep per-token renorm factors in block
-            records and attend over them on the tensor cores; other shapes use the restore
-            kernel, which rounds K and V.
+            restore.  INT3 and INT5 caches with hq / h <= 8 keep per-token renorm factors in
+            block records and attend over them on the tensor cores; other shapes (INT4,
+            hq / h > 8) use the restore kernel, which rounds K and V.
         ``"kv"`` (or ``bridge_rounding=True``): the restore kernel, K and V rounded as the
             bridge rounds them.
         ``"exact"``: K and V both the exact fp32 restore, nothing rounded (INT3 fp16
@@ -441,7 +458,7 @@ class PagedKVCache:
     def uses_alpha_path(self):
         """True when attend() runs the sealed blocks on the tensor-core kernels (block
         records with per-token renorm factors)."""
-        return self.restore_rounding != "kv" and self.bits == 3 and self.hq // self.h <= 8
+        return self.restore_rounding != "kv" and self.bits in (3, 5) and self.hq // self.h <= 8
 
     def read_bytes_per_step(self):
         """Algorithmic bytes one attend() reads: sealed blocks (codes + metadata) and tails, q and out.

@@ -89,13 +89,26 @@ class ShardedSequence:
     """One rank's share of a long sequence: its block range of K/V (reference group
     layout [1, h, n_r, ...]) plus, on the last rank, the native tail."""
 
-    def __init__(self, k_group, v_group, k_tail, v_tail, h, hq, bits):
+    def __init__(self, k_group, v_group, k_tail, v_tail, h, hq, bits, records=None):
+        """records: attend over block records with per-token renorm factors on the
+        tensor-core kernel (K rounded like the bridge, V exact; INT3 or INT5 with
+        hq / h <= 8), which is the default where it applies; False keeps the groups and
+        the restore kernel (K and V rounded like the bridge)."""
         self.kg, self.vg = k_group, v_group
         self.kt, self.vt = k_tail, v_tail
         self.h, self.hq, self.bits = h, hq, bits
         self.n = 0 if k_group is None else k_group["codes"].shape[2]
         self.t = 0 if k_tail is None else k_tail.shape[2]
         dev = (k_group["codes"] if k_group is not None else k_tail).device
+        if records is None:
+            records = bits in (3, 5) and hq // h <= 8
+        self.kp = self.vp = None
+        if self.n:
+            if records:
+                from .paged import group_record_pools
+                self.records, self.kp, self.vp = group_record_pools(k_group, v_group, bits)
+            else:
+                self.kp, self.vp = group_pool(k_group, h), group_pool(v_group, h)
         # send record: o [hq, 128] then lse [hq], written in place by the attention kernel
         self.rec = torch.empty((hq * 129,), dtype=torch.float32, device=dev)
         self.o = self.rec[:hq * 128].view(hq, 128)
@@ -110,8 +123,7 @@ class ShardedSequence:
         if out is None:
             out = self.lout if self.lout.dtype == q.dtype else torch.empty((1, self.hq, 128), dtype=q.dtype,
                                                                            device=q.device)
-        decode_attention(q.reshape(1, self.hq, 128), group_pool(self.kg, self.h) if self.n else None,
-                         group_pool(self.vg, self.h) if self.n else None, h=self.h, bits=self.bits,
+        decode_attention(q.reshape(1, self.hq, 128), self.kp, self.vp, h=self.h, bits=self.bits,
                          blk_stride_head=self.n, blk_stride_page=1, n_blocks=self.n, max_blocks=self.n,
                          k_tail=self.kt if self.t else None, v_tail=self.vt if self.t else None,
                          tail_stride_seq=self.h * self.t, tail_stride_head=self.t, tail_len=self.t, max_tail=self.t,

@@ -42,13 +42,13 @@ class Restored:
     rounded to dtype like restore_group; "exact": the fp32 restore before the cast) and
     the rest of the T tokens native."""
 
-    def __init__(self, src, nb_max, dtype):
+    def __init__(self, src, nb_max, dtype, bits=3):
         self.src, self.dtype = src, dtype
         h = src.shape[0]
         self.y = {}
         if nb_max:
             x = src[None, :, :nb_max * 64].astype(np.float32).reshape(1, h, nb_max, 64, 128)
-            q8, n, m, s, st = O.nsn_encode(x, 3)
+            q8, n, m, s, st = O.nsn_encode(x, bits)
             assert st == 0
             self.y["bridge"] = np.asarray(O.nsn_decode(q8, n, m, s, dtype), np.float32).reshape(h, nb_max * 64, 128)
             self.y["exact"] = np.asarray(O.nsn_decode(q8, n, m, s, np.float32), np.float32).reshape(h, nb_max * 64, 128)
@@ -59,8 +59,8 @@ class Restored:
         return np.concatenate(parts, 1).astype(np.float64)
 
 
-def rows(src, nb, dtype, kind):
-    return Restored(src, nb, dtype).rows(src.shape[1], nb, kind)
+def rows(src, nb, dtype, kind, bits=3):
+    return Restored(src, nb, dtype, bits).rows(src.shape[1], nb, kind)
 
 
 def attention64(q, k, v):
@@ -95,9 +95,9 @@ def fill(cache, b, k, v, tail64=False):
     return None, None
 
 
-def new_cache(batch, h, hq, max_blocks, dtype, mode="k"):
+def new_cache(batch, h, hq, max_blocks, dtype, mode="k", bits=3):
     from nsn_b200.paged import PagedKVCache
-    return PagedKVCache(batch, h, max_blocks=max_blocks, bits=3, dtype=dtype, hq=hq, restore_rounding=mode)
+    return PagedKVCache(batch, h, max_blocks=max_blocks, bits=bits, dtype=dtype, hq=hq, restore_rounding=mode)
 
 
 def exact_k_bar(q, k, v):
@@ -172,6 +172,111 @@ def test_default_path_matches_bridge(h, hq, dtype, q_scale):
         vx = rows(hv[b], nb, dtype, "exact")
         ok, err = O.within_tolerance(got32[b], attention64(q64, kb, vx), KROUND[0], KROUND[1] + vexact_bar(q64, kb, vx))
         assert ok, ("k rounded, v exact", b, L, err)
+
+
+@pytest.mark.parametrize("h,hq,dtype", [(8, 64, "float16"), (2, 16, "float16"), (2, 12, "bfloat16"),
+                                        (2, 8, "float16"), (1, 1, "bfloat16")])
+@pytest.mark.parametrize("q_scale", [1.0, float(np.sqrt(128))])
+def test_int5_default_path_matches_bridge(h, hq, dtype, q_scale):
+    """INT5 caches on the tensor-core kernel: the same contract and the same data as the INT3
+    cases above (K rounded like the bridge, V exact), through the INT5 code windows (codes at
+    window bits 6 and 7 shifted down).  The fp16 and fp32 cfg4 data (8 outlier channels,
+    V sigma 1) is covered by the step and full-size tests below."""
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(hq * 37 + h + (5 if dtype == "bfloat16" else 0) + int(q_scale))
+    lens = [64, 1, 130, 64 * 9 + 17, 64 * 21, 64 * 5 + 63]
+    cache = new_cache(len(lens), h, hq, 22, DT[dtype], bits=5)
+    assert cache.uses_alpha_path()
+    hk, hv = [], []
+    for b, L in enumerate(lens):
+        k = workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5).astype(np.float32)
+        v = workloads.np_kv(rng, (h, L, 128), (), 0.5).astype(np.float32)
+        if dtype == "bfloat16":
+            k, v = O.cast(k, "bfloat16"), O.cast(v, "bfloat16")
+        hk.append(k)
+        hv.append(v)
+        fill(cache, b, k, v)
+    q = (rng.standard_normal((len(lens), hq, 128)) * q_scale / np.sqrt(128)).astype(np.float32)
+    q = O.cast(q, dtype).astype(np.float32)
+    out32 = torch.empty((len(lens), hq, 128), dtype=torch.float32, device="cuda")
+    out = cache.attend(torch.from_numpy(q).cuda().to(DT[dtype]), out_f32=out32)
+    cache.check()
+    got, got32 = out.float().cpu().numpy(), out32.cpu().numpy()
+    for b, L in enumerate(lens):
+        nb = L // 64
+        q64 = q[b].astype(np.float64)
+        kb, vb = rows(hk[b], nb, dtype, "bridge", 5), rows(hv[b], nb, dtype, "bridge", 5)
+        ok, err = O.within_tolerance(got[b], attention64(q64, kb, vb), *O.TOLERANCE[dtype])
+        assert ok, ("bridge", b, L, err)
+        vx = rows(hv[b], nb, dtype, "exact", 5)
+        ok, err = O.within_tolerance(got32[b], attention64(q64, kb, vx), KROUND[0], KROUND[1] + vexact_bar(q64, kb, vx))
+        assert ok, ("k rounded, v exact", b, L, err)
+
+
+def test_int5_cache_steps_and_seals():
+    """An INT5 paged cache stepped through nsnkv_paged_step: the seal writes INT5 records,
+    and every output matches the bridge over the sequence so far."""
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(29)
+    h, hq, lens, steps = 2, 16, [100, 63, 64 * 3], 70
+    cache = new_cache(len(lens), h, hq, 6, torch.float16, bits=5)
+    hk = [workloads.np_kv(rng, (h, L + steps, 128), workloads.K_OUTLIERS_8, 0.5).astype(np.float32) for L in lens]
+    hv = [workloads.np_kv(rng, (h, L + steps, 128), (), 1.0).astype(np.float32) for L in lens]
+    for b, L in enumerate(lens):
+        fill(cache, b, hk[b][:, :L], hv[b][:, :L])
+    for s in range(steps):
+        q = (rng.standard_normal((len(lens), hq, 128)) / np.sqrt(128)).astype(np.float16)
+        kn = torch.from_numpy(np.stack([hk[b][:, lens[b] + s] for b in range(len(lens))])).cuda().half()
+        vn = torch.from_numpy(np.stack([hv[b][:, lens[b] + s] for b in range(len(lens))])).cuda().half()
+        out = cache.step(torch.from_numpy(q).cuda(), kn, vn).float().cpu().numpy()
+        if s in (0, 1, 36, 69):
+            for b, L in enumerate(lens):
+                T = L + s + 1
+                nb = (T - 1) // 64
+                src_k, src_v = hk[b][:, :T], hv[b][:, :T]
+                kb, vb = rows(src_k, nb, "float16", "bridge", 5), rows(src_v, nb, "float16", "bridge", 5)
+                ok, err = O.within_tolerance(out[b], attention64(q[b].astype(np.float64), kb, vb),
+                                             *O.TOLERANCE["float16"])
+                assert ok, (s, b, err)
+    cache.check()
+    assert cache.n_blocks.cpu().tolist() == [(L + steps) // 64 for L in lens]
+
+
+def test_cfg4_full_size_split_kv():
+    """cfg4 at full size (2047 INT5 blocks + 64 tail tokens, GQA 64:8) through the split-KV
+    path on block records: two shards on one GPU, their (o, lse) records merged, against the
+    bridge over the whole sequence."""
+    from nsn_b200 import codec, workloads
+    from nsn_b200.splitkv import ShardedSequence, merge_records, shard_range
+    c = workloads.CONFIGS[4]
+    h, hq, nb, t = c["h"], c["hq"], c["blocks"], 64
+    gen = torch.Generator(device="cuda").manual_seed(41)
+    T = nb * 64 + t
+    k = workloads.torch_kv(gen, (1, h, T, 128), c["k_outliers"], 0.5)
+    v = workloads.torch_kv(gen, (1, h, T, 128), (), c["v_sigma"])
+    q = (torch.randn((1, hq, 1, 128), generator=gen, device="cuda") / np.sqrt(128)).half()
+    g = codec.encode_group(k[:, :, :nb * 64].reshape(1, h, nb, 64, 128), 0, bits=5)
+    vg = codec.encode_group(v[:, :, :nb * 64].reshape(1, h, nb, 64, 128), 0, bits=5)
+    kt, vt = k[:, :, nb * 64:].contiguous(), v[:, :, nb * 64:].contiguous()
+    world, recs = 2, []
+    for r in range(world):
+        s, e = shard_range(nb, world, r)
+        sub = lambda gr: dict(codes=gr["codes"][:, :, s:e].contiguous(),
+                              metas=tuple(m[:, :, s:e].contiguous() for m in gr["metas"]))
+        last = r == world - 1
+        sh = ShardedSequence(sub(g), sub(vg), kt if last else None, vt if last else None, h, hq, 5)
+        assert sh.kp is not None and "alpha" in sh.kp  # the tensor-core path
+        o, lse = sh.local(q)
+        sh.check()
+        recs.append(torch.cat([o.reshape(-1), lse.reshape(-1)]))
+    out, status = merge_records(torch.cat(recs), world, hq, dtype=torch.float16)
+    assert int(status.item()) == 0
+    got = out.float().cpu().numpy().reshape(hq, 128)
+    q64 = q.float().cpu().numpy().reshape(hq, 128).astype(np.float64)
+    kk, vv = k[0].float().cpu().numpy(), v[0].float().cpu().numpy()
+    kb, vb = rows(kk, nb, "float16", "bridge", 5), rows(vv, nb, "float16", "bridge", 5)
+    ok, err = O.within_tolerance(got, attention64(q64, kb, vb), *O.TOLERANCE["float16"])
+    assert ok, err
 
 
 def test_default_path_q_magnitudes():
