@@ -277,7 +277,9 @@ int nsnkv_decode_attn_noalloc(int64_t batch, int hq, int h, int bits, int dtype,
  * unchanged.  Replaces the per-slot compress_to/post_decode seal
  * (experiments/nb06/source/loop_kv_nb06_packed.py:36-56) with the
  * seal-at-64 policy.  pending_append = 1 counts the token appended by the
- * preceding nsnkv_decode_attn (k_new != NULL) into the tail length.
+ * preceding nsnkv_decode_attn (k_new != NULL) into the tail length.  A sequence
+ * whose table row has no page left (n_blocks[b] == table_stride) keeps its full
+ * tail and sets NSNKV_ST_CAPACITY; the next append to it is refused the same way.
  */
 int nsnkv_seal_full_tails(int64_t batch, int h, int bits, int dtype,
                           void *k_tail, void *v_tail, int64_t tail_stride_seq, int64_t tail_stride_head,

@@ -607,7 +607,11 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
   const int h = blockIdx.x, kv = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int32_t tl = tail_len[b], nbk = n_blocks[b];
-  const bool full = tl + pending >= kBlock;
+  // a full tail seals into page n_blocks[b] of the sequence's table row; with no page
+  // left in the row it stays a full tail and the status says so (the next append is refused)
+  const bool room = nbk < table_stride;
+  const bool full = tl + pending >= kBlock && room;
+  if (tl + pending >= kBlock && !room && h == 0 && kv == 0 && threadIdx.x == 0) set_status(status, NSNKV_ST_CAPACITY);
   if (!full && !done) return;
   if (full) {
     const int32_t page = table[b * table_stride + nbk];
@@ -646,11 +650,12 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
   }
 }
 
-__global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_blocks, int pending) {
+__global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_blocks, int pending,
+                                   int64_t table_stride) {
   for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < batch;
        b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int32_t t = tail_len[b] + pending;
-    if (t >= kBlock) {
+    if (t >= kBlock && n_blocks[b] < table_stride) {  // (seal_kernel left a tail without a page full)
       n_blocks[b] += 1;
       t -= kBlock;
     }
@@ -825,7 +830,8 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
   }
 #undef NSNKV_SEAL
   if (!done)
-    seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending);
+    seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending,
+                                                                                   ts);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 
@@ -931,7 +937,8 @@ static int seal_impl(int64_t batch, int h, int bits, int dtype, void *k_tail, vo
   if (blk_bytes != 0 && (blk_bytes < code_bytes(bits) || blk_bytes % 16 != 0)) return NSNKV_ERR_ARG;
   const int64_t cs = blk_bytes ? blk_bytes : code_bytes(bits), ms = blk_bytes ? blk_bytes : kDim * 2;
   if (batch == 0) return NSNKV_OK;
-  if (!k_tail || !v_tail || !tail_len || !n_blocks || !block_table || !k_codes || !v_codes || !status)
+  if (!k_tail || !v_tail || !tail_len || !n_blocks || !block_table || table_stride <= 0 || !k_codes || !v_codes ||
+      !status)
     return NSNKV_ERR_ARG;
   if (!aligned16(k_tail) || !aligned16(v_tail) || !aligned16(k_codes) || !aligned16(v_codes)) return NSNKV_ERR_ARG;
   if ((k_alpha == nullptr) != (v_alpha == nullptr)) return NSNKV_ERR_ARG;

@@ -1,0 +1,164 @@
+"""Batched decode of a looped decoder over paged packed-KV caches (the cfg3 shape).
+
+The reference drives its looped model one sequence at a time through a connection cache
+per (loop, layer) slot (experiments/ac08/source/loop_kv_ac08_attention.py:46-96,
+experiments/nb06/source/loop_kv_nb06_attention.py:33-88): per token, loops x layers
+attention calls, each with host-side cache updates and a ``torch.cat`` of the slot's
+tails.  Here a batch of sequences steps together:
+
+* one ``PagedKVCache`` per (loop, layer) slot holds every sequence of the batch
+  (seal-at-64, block records on the tensor-core kernel);
+* a decode step is the model's projections and MLP on [batch, hidden] rows (cuBLAS
+  GEMMs) plus one ``nsnkv_paged_step`` per slot (append + attention + seal);
+* nothing in a step reads the device or allocates, so the whole step is captured once
+  as a CUDA graph (``capture``) and replayed per token (``replay``);
+* prefill runs causal SDPA (its FlashAttention kernels) over the fp16 prompt and encodes
+  each slot's keys and values into its cache.
+
+Keys are cached after RoPE, as the model's own cache update receives them.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .paged import PagedKVCache
+
+
+class PagedLoopedDecoder:
+    """Decode driver for an ``adapter.LoopedDecoder`` (its weights and layer modules).
+
+    ``batch`` sequences, up to ``max_tokens`` tokens each (prompt + decoded), one paged
+    cache per (loop, layer) slot with ``restore_rounding`` as in ``PagedKVCache``.
+    """
+
+    def __init__(self, model, batch: int, max_tokens: int, restore_rounding: str = "k"):
+        from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+        self.model, self.batch = model, batch
+        cfg = model.config
+        self.h, self.hq = cfg.num_key_value_heads, cfg.num_attention_heads
+        self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        if self.head_dim != 128:
+            raise ValueError("PagedLoopedDecoder: the packed cache stores head_dim 128")
+        self.rope = apply_rotary_pos_emb
+        self.device = model.embed.weight.device
+        self.dtype = model.embed.weight.dtype
+        self.max_blocks = -(-max_tokens // 64) + 1  # a spare page: a full tail always finds one
+        n_slots = model.loops * len(model.layers)
+        self.caches = [PagedKVCache(batch, self.h, self.max_blocks, bits=3, dtype=self.dtype, device=self.device,
+                                    hq=self.hq, restore_rounding=restore_rounding) for _ in range(n_slots)]
+        self.length = 0  # tokens per sequence held by the caches
+        self.graph = None
+        self._ids = torch.zeros(batch, dtype=torch.long, device=self.device)
+        self._pos = torch.zeros((1, 1), dtype=torch.long, device=self.device)
+        self._logits = None
+
+    # ------------------------------------------------------------ one layer
+    def _layer(self, layer, h, cos, sin, cache):
+        attn = layer.self_attn
+        B, T, _ = h.shape
+        x = layer.input_layernorm(h)
+        q = attn.q_proj(x).view(B, T, self.hq, self.head_dim).transpose(1, 2)
+        k = attn.k_proj(x).view(B, T, self.h, self.head_dim).transpose(1, 2)
+        v = attn.v_proj(x).view(B, T, self.h, self.head_dim).transpose(1, 2)
+        q, k = self.rope(q, k, cos, sin)
+        if T == 1:
+            o = cache.step(q[:, :, 0].contiguous(), k[:, :, 0].contiguous(), v[:, :, 0].contiguous())
+            o = o.reshape(B, 1, self.hq * self.head_dim)
+        else:
+            rep = self.hq // self.h
+            kr = k.repeat_interleave(rep, dim=1) if rep > 1 else k
+            vr = v.repeat_interleave(rep, dim=1) if rep > 1 else v
+            o = F.scaled_dot_product_attention(q, kr, vr, is_causal=True)
+            o = o.transpose(1, 2).reshape(B, T, self.hq * self.head_dim)
+            for b in range(B):
+                cache.prefill(b, k[b], v[b])
+        h = h + attn.o_proj(o)
+        return h + layer.mlp(layer.post_attention_layernorm(h))
+
+    def _forward(self, ids, pos):
+        m = self.model
+        h = m.embed(ids)
+        cos, sin = m.rotary(h, pos)
+        slot = 0
+        for _ in range(m.loops):
+            for layer in m.layers:
+                h = self._layer(layer, h, cos, sin, self.caches[slot])
+                slot += 1
+        return m.lm_head(m.norm(h[:, -1]))
+
+    # ------------------------------------------------------------ public API
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Prompt ids [batch, P] (every sequence the same length) -> last-token logits [batch, vocab]."""
+        if ids.shape[0] != self.batch or self.length:
+            raise ValueError("PagedLoopedDecoder.prefill: one prompt per sequence, into empty caches")
+        P = ids.shape[1]
+        if P + 1 > 64 * (self.max_blocks - 1):
+            raise ValueError("PagedLoopedDecoder.prefill: the prompt exceeds max_tokens")
+        pos = torch.arange(P, device=self.device)[None]
+        logits = self._forward(ids.to(self.device), pos)
+        self.length = P
+        return logits
+
+    @torch.no_grad()
+    def step(self, ids: torch.Tensor) -> torch.Tensor:
+        """One token per sequence, ids [batch] -> logits [batch, vocab] (eager launches)."""
+        if self.length + 1 > 64 * (self.max_blocks - 1):
+            raise ValueError("PagedLoopedDecoder.step: max_tokens reached")
+        self._pos.fill_(self.length)
+        logits = self._forward(ids.to(self.device).reshape(self.batch, 1), self._pos)
+        self.length += 1
+        return logits
+
+    @torch.no_grad()
+    def capture(self):
+        """Record the next decode step as a CUDA graph over static id / position buffers.
+
+        Capturing launches nothing; the caches' host counters (which size the attention
+        grid) advance once during the capture and are re-read from the device by
+        ``sync_counters``, which ``replay`` callers run when they stop replaying."""
+        if self.length + 1 > 64 * (self.max_blocks - 1):
+            raise ValueError("PagedLoopedDecoder.capture: max_tokens reached")
+        self._pos.fill_(self.length)
+        torch.cuda.synchronize(self.device)
+        snap = [(c.host_blocks.copy(), c.host_tail.copy()) for c in self.caches]
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._logits = self._forward(self._ids.reshape(self.batch, 1), self._pos)
+        for c, (nb, tl) in zip(self.caches, snap):  # nothing ran: the counters are where they were
+            c.host_blocks[:] = nb
+            c.host_tail[:] = tl
+
+    @torch.no_grad()
+    def replay(self, ids: torch.Tensor) -> torch.Tensor:
+        """One decode step through the captured graph: ids [batch] -> logits [batch, vocab]
+        (a view of the graph's output buffer, overwritten by the next replay)."""
+        if self.graph is None:
+            raise RuntimeError("PagedLoopedDecoder.replay: capture() first")
+        if self.length + 1 > 64 * (self.max_blocks - 1):
+            raise ValueError("PagedLoopedDecoder.replay: max_tokens reached")
+        self._ids.copy_(ids.reshape(self.batch), non_blocking=True)
+        self._pos.fill_(self.length)
+        self.graph.replay()
+        self.length += 1
+        return self._logits
+
+    def sync_counters(self):
+        """Re-read every cache's n_blocks / tail_len from the device into its host copies."""
+        for c in self.caches:
+            c.host_blocks[:] = c.n_blocks.cpu().numpy()
+            c.host_tail[:] = c.tail_len.cpu().numpy()
+
+    def check(self):
+        for c in self.caches:
+            c.check()
+
+    def kv_bytes(self):
+        """Bytes the caches hold for the sequences' tokens (reference format + renorm factors)."""
+        return sum(c.kv_bytes() for c in self.caches)
+
+    def release(self):
+        """Drop the captured graph (before the caches it references)."""
+        self.graph = None
+        self._logits = None

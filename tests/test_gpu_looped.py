@@ -1,0 +1,116 @@
+"""GPU checks of the batched looped-decoder driver (nsn_b200.looped.PagedLoopedDecoder).
+
+The driver is the model's own projections, norms and MLP around one PagedKVCache per
+(loop, layer) slot.  Its attention is checked against the reference bridge end to end:
+a second driver runs the same model and caches, but takes each decode step's attention
+from the bridge arithmetic (restore_group of the slot's exported groups in the cache
+dtype, then SDPA in fp32 over the restored rows, the native tail and the new token;
+experiments/nb06/source/loop_kv_nb06_kernel.py:156-174) while the caches advance through
+the same nsnkv_paged_step.  The two drivers' logits agree to the attention parity bar
+carried through the layers.  A CUDA-graph replay of the decode step gives the eager
+step's logits.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def small_model(loops=2, layers=2, hidden=256, heads=2, kv_heads=2):
+    from transformers import LlamaConfig
+    from nsn_b200 import adapter
+    cfg = LlamaConfig(vocab_size=512, hidden_size=hidden, intermediate_size=512, num_hidden_layers=layers,
+                      num_attention_heads=heads, num_key_value_heads=kv_heads, head_dim=128,
+                      max_position_embeddings=1024, rope_theta=10000.0, attn_implementation="sdpa")
+    torch.manual_seed(7)
+    return adapter.LoopedDecoder(cfg, loops=loops).cuda().half().eval()
+
+
+def bridge_driver_class():
+    from nsn_b200 import codec
+    from nsn_b200.looped import PagedLoopedDecoder
+
+    class BridgeDriver(PagedLoopedDecoder):
+        """Decode attention from the bridge over each slot's cache; the cache still steps."""
+
+        def _layer(self, layer, h, cos, sin, cache):
+            if h.shape[1] != 1:
+                return super()._layer(layer, h, cos, sin, cache)
+            attn = layer.self_attn
+            B = h.shape[0]
+            x = layer.input_layernorm(h)
+            q = attn.q_proj(x).view(B, 1, self.hq, 128).transpose(1, 2)
+            k = attn.k_proj(x).view(B, 1, self.h, 128).transpose(1, 2)
+            v = attn.v_proj(x).view(B, 1, self.h, 128).transpose(1, 2)
+            q, k = self.rope(q, k, cos, sin)
+            outs = []
+            for b in range(B):
+                kg, kt, vg, vt = cache.export_groups(b)
+                ks = [codec.restore_group(kg, self.dtype)[0]] if kg is not None else []
+                vs = [codec.restore_group(vg, self.dtype)[0]] if vg is not None else []
+                kk = torch.cat(ks + [kt[0], k[b]], 1).float()  # [h, T, 128]
+                vv = torch.cat(vs + [vt[0], v[b]], 1).float()
+                rep = self.hq // self.h
+                kk, vv = kk.repeat_interleave(rep, 0), vv.repeat_interleave(rep, 0)
+                s = torch.einsum("jd,jtd->jt", q[b, :, 0].float(), kk) / np.sqrt(128.0)
+                outs.append(torch.einsum("jt,jtd->jd", torch.softmax(s, -1), vv).to(self.dtype))
+            cache.step(q[:, :, 0].contiguous(), k[:, :, 0].contiguous(), v[:, :, 0].contiguous())
+            o = torch.stack(outs).reshape(B, 1, self.hq * 128)
+            h = h + attn.o_proj(o)
+            return h + layer.mlp(layer.post_attention_layernorm(h))
+
+    return BridgeDriver
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(2, 2), (4, 2)])
+def test_driver_matches_bridge_driver(heads, kv_heads):
+    from nsn_b200.looped import PagedLoopedDecoder
+    model = small_model(heads=heads, kv_heads=kv_heads)
+    B, P, steps = 3, 100, 70
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    ids = torch.randint(0, 512, (B, P + steps), generator=gen).cuda()
+    kern = PagedLoopedDecoder(model, B, P + steps)
+    ref = bridge_driver_class()(model, B, P + steps)
+    la, lb = kern.prefill(ids[:, :P]), ref.prefill(ids[:, :P])
+    assert torch.equal(la, lb)  # the same prefill path
+    worst = 0.0
+    for t in range(steps):
+        la = kern.step(ids[:, P + t]).float()
+        lb = ref.step(ids[:, P + t]).float()
+        err = (la - lb).abs().max().item() / max(lb.abs().max().item(), 1e-6)
+        worst = max(worst, err)
+    kern.check()
+    ref.check()
+    # both sets of caches sealed the same blocks
+    assert kern.caches[0].n_blocks.cpu().tolist() == [(P + steps) // 64] * B
+    assert worst < 2e-2, worst
+
+
+def test_graph_replay_matches_eager_steps():
+    from nsn_b200.looped import PagedLoopedDecoder
+    model = small_model()
+    B, P, steps = 2, 120, 40
+    gen = torch.Generator(device="cpu").manual_seed(12)
+    ids = torch.randint(0, 512, (B, P + steps), generator=gen).cuda()
+    eager = PagedLoopedDecoder(model, B, P + steps)
+    graph = PagedLoopedDecoder(model, B, P + steps)
+    eager.prefill(ids[:, :P])
+    graph.prefill(ids[:, :P])
+    for t in range(3):  # eager warm-up steps on both, then the capture
+        eager.step(ids[:, P + t])
+        graph.step(ids[:, P + t])
+    graph.capture()
+    for t in range(3, steps):
+        a = eager.step(ids[:, P + t]).float()
+        b = graph.replay(ids[:, P + t]).float()
+        err = (a - b).abs().max().item() / max(a.abs().max().item(), 1e-6)
+        assert err < 1e-3, (t, err)
+    torch.cuda.synchronize()
+    graph.sync_counters()
+    for ce, cg in zip(eager.caches, graph.caches):
+        assert torch.equal(ce.n_blocks, cg.n_blocks) and torch.equal(ce.tail_len, cg.tail_len)
+        assert list(ce.host_blocks) == list(cg.host_blocks) and list(ce.host_tail) == list(cg.host_tail)
+    graph.release()
+    eager.check()
+    graph.check()
