@@ -642,8 +642,10 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
       __threadfence();
       const int per_seq = static_cast<int>(gridDim.x * gridDim.y);
       if (atomicAdd(&done[b], 1) == per_seq - 1) {
+        // a full tail without a page keeps its rows: an append to it was not stored
+        const int64_t t = tl + pending;
         n_blocks[b] = nbk + (full ? 1 : 0);
-        tail_len[b] = tl + pending - (full ? kBlock : 0);
+        tail_len[b] = static_cast<int32_t>(full ? t - kBlock : (t < tsh ? t : tsh));
         done[b] = 0;
       }
     }
@@ -651,10 +653,11 @@ __global__ void __launch_bounds__(256) seal_kernel(const T *k_tail, const T *v_t
 }
 
 __global__ void seal_update_kernel(int64_t batch, int32_t *tail_len, int32_t *n_blocks, int pending,
-                                   int64_t table_stride) {
+                                   int64_t table_stride, int64_t tail_rows) {
   for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < batch;
        b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int32_t t = tail_len[b] + pending;
+    if (t > tail_rows) t = static_cast<int32_t>(tail_rows);  // an append to a full tail was not stored
     if (t >= kBlock && n_blocks[b] < table_stride) {  // (seal_kernel left a tail without a page full)
       n_blocks[b] += 1;
       t -= kBlock;
@@ -831,7 +834,7 @@ static int launch_seal(int64_t batch, int h, int bits, void *k_tail, void *v_tai
 #undef NSNKV_SEAL
   if (!done)
     seal_update_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, st>>>(batch, tail_len, n_blocks, pending,
-                                                                                   ts);
+                                                                                   ts, tsh);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 

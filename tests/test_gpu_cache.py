@@ -251,3 +251,46 @@ def test_paged_export_import_and_bytes_round_trip():
     kg, kt, _, _ = third.export_groups(0)
     assert torch.equal(kg["codes"], g4["codes"]) and torch.equal(kg["headers"], g4["headers"])
     assert torch.equal(kt, x[:, :, 256:])
+
+
+def test_full_table_row_keeps_its_tail():
+    """With the plan's host check bypassed (attend + seal called directly, as a replayed
+    graph would), a tail that fills when its sequence has no page left stays in place: the
+    status flags NSNKV_ST_CAPACITY, the next append is attended but not stored, and the
+    other sequence's pages and counters are untouched."""
+    from nsn_b200 import primitives as w
+    from nsn_b200 import workloads
+    from nsn_b200.paged import PagedKVCache
+    rng = np.random.default_rng(23)
+    h, hq = 2, 8
+    cache = PagedKVCache(2, h, max_blocks=2, bits=3, dtype=torch.float16, hq=hq)
+    lens = [2 * 64 + 62, 64 + 6]
+    for b, L in enumerate(lens):
+        cache.prefill(b, torch.from_numpy(workloads.np_kv(rng, (h, L, 128), workloads.K_OUTLIERS_4, 0.5)).cuda(),
+                      torch.from_numpy(workloads.np_kv(rng, (h, L, 128), (), 0.5)).cuda())
+    pages1 = cache.block_table[1].long()
+    before1 = cache.records[:, pages1].clone()
+
+    def one_step():
+        q = torch.from_numpy((rng.standard_normal((2, hq, 128)) / np.sqrt(128)).astype(np.float16)).cuda()
+        kn = torch.from_numpy(workloads.np_kv(rng, (2, h, 1, 128), (), 0.5)[:, :, 0]).cuda()
+        vn = torch.from_numpy(workloads.np_kv(rng, (2, h, 1, 128), (), 0.5)[:, :, 0]).cuda()
+        out = cache.attend(q, kn, vn)
+        cache.seal(1)
+        return out
+
+    one_step()  # sequence 0: tail 62 -> 63
+    cache.check()
+    one_step()  # tail 63 -> 64 with both pages used: no seal
+    assert cache.n_blocks.cpu().tolist() == [2, 1] and cache.tail_len.cpu().tolist() == [64, 8]
+    with pytest.raises(w.IntegrityError):
+        cache.check()
+    cache.status.zero_()
+    out = one_step()  # the append to the full tail is refused, the token still attended
+    assert cache.n_blocks.cpu().tolist() == [2, 1] and cache.tail_len.cpu().tolist() == [64, 9]
+    one_step()  # and again: the full tail stays at its 64 rows
+    assert cache.n_blocks.cpu().tolist() == [2, 1] and cache.tail_len.cpu().tolist() == [64, 10]
+    with pytest.raises(w.IntegrityError):
+        cache.check()
+    assert torch.isfinite(out.float()).all()
+    assert torch.equal(cache.records[:, pages1], before1)  # sequence 1 sealed nothing, its pages unchanged
