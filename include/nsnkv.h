@@ -364,6 +364,26 @@ int nsnkv_paged_plan_last_launches(void *plan);
 int nsnkv_paged_plan_destroy(void *plan);
 
 /*
+ * Fused per-token layer ops of a decoder's decode step (nsn_b200/looped.py), in the
+ * rounding order of the transformers Llama modules the reference's model adapter drives
+ * (experiments/ac08/source/loop_kv_ac08_attention.py:46-96).  Rows are contiguous, dtype
+ * NSNKV_F16 or NSNKV_BF16.
+ *   nsnkv_add_rmsnorm  residual_out = x + residual (residual may be NULL: x itself, and
+ *                      residual_out may then be NULL), out = weight * RMSNorm(residual_out)
+ *                      with fp32 statistics (LlamaRMSNorm); dim <= 8192
+ *   nsnkv_rope_split   one fused projection row [q (hq*128) | k (h*128) | v (h*128)] ->
+ *                      RoPE'd q [rows][hq][128], k [rows][h][128] and v [rows][h][128]
+ *                      (apply_rotary_pos_emb); cos / sin [128] per row, cs_stride elements
+ *                      apart (0: one position for every row)
+ *   nsnkv_swiglu       one fused row [gate (inter) | up (inter)] -> silu(gate) * up (LlamaMLP)
+ */
+int nsnkv_add_rmsnorm(int64_t rows, int dim, int dtype, const void *x, const void *residual, const void *weight,
+                      float eps, void *residual_out, void *out, void *stream);
+int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, const void *cos, const void *sin,
+                     int64_t cs_stride, void *q, void *k, void *v, void *stream);
+int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *out, void *stream);
+
+/*
  * Combine per-shard attention partials (one row per shard) into the final
  * output: out = sum_s exp(lse_s - L) * o_s with L = log sum_s exp(lse_s).
  *   o [n_shards][rows][128] fp32, lse [n_shards][rows] fp32, out [rows][128] of dtype.

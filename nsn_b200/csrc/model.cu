@@ -1,0 +1,179 @@
+// Fused per-token layer ops of the looped decoder's decode step (nsn_b200/looped.py).
+//
+// At decode the model's rows are few (one token per sequence), so each torch elementwise op
+// is its own small launch: the RMSNorm alone is six (upcast, square, mean, rsqrt, scale,
+// weight), RoPE about eight.  These kernels do each group in one launch, in the rounding
+// order of the transformers Llama modules the reference's adapter patches
+// (experiments/ac08/source/loop_kv_ac08_attention.py:46-96 calls them):
+//   add_rmsnorm  h = x + r (rounded to the dtype); y = w * dtype(h32 * rsqrt(mean(h32^2) + eps))
+//                (LlamaRMSNorm: fp32 statistics, the normalised row cast back, then the weight)
+//   rope_split   q = dtype(q * cos) + dtype(rotate_half(q) * sin), the same for k, v copied,
+//                from one fused q|k|v projection row into the contiguous q, k, v the paged
+//                cache step takes (apply_rotary_pos_emb)
+//   swiglu       y = dtype(silu(g)) * u from one fused gate|up projection row (LlamaMLP's
+//                act_fn(gate_proj(x)) * up_proj(x), silu computed in fp32)
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "nsnkv_common.cuh"
+
+namespace nsnkv {
+namespace {
+
+template <typename T> __device__ __forceinline__ float tf(T x);
+template <> __device__ __forceinline__ float tf<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float tf<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T> __device__ __forceinline__ T ft(float x);
+template <> __device__ __forceinline__ __half ft<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 ft<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+constexpr int kNormThreads = 256;
+
+// One CTA per row.  Each thread keeps its elements in registers between the two passes.
+template <typename T, int PER>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, const T *r, const T *w, float eps,
+                                                                    int dim, T *res_out, T *y) {
+  const int64_t row = blockIdx.x;
+  const T *xr = x + row * dim;
+  const T *rr = r ? r + row * dim : nullptr;
+  float hv[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    float v = 0.f;
+    if (c < dim) {
+      T hs = xr[c];
+      if (rr) hs = ft<T>(tf<T>(hs) + tf<T>(rr[c]));  // the residual add, rounded to the dtype
+      if (res_out) res_out[row * dim + c] = hs;
+      v = tf<T>(hs);
+    }
+    hv[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float rs = rsqrtf(tot / static_cast<float>(dim) + eps);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    if (c < dim) y[row * dim + c] = ft<T>(tf<T>(w[c]) * tf<T>(ft<T>(hv[i] * rs)));
+  }
+}
+
+// One CTA of 64 threads per (row, head): thread i rotates the pair (i, i + 64) of a 128-wide head.
+template <typename T>
+__global__ void __launch_bounds__(64) rope_split_kernel(const T *qkv, const T *cs, const T *sn, int64_t cs_stride,
+                                                        int hq, int h, T *q, T *k, T *v) {
+  const int64_t row = blockIdx.y;
+  const int head = blockIdx.x;  // 0 .. hq + 2h - 1 over the fused row's q, k, v heads
+  const int i = threadIdx.x;
+  const int width = (hq + 2 * h) * kDim;
+  const T *src = qkv + row * width + static_cast<int64_t>(head) * kDim;
+  if (head >= hq + h) {  // v: a copy
+    T *dst = v + (row * h + (head - hq - h)) * kDim;
+    dst[i] = src[i];
+    dst[i + 64] = src[i + 64];
+    return;
+  }
+  T *dst = head < hq ? q + (row * hq + head) * kDim : k + (row * h + (head - hq)) * kDim;
+  const T *c = cs + row * cs_stride, *s = sn + row * cs_stride;
+  const float x0 = tf<T>(src[i]), x1 = tf<T>(src[i + 64]);
+  // rotate_half: [-x1, x0]
+  dst[i] = ft<T>(tf<T>(ft<T>(x0 * tf<T>(c[i]))) + tf<T>(ft<T>(-x1 * tf<T>(s[i]))));
+  dst[i + 64] = ft<T>(tf<T>(ft<T>(x1 * tf<T>(c[i + 64]))) + tf<T>(ft<T>(x0 * tf<T>(s[i + 64]))));
+}
+
+template <typename T>
+__global__ void swiglu_kernel(const T *gu, int64_t rows, int inter, T *y) {
+  const int64_t n = rows * inter;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = e / inter, c = e % inter;
+    const float g = tf<T>(gu[row * 2 * inter + c]);
+    const float u = tf<T>(gu[row * 2 * inter + inter + c]);
+    const float act = g / (1.f + expf(-g));
+    y[e] = ft<T>(tf<T>(ft<T>(act)) * u);
+  }
+}
+
+template <typename T>
+int add_rmsnorm_launch(int64_t rows, int dim, const void *x, const void *r, const void *w, float eps, void *res_out,
+                       void *y, cudaStream_t st) {
+  const T *xp = static_cast<const T *>(x), *rp = static_cast<const T *>(r), *wp = static_cast<const T *>(w);
+  T *ro = static_cast<T *>(res_out), *yp = static_cast<T *>(y);
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (dim <= 4 * kNormThreads)
+    add_rmsnorm_kernel<T, 4><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
+  else if (dim <= 8 * kNormThreads)
+    add_rmsnorm_kernel<T, 8><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
+  else
+    add_rmsnorm_kernel<T, 32><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+}  // namespace
+}  // namespace nsnkv
+
+using namespace nsnkv;
+
+extern "C" {
+
+int nsnkv_add_rmsnorm(int64_t rows, int dim, int dtype, const void *x, const void *residual, const void *weight,
+                      float eps, void *residual_out, void *out, void *stream) {
+  if (rows < 0 || dim <= 0 || dim > 32 * kNormThreads || !(eps >= 0.f)) return NSNKV_ERR_ARG;
+  if (dtype != NSNKV_F16 && dtype != NSNKV_BF16) return NSNKV_ERR_ARG;
+  if (rows == 0) return NSNKV_OK;
+  if (!x || !weight || !out || rows > 0x7fffffffLL) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NSNKV_F16 ? add_rmsnorm_launch<__half>(rows, dim, x, residual, weight, eps, residual_out, out, st)
+                            : add_rmsnorm_launch<__nv_bfloat16>(rows, dim, x, residual, weight, eps, residual_out,
+                                                                out, st);
+}
+
+int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, const void *cos, const void *sin,
+                     int64_t cs_stride, void *q, void *k, void *v, void *stream) {
+  if (rows < 0 || hq <= 0 || h <= 0 || cs_stride < 0) return NSNKV_ERR_ARG;
+  if (dtype != NSNKV_F16 && dtype != NSNKV_BF16) return NSNKV_ERR_ARG;
+  if (rows == 0) return NSNKV_OK;
+  if (!qkv || !cos || !sin || !q || !k || !v || rows > 65535 || hq + 2 * h > 65535) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(hq + 2 * h), static_cast<unsigned>(rows));
+  if (dtype == NSNKV_F16)
+    rope_split_kernel<__half><<<grid, 64, 0, st>>>(
+        static_cast<const __half *>(qkv), static_cast<const __half *>(cos), static_cast<const __half *>(sin), cs_stride,
+        hq, h, static_cast<__half *>(q), static_cast<__half *>(k), static_cast<__half *>(v));
+  else
+    rope_split_kernel<__nv_bfloat16><<<grid, 64, 0, st>>>(
+        static_cast<const __nv_bfloat16 *>(qkv), static_cast<const __nv_bfloat16 *>(cos),
+        static_cast<const __nv_bfloat16 *>(sin), cs_stride, hq, h, static_cast<__nv_bfloat16 *>(q),
+        static_cast<__nv_bfloat16 *>(k), static_cast<__nv_bfloat16 *>(v));
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *out, void *stream) {
+  if (rows < 0 || inter <= 0) return NSNKV_ERR_ARG;
+  if (dtype != NSNKV_F16 && dtype != NSNKV_BF16) return NSNKV_ERR_ARG;
+  if (rows == 0) return NSNKV_OK;
+  if (!gate_up || !out) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n = rows * inter;
+  const unsigned blocks = static_cast<unsigned>(n / 256 + 1 < 148 * 8 ? n / 256 + 1 : 148 * 8);
+  if (dtype == NSNKV_F16)
+    swiglu_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half *>(gate_up), rows, inter,
+                                                  static_cast<__half *>(out));
+  else
+    swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(gate_up), rows, inter,
+                                                         static_cast<__nv_bfloat16 *>(out));
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+}  // extern "C"

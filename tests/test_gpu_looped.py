@@ -34,31 +34,21 @@ def bridge_driver_class():
     class BridgeDriver(PagedLoopedDecoder):
         """Decode attention from the bridge over each slot's cache; the cache still steps."""
 
-        def _layer(self, layer, h, cos, sin, cache):
-            if h.shape[1] != 1:
-                return super()._layer(layer, h, cos, sin, cache)
-            attn = layer.self_attn
-            B = h.shape[0]
-            x = layer.input_layernorm(h)
-            q = attn.q_proj(x).view(B, 1, self.hq, 128).transpose(1, 2)
-            k = attn.k_proj(x).view(B, 1, self.h, 128).transpose(1, 2)
-            v = attn.v_proj(x).view(B, 1, self.h, 128).transpose(1, 2)
-            q, k = self.rope(q, k, cos, sin)
+        def _attend(self, cache, q, k, v):
+            B = q.shape[0]
             outs = []
             for b in range(B):
                 kg, kt, vg, vt = cache.export_groups(b)
                 ks = [codec.restore_group(kg, self.dtype)[0]] if kg is not None else []
                 vs = [codec.restore_group(vg, self.dtype)[0]] if vg is not None else []
-                kk = torch.cat(ks + [kt[0], k[b]], 1).float()  # [h, T, 128]
-                vv = torch.cat(vs + [vt[0], v[b]], 1).float()
+                kk = torch.cat(ks + [kt[0], k[b, :, None]], 1).float()  # [h, T, 128]
+                vv = torch.cat(vs + [vt[0], v[b, :, None]], 1).float()
                 rep = self.hq // self.h
                 kk, vv = kk.repeat_interleave(rep, 0), vv.repeat_interleave(rep, 0)
-                s = torch.einsum("jd,jtd->jt", q[b, :, 0].float(), kk) / np.sqrt(128.0)
+                s = torch.einsum("jd,jtd->jt", q[b].float(), kk) / np.sqrt(128.0)
                 outs.append(torch.einsum("jt,jtd->jd", torch.softmax(s, -1), vv).to(self.dtype))
-            cache.step(q[:, :, 0].contiguous(), k[:, :, 0].contiguous(), v[:, :, 0].contiguous())
-            o = torch.stack(outs).reshape(B, 1, self.hq * 128)
-            h = h + attn.o_proj(o)
-            return h + layer.mlp(layer.post_attention_layernorm(h))
+            cache.step(q, k, v)
+            return torch.stack(outs)
 
     return BridgeDriver
 
@@ -114,3 +104,43 @@ def test_graph_replay_matches_eager_steps():
     graph.release()
     eager.check()
     graph.check()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fused_layer_ops_match_the_llama_modules(dtype):
+    """nsnkv_add_rmsnorm, nsnkv_rope_split and nsnkv_swiglu against the transformers
+    modules they replace at decode: RoPE and SwiGLU bit for bit; the RMSNorm within one unit
+    of the dtype (its fp32 sum of squares runs in another order than torch's mean)."""
+    from transformers.models.llama import modeling_llama as m
+    from nsn_b200.looped import add_rmsnorm, rope_split, swiglu
+    torch.manual_seed(5)
+    rows, dim, hq, h, inter = 4, 2048, 16, 4, 5632
+    x = torch.randn(rows, dim, device="cuda").to(dtype)
+    r = torch.randn(rows, dim, device="cuda").to(dtype)
+    norm = m.LlamaRMSNorm(dim, eps=1e-5).cuda().to(dtype)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(dim, device="cuda") + 0.5)
+        res, y = add_rmsnorm(x, r, norm.weight, norm.variance_epsilon)
+        assert torch.equal(res, x + r)
+        want = norm(x + r)
+        ulp = (want.float().abs() * (2.0 ** -10 if dtype == torch.float16 else 2.0 ** -7)).clamp_min(1e-6)
+        assert ((y.float() - want.float()).abs() <= ulp).all()
+        res0, y0 = add_rmsnorm(x, None, norm.weight, norm.variance_epsilon)
+        assert res0.data_ptr() == x.data_ptr()
+        assert ((y0.float() - norm(x).float()).abs() <= (norm(x).float().abs() * 2.0 ** -7).clamp_min(1e-6)).all()
+        # RoPE at one position for every row
+        qkv = torch.randn(rows, (hq + 2 * h) * 128, device="cuda").to(dtype)
+        cfg = m.LlamaConfig(hidden_size=dim, num_attention_heads=hq, num_key_value_heads=h, head_dim=128,
+                            rope_theta=10000.0, max_position_embeddings=4096)
+        rot = m.LlamaRotaryEmbedding(cfg).cuda()
+        cos, sin = rot(qkv[:, None], torch.tensor([[777]], device="cuda"))
+        q, k, v = rope_split(qkv, cos.reshape(-1), sin.reshape(-1), hq, h)
+        q4 = qkv[:, :hq * 128].view(rows, 1, hq, 128).transpose(1, 2)
+        k4 = qkv[:, hq * 128:(hq + h) * 128].view(rows, 1, h, 128).transpose(1, 2)
+        qr, kr = m.apply_rotary_pos_emb(q4, k4, cos, sin)
+        assert torch.equal(q, qr[:, :, 0]) and torch.equal(k, kr[:, :, 0])
+        assert torch.equal(v, qkv[:, (hq + h) * 128:].view(rows, h, 128))
+        # SwiGLU
+        gu = torch.randn(rows, 2 * inter, device="cuda").to(dtype) * 3
+        want = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+        assert torch.equal(swiglu(gu), want)
