@@ -117,3 +117,21 @@ def test_paged_plan_descriptor_and_host_checks():
     assert list(nb) == [0, 4, 2] and list(tl) == [5, 63, 0]  # unchanged by a rejected step
     assert lib.nsnkv_paged_plan_destroy(handle) == _lib.OK
     assert lib.nsnkv_paged_plan_destroy(P(None)) == _lib.ERR_ARG
+
+
+def test_layer_op_argument_errors():
+    """The fused layer ops reject bad shapes, dtypes and null pointers before launching."""
+    from nsn_b200 import _lib
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    f = P(1 << 20)
+    assert lib.nsnkv_add_rmsnorm(4, 8193, _lib.F16, f, None, f, 1e-5, None, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_add_rmsnorm(4, 2048, _lib.F32, f, None, f, 1e-5, None, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_add_rmsnorm(4, 2048, _lib.F16, None, None, f, 1e-5, None, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_add_rmsnorm(4, 2048, _lib.F16, f, None, f, -1.0, None, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_add_rmsnorm(0, 2048, _lib.F16, f, None, f, 1e-5, None, f, None) == _lib.OK  # nothing to do
+    assert lib.nsnkv_rope_split(4, 0, 2, _lib.F16, f, f, f, 0, f, f, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_rope_split(4, 16, 4, _lib.F16, f, None, f, 0, f, f, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_rope_split(70000, 16, 4, _lib.F16, f, f, f, 0, f, f, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_swiglu(4, 0, _lib.F16, f, f, None) == _lib.ERR_ARG
+    assert lib.nsnkv_swiglu(4, 5632, _lib.BF16, None, f, None) == _lib.ERR_ARG
