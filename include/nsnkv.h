@@ -376,12 +376,17 @@ int nsnkv_paged_plan_destroy(void *plan);
  *                      (apply_rotary_pos_emb); cos / sin [128] per row, cs_stride elements
  *                      apart (0: one position for every row)
  *   nsnkv_swiglu       one fused row [gate (inter) | up (inter)] -> silu(gate) * up (LlamaMLP)
+ *   nsnkv_gemv_rows    the projections on those few rows: each weight row streams from HBM
+ *                      once into tensor-core MMAs
  */
 int nsnkv_add_rmsnorm(int64_t rows, int dim, int dtype, const void *x, const void *residual, const void *weight,
                       float eps, void *residual_out, void *out, void *stream);
 int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, const void *cos, const void *sin,
                      int64_t cs_stride, void *q, void *k, void *v, void *stream);
 int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *out, void *stream);
+/* y [m][n] = x [m][k] . w [n][k]^T with fp32 accumulation, for decode rows: m <= 8, n % 8 == 0,
+ * k % 256 == 0, x and w 16-byte aligned (a torch Linear without bias on a few rows). */
+int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, void *stream);
 
 /*
  * Combine per-shard attention partials (one row per shard) into the final

@@ -82,6 +82,7 @@ SIGNATURES = [
     ("nsnkv_add_rmsnorm", c_int, [c_int64, c_int, c_int, P, P, P, ctypes.c_float, P, P, P]),
     ("nsnkv_rope_split", c_int, [c_int64, c_int, c_int, c_int, P, P, P, c_int64, P, P, P, P]),
     ("nsnkv_swiglu", c_int, [c_int64, c_int, c_int, P, P, P]),
+    ("nsnkv_gemv_rows", c_int, [c_int, c_int, c_int, c_int, P, P, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),

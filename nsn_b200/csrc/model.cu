@@ -105,6 +105,61 @@ __global__ void swiglu_kernel(const T *gu, int64_t rows, int inter, T *y) {
   }
 }
 
+// Y [m][n] = X [m][k] . W [n][k]^T for the few rows of a decode step (m <= 8): the weight
+// rows stream from HBM once, 16 bytes per lane, into mma.sync with fp32 accumulation.  A
+// CTA of 8 warps owns 8 output columns (8 weight rows); warp w takes the k range
+// [w k/8, (w+1) k/8).  Lane (g, t) loads 16 contiguous bytes of weight row n0 + g at
+// k0 + 8t and the same k of X row g; the k order inside each 32-wide block is permuted
+// alike for A and B (MMA slot 2t+j of k-step 0 <- k0 + 8t + j, slot 2t+8+j <- k0 + 8t + 2 + j;
+// k-step 1 takes k0 + 8t + 4..7), which leaves the dot products unchanged.  X rows past
+// m are zero; the warps' fp32 partials meet in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256) gemv_rows_kernel(const T *x, const T *w, T *y, int m, int n, int k) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * 8;
+  const int span = k / 8;
+  const int kb0 = warp * span + 8 * t;
+  const uint4 *wp = reinterpret_cast<const uint4 *>(w + static_cast<int64_t>(n0 + g) * k + kb0);
+  const uint4 *xp = reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(g) * k + kb0);
+  const bool row = g < m;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int kUnroll = 4;
+  int it = 0;
+  const int iters = span / 32;  // 32-wide k blocks of this warp: one uint4 (8 of the block's 32 k) per lane
+  for (; it + kUnroll <= iters; it += kUnroll) {
+    uint4 wv[kUnroll], xv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      wv[u] = __ldcs(wp + 4 * (it + u));
+      xv[u] = row ? xp[4 * (it + u)] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      mma16816<T>(c, xv[u].x, 0u, xv[u].y, 0u, wv[u].x, wv[u].y);
+      mma16816<T>(c, xv[u].z, 0u, xv[u].w, 0u, wv[u].z, wv[u].w);
+    }
+  }
+  for (; it < iters; ++it) {
+    const uint4 wv = __ldcs(wp + 4 * it);
+    const uint4 xv = row ? xp[4 * it] : make_uint4(0u, 0u, 0u, 0u);
+    mma16816<T>(c, xv.x, 0u, xv.y, 0u, wv.x, wv.y);
+    mma16816<T>(c, xv.z, 0u, xv.w, 0u, wv.z, wv.w);
+  }
+  __shared__ float part[8][8][8];  // [warp][row][column]
+  part[warp][g][2 * t] = c[0];
+  part[warp][g][2 * t + 1] = c[1];
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    const int r = threadIdx.x >> 3, col = threadIdx.x & 7;
+    if (r < m) {
+      float s = 0.f;
+#pragma unroll
+      for (int wi = 0; wi < 8; ++wi) s += part[wi][r][col];
+      y[static_cast<int64_t>(r) * n + n0 + col] = ft<T>(s);
+    }
+  }
+}
+
 template <typename T>
 int add_rmsnorm_launch(int64_t rows, int dim, const void *x, const void *r, const void *w, float eps, void *res_out,
                        void *y, cudaStream_t st) {
@@ -156,6 +211,23 @@ int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, co
         static_cast<const __nv_bfloat16 *>(qkv), static_cast<const __nv_bfloat16 *>(cos),
         static_cast<const __nv_bfloat16 *>(sin), cs_stride, hq, h, static_cast<__nv_bfloat16 *>(q),
         static_cast<__nv_bfloat16 *>(k), static_cast<__nv_bfloat16 *>(v));
+  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
+int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, void *stream) {
+  if (m < 0 || m > 8 || n < 0 || k < 0 || n % 8 != 0 || k % 256 != 0) return NSNKV_ERR_ARG;
+  if (dtype != NSNKV_F16 && dtype != NSNKV_BF16) return NSNKV_ERR_ARG;
+  if (m == 0 || n == 0) return NSNKV_OK;
+  if (!x || !w || !y || !aligned16(x) || !aligned16(w) || k == 0 || n / 8 > 0x7fffffff) return NSNKV_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(n / 8);
+  if (dtype == NSNKV_F16)
+    gemv_rows_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(x), static_cast<const __half *>(w),
+                                                   static_cast<__half *>(y), m, n, k);
+  else
+    gemv_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(x),
+                                                          static_cast<const __nv_bfloat16 *>(w),
+                                                          static_cast<__nv_bfloat16 *>(y), m, n, k);
   return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
 }
 

@@ -8,9 +8,9 @@ tails.  Here a batch of sequences steps together:
 
 * one ``PagedKVCache`` per (loop, layer) slot holds every sequence of the batch
   (seal-at-64, block records on the tensor-core kernel);
-* a decode step is, per layer evaluation, four cuBLAS GEMMs on [batch, hidden] rows
-  (fused q|k|v and gate|up weights), this library's fused per-token kernels
-  (nsnkv_add_rmsnorm twice, nsnkv_rope_split, nsnkv_swiglu) and one
+* a decode step is, per layer evaluation, four projections on [batch, hidden] rows
+  (nsnkv_gemv_rows, fused q|k|v and gate|up weights), this library's fused per-token
+  kernels (nsnkv_add_rmsnorm twice, nsnkv_rope_split, nsnkv_swiglu) and one
   ``nsnkv_paged_step`` (append + attention + seal);
 * nothing in a step reads the device or allocates, so the whole step is captured once
   as a CUDA graph (``capture``) and replayed per token (``replay``);
@@ -56,6 +56,21 @@ def rope_split(qkv, cos, sin, hq, h):
                                    sin.data_ptr(), 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), _stream(qkv))
     L.check(rc, "nsnkv_rope_split")
     return q, k, v
+
+
+def linear_rows(x, weight):
+    """x [m, k] @ weight[n, k]^T for decode rows (nsnkv_gemv_rows when m <= 8, n % 8 == 0 and
+    k % 256 == 0; torch's linear otherwise)."""
+    m, k = x.shape
+    n = weight.shape[0]
+    if not (m <= 8 and n % 8 == 0 and k % 256 == 0 and x.is_contiguous() and weight.is_contiguous()
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0):
+        return F.linear(x, weight)
+    y = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    rc = L.load().nsnkv_gemv_rows(m, n, k, L.DTYPE_CODE[x.dtype], x.data_ptr(), weight.data_ptr(), y.data_ptr(),
+                                  _stream(x))
+    L.check(rc, "nsnkv_gemv_rows")
+    return y
 
 
 def swiglu(gate_up):
@@ -157,14 +172,14 @@ class PagedLoopedDecoder:
                     h, x = add_rmsnorm(h, None, ln1.weight, ln1.variance_epsilon)
                 else:
                     h, x = add_rmsnorm(pending, h, ln1.weight, ln1.variance_epsilon)
-                q, k, v = rope_split(F.linear(x, wqkv), cos, sin, self.hq, self.h)
+                q, k, v = rope_split(linear_rows(x, wqkv), cos, sin, self.hq, self.h)
                 o = self._attend(self.caches[slot], q, k, v)
-                h, x = add_rmsnorm(F.linear(o.reshape(h.shape[0], -1), a.o_proj.weight), h, ln2.weight,
+                h, x = add_rmsnorm(linear_rows(o.reshape(h.shape[0], -1), a.o_proj.weight), h, ln2.weight,
                                    ln2.variance_epsilon)
-                pending = F.linear(swiglu(F.linear(x, wgu)), mlp.down_proj.weight)
+                pending = linear_rows(swiglu(linear_rows(x, wgu)), mlp.down_proj.weight)
                 slot += 1
         _, x = add_rmsnorm(pending, h, m.norm.weight, m.norm.variance_epsilon)
-        return m.lm_head(x)
+        return linear_rows(x, m.lm_head.weight)
 
     # ------------------------------------------------------------ public API
     @torch.no_grad()

@@ -144,3 +144,17 @@ def test_fused_layer_ops_match_the_llama_modules(dtype):
         gu = torch.randn(rows, 2 * inter, device="cuda").to(dtype) * 3
         want = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
         assert torch.equal(swiglu(gu), want)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("m,n,k", [(4, 6144, 2048), (1, 2048, 5632), (8, 512, 256), (3, 32000, 2048)])
+def test_gemv_rows_matches_linear(dtype, m, n, k):
+    """nsnkv_gemv_rows against torch's linear (fp32 accumulation in both, different order)."""
+    from nsn_b200.looped import linear_rows
+    torch.manual_seed(m * 7 + k)
+    x = torch.randn(m, k, device="cuda").to(dtype)
+    w = (torch.randn(n, k, device="cuda") / np.sqrt(k)).to(dtype)
+    got = linear_rows(x, w).float()
+    want = (x.double() @ w.double().t())
+    tol = (2.0 ** -10 if dtype == torch.float16 else 2.0 ** -7) * want.abs() + 1e-3
+    assert ((got.double() - want).abs() <= tol).all(), (got.double() - want).abs().max().item()
