@@ -1945,7 +1945,21 @@ static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max
   ch = (ch + 3) / 4 * 4;
   if (ch < 4) ch = 4;
   if (ch > 32) ch = 32;
-  return static_cast<int>(std::max<int64_t>(ch, chunk_blocks_for(batch, h, max_blocks, max_tail)));
+  const int64_t floor_ch = chunk_blocks_for(batch, h, max_blocks, max_tail);
+  ch = std::max<int64_t>(ch, floor_ch);
+  if (batch == 1 && ch > 4) {
+    // One sequence: every CTA but the last of each head runs ch blocks, so the step takes
+    // about waves x (ch + 2 blocks of start-up).  Pick the multiple of 4 that minimises it
+    // (cfg4 on one GPU: 28 blocks fill exactly two waves where 32 leave the second 73% full).
+    int64_t best = ch, best_cost = INT64_MAX;
+    for (int64_t c = std::max<int64_t>(4, (floor_ch + 3) / 4 * 4); c <= 32; c += 4) {
+      const int64_t ctas = units * ((max_blocks + c - 1) / c);
+      const int64_t cost = (ctas + target - 1) / target * (c + 2);
+      if (cost < best_cost) best = c, best_cost = cost;
+    }
+    ch = best;
+  }
+  return static_cast<int>(ch);
 }
 
 // attn_sealed_kernel for BITS, the dtype and the head-tile count, with its shared memory
