@@ -126,14 +126,14 @@ def test_cfg1_full_size_fused_vs_bridge(dtype):
 
 @pytest.mark.parametrize("group", [1, 2, 4, 6, 8])
 def test_gqa_groups_and_int5(group):
-    """Every built GQA group size, INT3 and INT5, odd block counts and tails."""
+    """Every built GQA group size, INT3, INT4 and INT5, odd block counts and tails."""
     from nsn_b200 import kernel as K
     from nsn_b200 import codec as C
     from nsn_b200 import primitives as P
     rng = np.random.default_rng(100 + group)
     from nsn_b200 import workloads
     h = 2
-    for bits, nb, t in ((3, 5, 17), (5, 9, 1), (3, 1, 0), (5, 0, 40)):
+    for bits, nb, t in ((3, 5, 17), (5, 9, 1), (3, 1, 0), (5, 0, 40), (4, 7, 33)):
         total = nb * 64 + t
         k = workloads.np_kv(rng, (1, h, total, 128), workloads.K_OUTLIERS_8, 0.5).astype(np.float32)
         v = workloads.np_kv(rng, (1, h, total, 128), (), 1.0).astype(np.float32)

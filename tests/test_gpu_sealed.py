@@ -242,6 +242,36 @@ def test_int5_cache_steps_and_seals():
     assert cache.n_blocks.cpu().tolist() == [(L + steps) // 64 for L in lens]
 
 
+def test_int4_cache_steps_on_the_restore_kernel():
+    """INT4 caches (no tensor-core kernel) step through the plan on the restore kernel, K and
+    V rounded like the bridge, with the seal's counter kernel (no renorm factors)."""
+    from nsn_b200 import workloads
+    rng = np.random.default_rng(31)
+    h, hq, lens, steps = 2, 8, [70, 127], 66
+    cache = new_cache(len(lens), h, hq, 5, torch.float16, bits=4)
+    assert not cache.uses_alpha_path()
+    hk = [workloads.np_kv(rng, (h, L + steps, 128), workloads.K_OUTLIERS_4, 0.5).astype(np.float32) for L in lens]
+    hv = [workloads.np_kv(rng, (h, L + steps, 128), (), 0.5).astype(np.float32) for L in lens]
+    for b, L in enumerate(lens):
+        fill(cache, b, hk[b][:, :L], hv[b][:, :L])
+    for s in range(steps):
+        q = (rng.standard_normal((len(lens), hq, 128)) / np.sqrt(128)).astype(np.float16)
+        kn = torch.from_numpy(np.stack([hk[b][:, lens[b] + s] for b in range(len(lens))])).cuda().half()
+        vn = torch.from_numpy(np.stack([hv[b][:, lens[b] + s] for b in range(len(lens))])).cuda().half()
+        out = cache.step(torch.from_numpy(q).cuda(), kn, vn).float().cpu().numpy()
+        if s in (0, 57, 65):
+            for b, L in enumerate(lens):
+                T = L + s + 1
+                nb = (T - 1) // 64
+                kb = rows(hk[b][:, :T], nb, "float16", "bridge", 4)
+                vb = rows(hv[b][:, :T], nb, "float16", "bridge", 4)
+                ok, err = O.within_tolerance(out[b], attention64(q[b].astype(np.float64), kb, vb),
+                                             *O.TOLERANCE["float16"])
+                assert ok, (s, b, err)
+    cache.check()
+    assert cache.n_blocks.cpu().tolist() == [(L + steps) // 64 for L in lens]
+
+
 def test_cfg4_full_size_split_kv():
     """cfg4 at full size (2047 INT5 blocks + 64 tail tokens, GQA 64:8) through the split-KV
     path on block records: two shards on one GPU, their (o, lse) records merged, against the
