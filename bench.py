@@ -426,6 +426,38 @@ def cfg4_measure(args, rank, world, local, dist, with_encode=True, steps=None, w
     local_graph = torch.cuda.CUDAGraph()  # the same step's local attention alone
     with torch.cuda.graph(local_graph):
         sh.local(static_q)
+    # the exchange over peer memory fused with the merge (more than one rank)
+    peer, peer_graph, peer_note = None, None, None
+    if dist is not None and world > 1:
+        from nsn_b200.splitkv import PeerRecords
+        try:
+            peer = PeerRecords(hq)
+        except Exception as ex:  # symmetric memory unavailable: the NCCL path only
+            peer_note = f"peer exchange unavailable: {type(ex).__name__}"
+        flag = torch.tensor([0 if peer is None else 1], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)  # every rank takes the same path
+        if int(flag.item()) == 0:
+            peer = None
+        if peer is not None:
+            # used only once it reproduces the NCCL path's bits with a clean status on every rank
+            static_q.copy_(qs[0])
+            want = sh.decode(static_q).clone()
+            for i in range(warmup):
+                static_q.copy_(qs[i])
+                got = sh.decode(static_q, out=static_out, peer=peer)
+            static_q.copy_(qs[0])
+            got = sh.decode(static_q, out=static_out, peer=peer)
+            torch.cuda.synchronize(device)
+            good = torch.equal(got.view(torch.int16), want.view(torch.int16)) and int(sh.status.item()) == 0
+            flag = torch.tensor([1 if good else 0], device=device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()) == 0:
+                peer, peer_note = None, "peer exchange disagreed with the NCCL path or timed out: not used"
+                sh.status.zero_()
+        if peer is not None:
+            peer_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(peer_graph):
+                sh.decode(static_q, out=static_out, peer=peer)
     torch.cuda.synchronize(device)
 
     def timed(gr, n_steps):
@@ -445,19 +477,25 @@ def cfg4_measure(args, rank, world, local, dist, with_encode=True, steps=None, w
     if dist:
         dist.barrier()
     with ClockSampler(local) as clk:
-        step_ms = timed(graph, steps)
+        nccl_ms = timed(graph, steps)
         local_ms = timed(local_graph, steps)
+        peer_ms = timed(peer_graph, steps) if peer_graph is not None else 0.0
     sh.check()
-    del graph, local_graph  # graphs holding NCCL work are released before the process group
+    del graph, local_graph, peer_graph  # graphs holding NCCL work are released before the process group
     torch.cuda.synchronize(device)
-    t = torch.tensor([step_ms, enc_ms, local_ms], dtype=torch.float64, device=device)
+    t = torch.tensor([nccl_ms, enc_ms, local_ms, peer_ms], dtype=torch.float64, device=device)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, enc_ms_max, local_ms = t.tolist()
+    nccl_ms, enc_ms_max, local_ms, peer_ms = t.tolist()
+    step_ms = peer_ms if peer_ms > 0 else nccl_ms
+    exchange = ("peer memory (nsnkv_peer_merge_records: NVLink stores into every rank's symmetric area, fused "
+                "with the merge)" if peer_ms > 0 else "NCCL all-gather + nsnkv_merge_shard_records")
     total_bytes = 2 * 8 * (nb_total * 5760 + 64 * 256) + 2 * hq * 256
     total_enc_bytes = 2 * (nb_total * 8 * 64 * 128 * 2 + nb_total * 8 * 5760)
     hbm, peak_kind = peaks()
     return {"n_gpus": world, "step_ms": step_ms, "tokens_per_s": 1000.0 / step_ms,
+            "exchange": exchange if world > 1 else "none (one rank)",
+            "nccl_step_ms": nccl_ms if world > 1 else None, "peer_note": peer_note,
             "local_attention_ms": local_ms, "gather_merge_ms": max(step_ms - local_ms, 0.0),
             "decode_gbs_whole_job": total_bytes / (step_ms / 1000.0) / 1e9,
             "frac_per_gpu": total_bytes / (step_ms / 1000.0) / 1e9 / world / hbm, "peak": hbm, "peak_kind": peak_kind,
@@ -476,8 +514,9 @@ def run_cfg4(args, rank, world, local, dist):
                 "ms_per_step": r["step_ms"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "fp16", "data": "synthetic",
                 "config": {"workload": "cfg4-long-131k-int5: 2047 INT5 blocks + 64 tail, GQA 64:8, split-KV "
-                                       "(local fused attention + one NCCL all-gather of the (o, lse) records + "
-                                       "merge kernel, replayed as a CUDA graph)",
+                                       "(local fused attention + the (o, lse) record exchange and merge, "
+                                       "replayed as a CUDA graph)",
+                           "exchange": r["exchange"], "nccl_step_ms": r["nccl_step_ms"],
                            "global_batch": 1, "context": 131072, "parallelism": f"seq-split{world}",
                            "l2": "flushed before every timed step"},
                 "decode_gbs_whole_job": r["decode_gbs_whole_job"],
@@ -822,9 +861,10 @@ def main():
         cfg4 = cfg4_measure(args, rank, world, local, dist, with_encode=False, steps=min(args.steps, 20), warmup=3)
         cfg4["what"] = ("cfg4 split-KV decode step: one 131072-token INT5 sequence (2047 blocks + 64 tail, GQA "
                         "64:8) split by block ranges over the ranks; local fused attention (attn_sealed_kernel "
-                        "over INT5 block records, K rounded like the bridge) + one NCCL all-gather of the "
-                        "(o, lse) records + merge kernel, replayed as a CUDA graph, L2 flushed; "
-                        "gather_merge_ms = step - local attention alone (max over ranks)")
+                        "over INT5 block records, K rounded like the bridge) + the (o, lse) record exchange and "
+                        "merge named by `exchange` (nccl_step_ms: the NCCL all-gather + merge kernel instead), "
+                        "replayed as a CUDA graph, L2 flushed; gather_merge_ms = step - local attention alone "
+                        "(max over ranks)")
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:

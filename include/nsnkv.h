@@ -406,6 +406,23 @@ int nsnkv_merge_shard_records(int n_shards, int64_t rows, const float *records, 
                               void *out, float *out_f32, float *lse_out, int32_t *status, void *stream);
 
 /*
+ * The split-KV record exchange over peer memory, fused with the merge (replaces the
+ * NCCL all-gather + nsnkv_merge_shard_records pair).  Every rank owns an area of
+ * nsnkv_peer_area_words(world, hq) fp32 words that every other rank has mapped
+ * (symmetric memory): peer_areas is a device array of the world ranks' area addresses
+ * as this rank sees them, area this rank's own.  Areas and epochs [hq] (uint32, this
+ * rank's) are zero before the first call on every rank, and every rank calls with the
+ * same world and hq, once per decode step.  record is this rank's [o (hq x 128) | lse (hq)].
+ * The kernel writes its record into every peer's area, waits (bounded, about a second;
+ * NSNKV_ST_TIMEOUT and no output on expiry) until every rank's record has arrived in
+ * its own, and writes the merged out [hq][128] (out_f32 / lse_out may be NULL).
+ */
+int64_t nsnkv_peer_area_words(int world, int hq);
+int nsnkv_peer_merge_records(int world, int rank, int hq, int dtype, const float *record, void *const *peer_areas,
+                             float *area, uint32_t *epochs, void *out, float *out_f32, float *lse_out,
+                             int32_t *status, void *stream);
+
+/*
  * Int3AsymNsepPchanCache (src/nsn/cache.py:134-313, from_fp16 / to_fp16): x is
  * [rows][tokens][dim] (dim % 8 == 0, 8 <= dim <= 256, rows <= 65535) in x_dtype.
  * Outputs: packed [rows][tokens][3*dim/8] (3-bit indices, 8 per 3 bytes, LSB first:

@@ -83,6 +83,8 @@ SIGNATURES = [
     ("nsnkv_rope_split", c_int, [c_int64, c_int, c_int, c_int, P, P, P, c_int64, P, P, P, P]),
     ("nsnkv_swiglu", c_int, [c_int64, c_int, c_int, P, P, P]),
     ("nsnkv_gemv_rows", c_int, [c_int, c_int, c_int, c_int, P, P, P, P]),
+    ("nsnkv_peer_area_words", c_int64, [c_int, c_int]),
+    ("nsnkv_peer_merge_records", c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     ("nsnkv_merge_shard_records", c_int, [c_int, c_int64, P, c_int64, c_int, P, P, P, P, P]),
     ("nsnkv_int3asym_scratch_bytes", c_int64, [c_int64, c_int64, c_int]),

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libnsnkv.so"
-SOURCES = ["codec.cu", "attention.cu", "int3asym.cu", "scores.cu", "paged_step.cu", "model.cu"]
+SOURCES = ["codec.cu", "attention.cu", "int3asym.cu", "scores.cu", "paged_step.cu", "model.cu", "peer_merge.cu"]
 HEADERS = ["nsnkv_common.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

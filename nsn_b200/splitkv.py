@@ -85,6 +85,41 @@ def merge_records(records: torch.Tensor, n_shards: int, rows: int, dtype=torch.f
     return out, status
 
 
+class PeerRecords:
+    """The (o, lse) record exchange over peer memory, fused with the merge
+    (nsnkv_peer_merge_records): every rank maps every other rank's area (torch's
+    symmetric memory), writes its record into all of them with NVLink stores and merges
+    once the peers' records have landed in its own.  One kernel per step instead of an
+    NCCL all-gather and a merge kernel; capturable in a CUDA graph (the epochs live on the
+    device).  Every rank of ``group`` constructs it with the same hq, and then calls
+    ``merge`` once per step."""
+
+    def __init__(self, hq: int, group=None, device=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        self.group = group if group is not None else dist.group.WORLD
+        self.world, self.rank, self.hq = dist.get_world_size(self.group), dist.get_rank(self.group), hq
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        words = L.load().nsnkv_peer_area_words(self.world, hq)
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            symm.enable_symm_mem_for_group(self.group.group_name)
+        self.area = symm.empty(words, dtype=torch.float32, device=dev)
+        self.area.zero_()
+        self.handle = symm.rendezvous(self.area, self.group)
+        self.epochs = torch.zeros(hq, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(self.group)  # every area is zero before any rank pushes into it
+        self.peers = self.handle.buffer_ptrs_dev
+
+    def merge(self, record: torch.Tensor, out: torch.Tensor, status: torch.Tensor):
+        """record [hq * 129] fp32 ([o | lse]) -> out [hq, 128] merged over the ranks."""
+        rc = L.load().nsnkv_peer_merge_records(
+            self.world, self.rank, self.hq, L.DTYPE_CODE[out.dtype], L.ptr(record), self.peers, L.ptr(self.area),
+            L.ptr(self.epochs), L.ptr(out), None, None, L.ptr(status), L.stream_handle(out.device))
+        L.check(rc, "nsnkv_peer_merge_records")
+        return out
+
+
 class ShardedSequence:
     """One rank's share of a long sequence: its block range of K/V (reference group
     layout [1, h, n_r, ...]) plus, on the last rank, the native tail."""
@@ -131,8 +166,10 @@ class ShardedSequence:
                          status=self.status)
         return self.o, self.lse
 
-    def decode(self, q, group=None, out=None):
-        """Split-KV decode of q [1, hq, 1, 128]: local partials, all-gather, merge.
+    def decode(self, q, group=None, out=None, peer=None):
+        """Split-KV decode of q [1, hq, 1, 128]: local partials, then the exchange and merge:
+        over peer memory when ``peer`` (a PeerRecords of the group) is given, else one NCCL
+        all-gather and nsnkv_merge_shard_records.
 
         Without an initialised process group (or with one rank) the local pass
         already covers the whole sequence and its output is returned as is."""
@@ -142,6 +179,9 @@ class ShardedSequence:
             self.local(q, out=res.view(1, self.hq, 128))
             return res
         self.local(q)
+        if peer is not None:
+            res = torch.empty((self.hq, 128), dtype=q.dtype, device=q.device) if out is None else out
+            return peer.merge(self.rec, res, self.status)
         world = dist.get_world_size(group)
         if self.recv is None or self.recv.numel() != world * self.rec.numel():
             self.recv = torch.empty((world * self.rec.numel(),), dtype=torch.float32, device=self.rec.device)

@@ -3,7 +3,10 @@
 Each rank holds a contiguous block range of one INT5 GQA 64:8 sequence (the last
 rank also holds the tail), runs the fused attention locally, all-gathers the
 (o, lse) partials and merges them; rank 0 compares with one-pass attention over
-the whole sequence on its GPU.
+the whole sequence on its GPU.  The exchange over peer memory
+(nsnkv_peer_merge_records) must give the same bits, eagerly and from CUDA-graph
+replays.  NVLink multicast stays off (NCCL_NVLS_ENABLE=0; the peer kernel uses
+plain stores).
 """
 import datetime
 import os
@@ -53,12 +56,29 @@ def _worker(rank, world, port, q_out):
         out = sh.decode(q)
         torch.cuda.synchronize()
         sh.check()
+        # the exchange over peer memory merges to the same bits, eagerly and in graph replays
+        from nsn_b200.splitkv import PeerRecords
+        peer = PeerRecords(hq)
+        same = True
+        for _ in range(3):
+            same &= torch.equal(sh.decode(q, peer=peer).view(torch.int16), out.view(torch.int16))
+        static = torch.empty_like(out)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            sh.decode(q, out=static, peer=peer)
+        for _ in range(3):
+            static.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            same &= torch.equal(static.view(torch.int16), out.view(torch.int16))
+        del graph
+        sh.check()
         if rank == 0:
             one = kernel.pipeline("GQA_FUSED", (g, kt, q, vg, vt)).float().reshape(hq, 128)
             ok, err = O.within_tolerance(out.float().cpu().numpy(), one.cpu().numpy(), *O.TOLERANCE["float16"])
-            q_out.put(("ok" if ok else "mismatch", err))
+            q_out.put(("ok" if ok and same else "mismatch", (err, same)))
         else:
-            q_out.put(("ok", 0.0))
+            q_out.put(("ok" if same else "mismatch", same))
     except Exception as ex:
         q_out.put(("error", repr(ex)[:300]))
     finally:
@@ -68,6 +88,7 @@ def _worker(rank, world, port, q_out):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_split_kv_over_nccl_two_gpus():
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -79,3 +100,43 @@ def test_split_kv_over_nccl_two_gpus():
         p.join(timeout=120)
     for kind, val in res:
         assert kind == "ok", val
+
+
+def _single_rank(q_out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_port())
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", 0))
+    try:
+        from nsn_b200 import _lib as L
+        from nsn_b200.splitkv import PeerRecords, merge_records
+        hq = 64
+        gen = torch.Generator(device="cuda").manual_seed(9)
+        peer = PeerRecords(hq)
+        status = L.status_tensor(torch.device("cuda", 0))
+        same = True
+        for _ in range(4):  # the epochs advance: every call waits on its own fresh flags
+            rec = torch.randn(hq * 129, generator=gen, device="cuda")
+            got = peer.merge(rec, torch.empty((hq, 128), dtype=torch.float16, device="cuda"), status)
+            want, _ = merge_records(rec, 1, hq, dtype=torch.float16)
+            same &= torch.equal(got.view(torch.int16), want.view(torch.int16))
+        torch.cuda.synchronize()
+        q_out.put(("ok" if same and int(status.item()) == 0 else "mismatch", int(status.item())))
+    except Exception as ex:
+        q_out.put(("error", repr(ex)[:300]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_merge_single_rank():
+    """One rank: the kernel pushes into its own area, finds its own flag and merges as
+    nsnkv_merge_shard_records does."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_single_rank, args=(q,))
+    p.start()
+    kind, val = q.get(timeout=300)
+    p.join(timeout=120)
+    assert kind == "ok", val
