@@ -248,9 +248,10 @@ def run_cfg1(args, rank, world, local, dist):
 
     Times one decode-attention call two ways: replays of a CUDA graph of 100 calls (the
     reference's method; the 30.6 MB working set then stays in the 126 MB L2), and single
-    calls with L2 flushed before each. Both the renorm-factor path (nsnkv_decode_attn_alpha,
-    the paged cache's default) and the restore path (nsnkv_decode_attn, the drop-in VF01
-    entry point with bridge rounding) run on the same blocks."""
+    calls with L2 flushed before each, on the same blocks: the paged cache's default
+    (nsnkv_decode_attn_alpha over block records, K rounded like the bridge), its exact mode,
+    and the restore path (nsnkv_decode_attn, the drop-in VF01 entry point with bridge
+    rounding).  value: the default's latency with L2 flushed."""
     if rank != 0:
         return
     from nsn_b200 import primitives as P
@@ -287,13 +288,14 @@ def run_cfg1(args, rank, world, local, dist):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     res = {}
-    for name, alpha in (("renorm_factor_path", True), ("restore_path", False)):
+    for name, alpha, exact in (("default_k_rounded", True, False), ("exact", True, True),
+                               ("restore_path", False, False)):
         kp, vp = pools_of(alpha)
 
         def call():
             decode_attention(q, kp, vp, h=h, bits=3, blk_stride_head=nb, blk_stride_page=1, n_blocks=nb,
                              max_blocks=nb, k_tail=kt, v_tail=vt, tail_stride_seq=h * t, tail_stride_head=t,
-                             tail_len=t, max_tail=t, out=out, status=status, ws=ws)
+                             tail_len=t, max_tail=t, out=out, status=status, ws=ws, exact=exact)
 
         for _ in range(5):
             call()
@@ -324,8 +326,7 @@ def run_cfg1(args, rank, world, local, dist):
             torch.cuda.synchronize(device)
             warm.append(e0.elapsed_time(e1) * 1000.0 / 100)
         del graph
-        per_block = 3072 + (64 * 4 if alpha else 64 * 2) + 128 * 4
-        nbytes = h * nb * 2 * per_block + h * t * 2 * 256 + 2 * hq * 256
+        nbytes = h * nb * 2 * BLOCK_BYTES + h * t * 2 * 256 + 2 * hq * 256  # algorithmic bytes, every path
         cold.sort()
         warm.sort()
         res[name] = {"us_per_call_graph_replay": warm[len(warm) // 2], "us_per_call_l2_flushed": cold[len(cold) // 2],
@@ -335,7 +336,7 @@ def run_cfg1(args, rank, world, local, dist):
     for r in res.values():
         r["frac_l2_flushed"] = r["gbs_l2_flushed"] / hbm
     line = {"metric": "cfg1 single-sequence decode attention (511 INT3 blocks + 64 tail, GQA 32:8)",
-            "unit": "us/call", "value": res["renorm_factor_path"]["us_per_call_l2_flushed"],
+            "unit": "us/call", "value": res["default_k_rounded"]["us_per_call_l2_flushed"],
             "higher_is_better": False, "n_gpus": 1, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "cfg1", "seed": c["seed"], "paths": res, "peak_gbs": hbm, "peak_kind": peak_kind,
                        "note": "graph replay keeps the 30.6 MB working set in L2; the flushed figure is the HBM one"}}
