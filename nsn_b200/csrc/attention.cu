@@ -1947,12 +1947,16 @@ static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max
   if (ch > 32) ch = 32;
   const int64_t floor_ch = chunk_blocks_for(batch, h, max_blocks, max_tail);
   ch = std::max<int64_t>(ch, floor_ch);
-  if (batch == 1 && ch > 4) {
-    // One sequence: every CTA but the last of each head runs ch blocks, so the step takes
-    // about waves x (ch + 2 blocks of start-up).  Pick the multiple of 4 that minimises it
-    // (cfg4 on one GPU: 28 blocks fill exactly two waves where 32 leave the second 73% full).
-    int64_t best = ch, best_cost = INT64_MAX;
-    for (int64_t c = std::max<int64_t>(4, (floor_ch + 3) / 4 * 4); c <= 32; c += 4) {
+  if (batch == 1) {
+    // One sequence: every CTA but the last of each head runs c blocks.  Candidates start at
+    // about two CTAs per SM, at most 16 blocks (fewer, longer chunks cost fewer CTA starts
+    // and a shorter merge; on B200, cfg1 ran fastest at 12-16 blocks); the multiple of 4
+    // that minimises waves x (c + 2 blocks of start-up) wins (cfg4 on one GPU: 28 blocks
+    // fill two waves exactly where 32 leave the second 73% full).
+    const int64_t c0 = (units * max_blocks + 2 * 148 - 1) / (2 * 148);
+    const int64_t lo = std::max<int64_t>(std::min<int64_t>((c0 + 3) / 4 * 4, 16), (floor_ch + 3) / 4 * 4);
+    int64_t best = lo, best_cost = INT64_MAX;
+    for (int64_t c = lo; c <= 32; c += 4) {
       const int64_t ctas = units * ((max_blocks + c - 1) / c);
       const int64_t cost = (ctas + target - 1) / target * (c + 2);
       if (cost < best_cost) best = c, best_cost = cost;
@@ -1989,7 +1993,9 @@ int attn_last_launches() { return g_attn_launches; }
 // benchmark's sequences: decode steps 7% faster at 8 sequences, 2.6% slower at 64).
 static bool fuse_merge(int64_t batch, int h, int32_t max_blocks, int32_t max_tail, int32_t ch, int32_t max_chunks,
                        int per_sm, int64_t blocks_total) {
-  if (max_chunks > kFusedChunks) return false;
+  // few units (one sequence's kv heads) leave each last CTA a long serial merge, where the
+  // merge kernel spreads the query heads over CTAs (cfg1: 31.7 against 25.6 us)
+  if (max_chunks > kFusedChunks || batch * h < 32) return false;
   const int64_t avg = blocks_total > 0 ? (blocks_total + batch - 1) / batch : max_blocks;
   const int64_t tail_chunks = (static_cast<int64_t>(max_tail) + 1 + static_cast<int64_t>(ch) * kBlock - 1) /
                               (static_cast<int64_t>(ch) * kBlock);
