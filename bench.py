@@ -14,8 +14,10 @@ distributions); the reference measures on captured model K/V that is not
 available here.
 
 Prints one JSON line on rank 0.  `value` = decoded tokens/s of the whole job
-(batch / max-over-ranks device time per step); timed with CUDA events per step,
-L2 flushed (a 256 MiB write) before every timed step, outside the events.
+(batch / max-over-ranks device time per step), K steps back to back between one
+pair of CUDA events.  Inputs larger than L2 instead of a flush: the timed steps
+rotate over as many caches of the rank's sequences as make two L2 sizes of
+blocks (one at 64 sequences, four at 8), so every step reads its blocks from HBM.
 """
 from __future__ import annotations
 
@@ -696,133 +698,146 @@ def main():
     from nsn_b200 import _lib as L
     blocks, tails = workloads.np_cfg2_lengths(args.batch)
     seqs = shard_sequences(blocks, tails, world, rank)
-    total_steps = args.warmup + args.steps + min(args.steps, 16)
+    total_steps = args.warmup + args.steps + 16
     # (+ the end-to-end and latency steps below)
     cache = build_cache(seqs, blocks, tails, total_steps + 1 + 48, device, rounding=args.restore_rounding)
     lib = L.load()
     n_seq = len(seqs)
     q, kn, vn = step_inputs(n_seq, total_steps + 1, device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    # The timed steps rotate over R caches holding the same sequences (built from the same
+    # seeds), R the smallest count whose bytes reach two L2 sizes: between two steps on one
+    # cache at least two L2 sizes of other blocks stream in, so every step reads its blocks
+    # from HBM without an L2 flush between steps (at 64 sequences R = 1).
+    rot_bytes = int((2 * 8 * (cache.host_blocks.astype(np.int64) * BLOCK_BYTES
+                              + (cache.host_tail.astype(np.int64) + 1) * 256)).sum())
+    l2 = getattr(torch.cuda.get_device_properties(device), "L2_cache_size", 0) or (126 << 20)
+    n_rot = max(1, -(-2 * l2 // max(rot_bytes, 1)))
+    rot = [cache] + [build_cache(seqs, blocks, tails, total_steps + 1 + 48, device, rounding=args.restore_rounding)
+                     for _ in range(n_rot - 1)]
 
-    # algorithmic bytes of the next step's attention (sealing changes them) and the kernel's
-    # own extra reads (fp32 factors in place of fp16 norms), from the cache's host counters
-    def attn_bytes():
-        nb = cache.host_blocks.astype(np.int64)
-        tl = cache.host_tail.astype(np.int64) + 1  # + the appended token
-        algo = int((2 * 8 * (nb * BLOCK_BYTES + tl * 256)).sum() + 2 * n_seq * 32 * 256)
-        over = int((2 * 8 * nb).sum()) * FACTOR_OVERHEAD if cache.uses_alpha_path() else 0
-        return algo, over
-
-    for i in range(args.warmup):
-        cache.step(q[i], kn[i], vn[i])
+    for i in range(max(args.warmup, n_rot)):
+        rot[i % n_rot].step(q[i % args.warmup], kn[i % args.warmup], vn[i % args.warmup])
     torch.cuda.synchronize(device)
-    cache.check()
+    for c in rot:
+        c.check()
 
     E = lambda: torch.cuda.Event(enable_timing=True)
-    ev = [(E(), E()) for _ in range(args.steps)]
     launches = 0
     if dist:
         dist.barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clk:
-        # the timed steps: L2 flushed before each, one event pair around each step
+        # the timed steps: back to back, rotating over the caches, one event pair around all
+        t0, t1 = E(), E()
+        t0.record(stream)
         for i in range(args.steps):
-            flush.zero_()
             s = args.warmup + i
-            ev[i][0].record(stream)
-            cache.step(q[s], kn[s], vn[s])
-            ev[i][1].record(stream)
-            launches += lib.nsnkv_paged_plan_last_launches(cache._plan)
+            c = rot[i % n_rot]
+            c.step(q[s], kn[s], vn[s])
+            launches += lib.nsnkv_paged_plan_last_launches(c._plan)
+        t1.record(stream)
         torch.cuda.synchronize(device)
     if dist:
         dist.barrier()
-    cache.check()
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    mean_step = sum(step_ms) / len(step_ms)
-    # the attention launches of further steps, timed apart from their seal by an event the
-    # step records between them (that event costs the seal its overlap, so these steps are
-    # not the timed ones); their algorithmic bytes from the host counters
-    n_attn = min(args.steps, 16)
-    aev = [(E(), E()) for _ in range(n_attn)]
-    bytes_per = []
-    for i in range(n_attn):
-        bytes_per.append(attn_bytes())
-        flush.zero_()
-        s = args.warmup + args.steps + i
-        aev[i][0].record(stream)
-        cache.step(q[s], kn[s], vn[s], attn_event=aev[i][1])
-    torch.cuda.synchronize(device)
-    cache.check()
-    mean_attn = sum(a.elapsed_time(b) for a, b in aev) / n_attn
+    for c in rot:
+        c.check()
+    mean_step = t0.elapsed_time(t1) / args.steps
+    # ---- attention alone, the roofline's kernel time: one decode call's chain of launches
+    # (chunk grid, tail grid, merge unless fused) with the appended token, as inside a step but
+    # without the seal, back to back in a CUDA graph that rotates over the caches as the timed
+    # steps do (every call reads its blocks from HBM), replayed between one event pair.  The
+    # calls advance no counter: each writes its cache's next tail row, which the next step
+    # overwrites.  Algorithmic bytes per call from each cache's host counters.
+    from nsn_b200.kernel import decode_attention
+    from nsn_b200 import primitives as P
+    n_calls = n_rot * max(1, -(-16 // n_rot))
+    s_attn = args.warmup + args.steps
+
+    def graph_ms(call):
+        for i in range(3):
+            call(rot[i % n_rot], s_attn + i)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n_calls):
+                call(rot[i % n_rot], s_attn + i % 16)
+        g.replay()
+        torch.cuda.synchronize(device)
+        a0, a1 = E(), E()
+        a0.record(stream)
+        g.replay()
+        a1.record(stream)
+        torch.cuda.synchronize(device)
+        del g
+        for c in rot:
+            c.check()
+        return a0.elapsed_time(a1) / n_calls
+
+    def call_bytes(c):
+        nb = c.host_blocks.astype(np.int64)
+        tl = c.host_tail.astype(np.int64) + 1
+        algo = int((2 * 8 * (nb * BLOCK_BYTES + tl * 256)).sum() + 2 * n_seq * 32 * 256)
+        over = int((2 * 8 * nb).sum()) * FACTOR_OVERHEAD if c.uses_alpha_path() else 0
+        return algo, over
+
+    mean_attn = graph_ms(lambda c, s: c.attend(q[s], kn[s], vn[s]))
+    bytes_attn = sum(call_bytes(rot[i % n_rot])[0] for i in range(n_calls)) / n_calls
+    bytes_over = sum(call_bytes(rot[i % n_rot])[1] for i in range(n_calls)) / n_calls
     t = torch.tensor([mean_step, mean_attn], dtype=torch.float64, device=device)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     mean_step, mean_attn_max = t.tolist()
-    bytes_attn = sum(b[0] for b in bytes_per) / n_attn
-    bytes_over = sum(b[1] for b in bytes_per) / n_attn
 
-    # ---- both tensor-core kernels on the same blocks, attention only (no append): the
-    # library default (K rounded like the bridge) and the exact restore
+    # ---- both tensor-core kernels on the same blocks, timed as above: the library default
+    # (K rounded like the bridge) and the exact restore
     kernels = None
     if cache.uses_alpha_path() and cache.hq // cache.h <= 4:
-        from nsn_b200.kernel import decode_attention
-        from nsn_b200 import primitives as P
-        kw = dict(h=cache.h, bits=3, blk_stride_head=cache.pages, blk_stride_page=1, n_blocks=cache.n_blocks,
-                  max_blocks=cache.max_blocks, k_tail=cache.k_tail, v_tail=cache.v_tail,
-                  tail_stride_seq=cache.h * P.BLOCK, tail_stride_head=P.BLOCK, tail_len=cache.tail_len,
-                  max_tail=P.BLOCK - 1, block_table=cache.block_table, status=cache.status, ws=cache.ws,
-                  blk_bytes=cache.blk_bytes)
-        res = {}
-        for name, ex in (("default", False), ("exact", True)):
-            for _ in range(3):
-                decode_attention(q[0], cache.k_pool, cache.v_pool, exact=ex, **kw)
-            ts = []
-            for i in range(min(args.steps, 16)):
-                flush.zero_()
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a0.record(stream)
-                decode_attention(q[i], cache.k_pool, cache.v_pool, exact=ex, **kw)
-                a1.record(stream)
-                torch.cuda.synchronize(device)
-                ts.append(a0.elapsed_time(a1))
-            res[name] = sum(ts) / len(ts)
-        cache.check()
-        nb = cache.n_blocks.long()
-        algo = int((2 * 8 * (nb * BLOCK_BYTES + cache.tail_len.long() * 256)).sum() + 2 * n_seq * 32 * 256)
-        kernels = {"what": "attention only (no append) on the same cache state, L2 flushed, rank 0",
+        def via(ex):
+            def call(c, s):
+                decode_attention(q[s], c.k_pool, c.v_pool, h=c.h, bits=3, blk_stride_head=c.pages, blk_stride_page=1,
+                                 n_blocks=c.n_blocks, max_blocks=c.max_blocks, k_tail=c.k_tail, v_tail=c.v_tail,
+                                 tail_stride_seq=c.h * P.BLOCK, tail_stride_head=P.BLOCK, tail_len=c.tail_len,
+                                 max_tail=P.BLOCK - 1, block_table=c.block_table, k_new=kn[s], v_new=vn[s],
+                                 out=c.out, status=c.status, ws=c.ws, blk_bytes=c.blk_bytes, exact=ex,
+                                 blocks_total=int(c.host_blocks.sum()))
+            return call
+
+        res = {name: graph_ms(via(ex)) for name, ex in (("default", False), ("exact", True))}
+        kernels = {"what": "attention (with the append, no seal), back to back in a CUDA graph rotating over the "
+                           "timed caches, rank 0",
                    "default_k_rounded": {"attn_ms": res["default"],
-                                         "frac": algo / (res["default"] / 1000.0) / 1e9 / peaks()[0],
+                                         "frac": bytes_attn / (res["default"] / 1000.0) / 1e9 / peaks()[0],
                                          "contract": "K rounded to fp16 as restore_group rounds it, V exact: "
                                                      "within the parity bar of the reference bridge on every "
                                                      "input (golden cases incl. unscaled cfg0 queries)"},
-                   "exact": {"attn_ms": res["exact"], "frac": algo / (res["exact"] / 1000.0) / 1e9 / peaks()[0],
+                   "exact": {"attn_ms": res["exact"],
+                             "frac": bytes_attn / (res["exact"] / 1000.0) / 1e9 / peaks()[0],
                              "contract": "exact fp32 restore of K and V: within the parity bar of the bridge "
                                          "on this workload's 1/sqrt(128)-scaled queries (full-size cfg2 test)"}}
 
     # ---- end to end through the public API with host buffers (pinned), rank-local
     e2e = None
     if True:
-        # a step's q, k_new and v_new sit back to back in one pinned host buffer and move with
-        # one host-to-device copy (as a serving loop would stage them); the views feed the API
-        nq, nk = q[0].numel(), kn[0].numel()
+        # a step's q, k_new and v_new sit back to back in one pinned host buffer, and the output
+        # returns to pinned host memory: PagedKVCache.step_host (nsnkv_paged_step_host), whose
+        # plan stages them through two device slots on copy streams of its own, so the copies
+        # of neighbouring steps overlap each step's kernels
         inh = torch.cat([q[:4].reshape(4, -1), kn[:4].reshape(4, -1), vn[:4].reshape(4, -1)], 1).cpu().pin_memory()
-        ind = torch.empty(inh.shape[1], dtype=inh.dtype, device=device)
-        qd = ind[:nq].view(q[0].shape)
-        knd = ind[nq:nq + nk].view(kn[0].shape)
-        vnd = ind[nq + nk:].view(vn[0].shape)
-        outh = torch.empty((n_seq, 32, 128), dtype=torch.float16).pin_memory()
+        outh = [torch.empty((n_seq, 32, 128), dtype=torch.float16).pin_memory() for _ in range(2)]
+        fin = [E() for _ in rot]  # per cache: its last output copy
         e_steps = max(8, min(args.steps, 32))
+        for i, c in enumerate(rot):  # untimed: each plan makes its staging at its first host step
+            c.step_host(inh[i % 4], outh[0], done_event=fin[i])
         torch.cuda.synchronize(device)
         if dist:
             dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
+        e0, e1 = E(), E()
         e0.record(stream)
         for i in range(e_steps):
-            ind.copy_(inh[i % 4], non_blocking=True)
-            o = cache.step(qd, knd, vnd)
-            outh.copy_(o, non_blocking=True)
+            rot[i % n_rot].step_host(inh[i % 4], outh[i % 2], done_event=fin[i % n_rot])
+        for ev_ in fin:
+            stream.wait_event(ev_)
         e1.record(stream)
         torch.cuda.synchronize(device)
         te = torch.tensor([e0.elapsed_time(e1) / e_steps], dtype=torch.float64, device=device)
@@ -830,25 +845,26 @@ def main():
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = te.item()
         e2e = {"value": args.batch / (e2e_ms / 1000.0), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(qd.numel() * 2 + knd.numel() * 2 + vnd.numel() * 2),
-               "d2h_bytes_per_step": int(outh.numel() * 2), "ms_per_step": e2e_ms,
-               "path": "PagedKVCache.step (public API), pinned host q|k_new|v_new in (one copy), output out, per rank; "
-                       "steps enqueued back to back (throughput)"}
-        # latency: the same step with the host waiting for each step's output
+               "h2d_bytes_per_step": int(inh[0].numel() * 2), "d2h_bytes_per_step": int(outh[0].numel() * 2),
+               "ms_per_step": e2e_ms,
+               "path": "PagedKVCache.step_host (nsnkv_paged_step_host, the C-ABI step with host buffers): pinned "
+                       "host q|k_new|v_new in, output to pinned host memory, per rank; steps enqueued back to back "
+                       "(throughput), the plan's copy streams overlapping neighbouring steps; rotating over the "
+                       "same caches as the timed steps"}
+        # latency: the same call with the host waiting for each step's output
         lat = []
         for i in range(min(args.steps, 16)):
-            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0, l1 = E(), E()
             l0.record(stream)
-            ind.copy_(inh[i % 4], non_blocking=True)
-            o = cache.step(qd, knd, vnd)
-            outh.copy_(o, non_blocking=True)
-            l1.record(stream)
+            rot[i % n_rot].step_host(inh[i % 4], outh[0], done_event=l1)
             l1.synchronize()
             lat.append(l0.elapsed_time(l1))
         lat.sort()
         e2e["latency_ms_per_step"] = lat[len(lat) // 2]
-        e2e["latency_what"] = "median of device time from the input copy to the output copy, the host waiting each step"
-        cache.check()
+        e2e["latency_what"] = ("median of device time from the call's entry on the stream to its output copy's end, "
+                               "the host waiting for each step")
+        for c in rot:
+            c.check()
 
     hbm, peak_kind = peaks()
     achieved = bytes_attn / (mean_attn / 1000.0) / 1e9  # this rank
@@ -881,7 +897,10 @@ def main():
                                    "GQA 32:8, head_dim 128, ctx U{32..256} blocks + tail U[0,63], "
                                    f"q N(0,1)/sqrt(128); PagedKVCache restore_rounding={args.restore_rounding!r}",
                        "global_batch": args.batch, "hq": 32, "h": 8, "bits": 3, "parallelism": f"batch-shard{world}",
-                       "l2": "flushed (256 MiB write) before every timed step, outside the events",
+                       "l2": f"not flushed: inputs larger than L2; the timed steps rotate over {n_rot} cache(s) of "
+                             f"the rank's sequences ({rot_bytes / 1e6:.1f} MB of blocks each), so at least two L2 "
+                             "sizes of other blocks stream in between two steps on one cache",
+                       "rotation_caches_rank0": n_rot,
                        "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
             "roofline": {"bound": "hbm",
@@ -895,6 +914,9 @@ def main():
                                         args.restore_rounding],
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": peak_kind, "traffic": None,
+                         "time_what": f"mean device time of one attention call (with the append, no seal) over "
+                                      f"{n_calls} calls back to back in a CUDA graph rotating over the timed caches, "
+                                      "rank 0",
                          "traffic_note": "not captured in this run (ncu figures are in the committed profile summaries)",
                          "bytes_per_launch": bytes_attn,
                          "bytes_what": "algorithmic: 3712 B per sealed K or V block (codes + fp16 norm + min/scale), "

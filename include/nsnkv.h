@@ -359,6 +359,23 @@ typedef struct nsnkv_paged_desc {
 int nsnkv_paged_plan_create(const nsnkv_paged_desc *desc, void **plan);
 int nsnkv_paged_step(void *plan, const void *q, const void *k_new, const void *v_new, void *out,
                      void *attn_event, void *stream);
+/*
+ * One step with host buffers: host_in holds the step's q [batch, hq, 128], k_new and
+ * v_new [batch, h, 128] back to back in the cache dtype; host_out receives the output
+ * [batch, hq, 128].  The plan copies host_in into one of two device slots on a copy
+ * stream of its own, runs nsnkv_paged_step on `stream` over that slot, and copies the
+ * output back on a second copy stream; with pinned host buffers the copies of
+ * neighbouring steps overlap this step's kernels.  The input copy starts once `stream`
+ * reached the previous host-buffer call (the first call: this one).  done_event (a
+ * cudaEvent_t, may be NULL) is recorded after the output copy: host_out is written, and
+ * host_in may be reused, once it completed.  The slots and streams are made on the
+ * current device at the first call (later calls on another device: NSNKV_ERR_ARG) and
+ * released by nsnkv_paged_plan_destroy, which first waits for the plan's copies.
+ * Replaces the caller-side staging of the reference's decode step (its tensors move
+ * to the device inside the HF forward,
+ * experiments/nb06/source/loop_kv_nb06_attention.py:33-88).
+ */
+int nsnkv_paged_step_host(void *plan, const void *host_in, void *host_out, void *done_event, void *stream);
 /* Kernels the plan's last successful step launched (0 before the first step). */
 int nsnkv_paged_plan_last_launches(void *plan);
 int nsnkv_paged_plan_destroy(void *plan);

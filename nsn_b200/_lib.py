@@ -77,6 +77,7 @@ SIGNATURES = [
                                             c_int64, P, P]),
     ("nsnkv_paged_plan_create", c_int, [P, P]),
     ("nsnkv_paged_step", c_int, [P, P, P, P, P, P, P]),
+    ("nsnkv_paged_step_host", c_int, [P, P, P, P, P]),
     ("nsnkv_paged_plan_last_launches", c_int, [P]),
     ("nsnkv_paged_plan_destroy", c_int, [P]),
     ("nsnkv_add_rmsnorm", c_int, [c_int64, c_int, c_int, P, P, P, ctypes.c_float, P, P, P]),

@@ -239,6 +239,7 @@ class PagedKVCache:
         self._plan = None
         self._plan = self._make_plan(lib)
         self._step_fn = lib.nsnkv_paged_step
+        self._step_host_fn = lib.nsnkv_paged_step_host
         self._q_shape = (batch, self.hq, w.DIM)
         self._kv_shape = (batch, h, w.DIM)
 
@@ -431,6 +432,32 @@ class PagedKVCache:
         if rc:
             L.check(rc, "nsnkv_paged_step")
         return o
+
+    def step_host(self, host_in: torch.Tensor, host_out: torch.Tensor, done_event=None):
+        """One decode step from host memory (nsnkv_paged_step_host): ``host_in`` holds the
+        step's q [batch, hq, 128], k_new and v_new [batch, h, 128] back to back, ``host_out``
+        receives the output [batch, hq, 128]; both CPU tensors of the cache dtype, pinned for
+        the copies to overlap the neighbouring steps.  The copies run on the plan's own
+        streams: ``host_out`` is written (and ``host_in`` free again) once ``done_event`` (a
+        torch.cuda.Event, recorded by the call) completed."""
+        dt = self.dtype
+        n_in = self.batch * (self.hq + 2 * self.h) * 128
+        ok = (host_in.device.type == "cpu" and host_out.device.type == "cpu" and host_in.dtype == dt
+              and host_out.dtype == dt and host_in.is_contiguous() and host_out.is_contiguous()
+              and host_in.numel() == n_in and host_out.numel() == self.batch * self.hq * 128)
+        w.require(ok, "paged host step operands: contiguous CPU tensors of the cache dtype, q|k_new|v_new "
+                      "(batch * (hq + 2 h) * 128 elements) in and batch * hq * 128 out")
+        stream = torch.cuda.current_stream(self.device)
+        ev = None
+        if done_event is not None:
+            if not done_event.cuda_event:  # torch creates the event at its first record
+                done_event.record(stream)
+            ev = done_event.cuda_event
+        with torch.cuda.device(self.device):
+            rc = self._step_host_fn(self._plan, host_in.data_ptr(), host_out.data_ptr(), ev, stream.cuda_stream)
+        if rc:
+            L.check(rc, "nsnkv_paged_step_host")
+        return host_out
 
     def check(self):
         st = int(self.status.item())

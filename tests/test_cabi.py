@@ -115,6 +115,10 @@ def test_paged_plan_descriptor_and_host_checks():
     tl[1] = 63
     assert lib.nsnkv_paged_step(handle, P(fake), P(fake), P(fake), P(fake), P(None), P(None)) == _lib.ERR_TOO_LARGE
     assert list(nb) == [0, 4, 2] and list(tl) == [5, 63, 0]  # unchanged by a rejected step
+    # the host-buffer step: the same checks, before any staging is made (no device touched)
+    assert lib.nsnkv_paged_step_host(handle, P(None), P(fake), P(None), P(None)) == _lib.ERR_ARG
+    assert lib.nsnkv_paged_step_host(P(None), P(fake), P(fake), P(None), P(None)) == _lib.ERR_ARG
+    assert lib.nsnkv_paged_step_host(handle, P(fake), P(fake), P(None), P(None)) == _lib.ERR_TOO_LARGE
     assert lib.nsnkv_paged_plan_destroy(handle) == _lib.OK
     assert lib.nsnkv_paged_plan_destroy(P(None)) == _lib.ERR_ARG
 

@@ -294,3 +294,56 @@ def test_full_table_row_keeps_its_tail():
         cache.check()
     assert torch.isfinite(out.float()).all()
     assert torch.equal(cache.records[:, pages1], before1)  # sequence 1 sealed nothing, its pages unchanged
+
+
+@pytest.mark.parametrize("mode", ["exact", "k"])
+def test_host_buffer_step_matches_device_step(mode):
+    """nsnkv_paged_step_host (PagedKVCache.step_host) against nsnkv_paged_step on a twin
+    cache: 70 steps with seals, the inputs from pinned host memory, two output slots in flight
+    at once and the host reading each output only after its done event; every output and the
+    final counters and records are bit-equal.  Another device plan's steps on the caller's
+    stream interleave with the copies."""
+    from nsn_b200 import workloads
+    from nsn_b200.paged import PagedKVCache
+    rng = np.random.default_rng(31)
+    h, hq, lens = 2, 8, [3 * 64 + 60, 64 + 1, 5]
+    caches = []
+    for _ in range(2):
+        c = PagedKVCache(len(lens), h, max_blocks=6, bits=3, dtype=torch.float16, hq=hq, restore_rounding=mode)
+        r2 = np.random.default_rng(32)
+        for b, L in enumerate(lens):
+            c.prefill(b, torch.from_numpy(workloads.np_kv(r2, (h, L, 128), workloads.K_OUTLIERS_4, 0.5)).cuda(),
+                      torch.from_numpy(workloads.np_kv(r2, (h, L, 128), (), 0.5)).cuda())
+        caches.append(c)
+    dev_cache, host_cache = caches
+    B, steps = len(lens), 70
+    q = (rng.standard_normal((steps, B, hq, 128)) / np.sqrt(128)).astype(np.float16)
+    kn = workloads.np_kv(rng, (steps, B, h, 128), (), 0.5)
+    vn = workloads.np_kv(rng, (steps, B, h, 128), (), 0.5)
+    inh = torch.from_numpy(np.concatenate([q.reshape(steps, -1), kn.reshape(steps, -1), vn.reshape(steps, -1)],
+                                          1)).pin_memory()
+    outh = [torch.empty((B, hq, 128), dtype=torch.float16).pin_memory() for _ in range(2)]
+    evs = [torch.cuda.Event() for _ in range(2)]
+    got, want = [], []
+    for s in range(steps):
+        j = s % 2
+        if s >= 2:
+            evs[j].synchronize()
+            got.append(outh[j].clone())
+        host_cache.step_host(inh[s], outh[j], done_event=evs[j])
+        want.append(dev_cache.step(torch.from_numpy(q[s]).cuda(), torch.from_numpy(kn[s]).cuda(),
+                                   torch.from_numpy(vn[s]).cuda()).cpu())
+    for s in range(steps - 2, steps):
+        evs[s % 2].synchronize()
+        got.append(outh[s % 2].clone())
+    torch.cuda.synchronize()
+    dev_cache.check()
+    host_cache.check()
+    for s in range(steps):
+        assert torch.equal(got[s], want[s]), s
+    assert torch.equal(dev_cache.n_blocks, host_cache.n_blocks) and torch.equal(dev_cache.tail_len,
+                                                                                 host_cache.tail_len)
+    assert list(dev_cache.host_blocks) == list(host_cache.host_blocks)
+    assert torch.equal(dev_cache.records, host_cache.records)
+    with pytest.raises(Exception):
+        host_cache.step_host(inh[0].cuda(), outh[0])  # device tensors are refused
