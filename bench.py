@@ -17,7 +17,7 @@ Prints one JSON line on rank 0.  `value` = decoded tokens/s of the whole job
 (batch / max-over-ranks device time per step), K steps back to back between one
 pair of CUDA events.  Inputs larger than L2 instead of a flush: the timed steps
 rotate over as many caches of the rank's sequences as make two L2 sizes of
-blocks (one at 64 sequences, four at 8), so every step reads its blocks from HBM.
+blocks (one at 64 sequences, five at 8), so every step reads its blocks from HBM.
 """
 from __future__ import annotations
 
@@ -490,15 +490,19 @@ def cfg4_measure(args, rank, world, local, dist, with_encode=True, steps=None, w
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     nccl_ms, enc_ms_max, local_ms, peer_ms = t.tolist()
-    step_ms = peer_ms if peer_ms > 0 else nccl_ms
+    # both exchanges give the same bits (the peer path is used only once it reproduced the
+    # NCCL path's); the step is the faster of the two at this world size
+    use_peer = 0 < peer_ms < nccl_ms
+    step_ms = peer_ms if use_peer else nccl_ms
     exchange = ("peer memory (nsnkv_peer_merge_records: NVLink stores into every rank's symmetric area, fused "
-                "with the merge)" if peer_ms > 0 else "NCCL all-gather + nsnkv_merge_shard_records")
+                "with the merge)" if use_peer else "NCCL all-gather + nsnkv_merge_shard_records")
     total_bytes = 2 * 8 * (nb_total * 5760 + 64 * 256) + 2 * hq * 256
     total_enc_bytes = 2 * (nb_total * 8 * 64 * 128 * 2 + nb_total * 8 * 5760)
     hbm, peak_kind = peaks()
     return {"n_gpus": world, "step_ms": step_ms, "tokens_per_s": 1000.0 / step_ms,
             "exchange": exchange if world > 1 else "none (one rank)",
-            "nccl_step_ms": nccl_ms if world > 1 else None, "peer_note": peer_note,
+            "nccl_step_ms": nccl_ms if world > 1 else None, "peer_step_ms": peer_ms if peer_ms > 0 else None,
+            "peer_note": peer_note,
             "local_attention_ms": local_ms, "gather_merge_ms": max(step_ms - local_ms, 0.0),
             "decode_gbs_whole_job": total_bytes / (step_ms / 1000.0) / 1e9,
             "frac_per_gpu": total_bytes / (step_ms / 1000.0) / 1e9 / world / hbm, "peak": hbm, "peak_kind": peak_kind,
@@ -873,13 +877,14 @@ def main():
     # ---- cfg4 split-KV on the same ranks (every rank takes part in its all-gathers)
     cfg4 = None
     if not args.no_cfg4:
-        del cache, q, kn, vn
+        del cache, rot, c, q, kn, vn
         torch.cuda.empty_cache()
         cfg4 = cfg4_measure(args, rank, world, local, dist, with_encode=False, steps=min(args.steps, 20), warmup=3)
         cfg4["what"] = ("cfg4 split-KV decode step: one 131072-token INT5 sequence (2047 blocks + 64 tail, GQA "
                         "64:8) split by block ranges over the ranks; local fused attention (attn_sealed_kernel "
                         "over INT5 block records, K rounded like the bridge) + the (o, lse) record exchange and "
-                        "merge named by `exchange` (nccl_step_ms: the NCCL all-gather + merge kernel instead), "
+                        "merge named by `exchange`, the faster of the two verified exchanges (nccl_step_ms: the NCCL "
+                        "all-gather + merge kernel; peer_step_ms: the peer-memory exchange fused with the merge), "
                         "replayed as a CUDA graph, L2 flushed; gather_merge_ms = step - local attention alone "
                         "(max over ranks)")
     if rank == 0:
