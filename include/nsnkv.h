@@ -395,6 +395,9 @@ int nsnkv_paged_plan_destroy(void *plan);
  *   nsnkv_swiglu       one fused row [gate (inter) | up (inter)] -> silu(gate) * up (LlamaMLP)
  *   nsnkv_gemv_rows    the projections on those few rows: each weight row streams from HBM
  *                      once into tensor-core MMAs
+ * All four launch with programmatic dependent launch: a kernel may become resident while
+ * the kernel before it on the stream finishes, and waits for it (griddepcontrol.wait)
+ * before reading anything; stream order is kept.
  */
 int nsnkv_add_rmsnorm(int64_t rows, int dim, int dtype, const void *x, const void *residual, const void *weight,
                       float eps, void *residual_out, void *out, void *stream);
@@ -402,8 +405,12 @@ int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, co
                      int64_t cs_stride, void *q, void *k, void *v, void *stream);
 int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *out, void *stream);
 /* y [m][n] = x [m][k] . w [n][k]^T with fp32 accumulation, for decode rows: m <= 8, n % 8 == 0,
- * k % 256 == 0, x and w 16-byte aligned (a torch Linear without bias on a few rows). */
-int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, void *stream);
+ * k % 256 == 0, x and w 16-byte aligned (a torch Linear without bias on a few rows).
+ * flags: NSNKV_GEMV_FIXED_WEIGHTS when no work enqueued on the stream before this call
+ * writes w (model weights while decoding): the first weight loads then start before the
+ * wait for the preceding kernel, overlapping it; x is read after the wait either way. */
+#define NSNKV_GEMV_FIXED_WEIGHTS 1
+int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, int flags, void *stream);
 
 /*
  * Combine per-shard attention partials (one row per shard) into the final

@@ -31,6 +31,7 @@ ST_CAPACITY = 64
 
 ATTN_RECORD_ORDER = 1  # nsnkv_decode_attn_alpha flags
 ATTN_EXACT = 2
+GEMV_FIXED_WEIGHTS = 1
 
 F16, BF16, F32 = 0, 1, 2
 DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
@@ -83,7 +84,7 @@ SIGNATURES = [
     ("nsnkv_add_rmsnorm", c_int, [c_int64, c_int, c_int, P, P, P, ctypes.c_float, P, P, P]),
     ("nsnkv_rope_split", c_int, [c_int64, c_int, c_int, c_int, P, P, P, c_int64, P, P, P, P]),
     ("nsnkv_swiglu", c_int, [c_int64, c_int, c_int, P, P, P]),
-    ("nsnkv_gemv_rows", c_int, [c_int, c_int, c_int, c_int, P, P, P, P]),
+    ("nsnkv_gemv_rows", c_int, [c_int, c_int, c_int, c_int, P, P, P, c_int, P]),
     ("nsnkv_peer_area_words", c_int64, [c_int, c_int]),
     ("nsnkv_peer_merge_records", c_int, [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     ("nsnkv_merge_shards", c_int, [c_int, c_int64, P, P, c_int, P, P, P, P, P]),

@@ -31,10 +31,36 @@ template <> __device__ __forceinline__ __nv_bfloat16 ft<__nv_bfloat16>(float x) 
 
 constexpr int kNormThreads = 256;
 
+// Programmatic dependent launch.  Every kernel here is launched with programmatic stream
+// serialisation, so it may become resident while the kernel before it on the stream is
+// still running.  It waits (griddepcontrol.wait: that kernel complete and its writes
+// visible) before it reads anything that kernel may have written, and only after the wait
+// lets the kernel after it launch.  So a kernel that starts early never overlaps any
+// kernel but its immediate predecessor, which has itself passed its own wait.
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+int launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+}
+
 // One CTA per row.  Each thread keeps its elements in registers between the two passes.
 template <typename T, int PER>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, const T *r, const T *w, float eps,
                                                                     int dim, T *res_out, T *y) {
+  dep_wait();
+  dep_release();
   const int64_t row = blockIdx.x;
   const T *xr = x + row * dim;
   const T *rr = r ? r + row * dim : nullptr;
@@ -73,6 +99,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, c
 template <typename T>
 __global__ void __launch_bounds__(64) rope_split_kernel(const T *qkv, const T *cs, const T *sn, int64_t cs_stride,
                                                         int hq, int h, T *q, T *k, T *v) {
+  dep_wait();
+  dep_release();
   const int64_t row = blockIdx.y;
   const int head = blockIdx.x;  // 0 .. hq + 2h - 1 over the fused row's q, k, v heads
   const int i = threadIdx.x;
@@ -94,6 +122,8 @@ __global__ void __launch_bounds__(64) rope_split_kernel(const T *qkv, const T *c
 
 template <typename T>
 __global__ void swiglu_kernel(const T *gu, int64_t rows, int inter, T *y) {
+  dep_wait();
+  dep_release();
   const int64_t n = rows * inter;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -112,9 +142,13 @@ __global__ void swiglu_kernel(const T *gu, int64_t rows, int inter, T *y) {
 // k0 + 8t and the same k of X row g; the k order inside each 32-wide block is permuted
 // alike for A and B (MMA slot 2t+j of k-step 0 <- k0 + 8t + j, slot 2t+8+j <- k0 + 8t + 2 + j;
 // k-step 1 takes k0 + 8t + 4..7), which leaves the dot products unchanged.  X rows past
-// m are zero; the warps' fp32 partials meet in shared memory.
+// m are zero; the warps' fp32 partials meet in shared memory.  With fixed_w (weights that
+// no work still running on the stream writes: model weights while decoding) a lane's first
+// weight vectors are loaded before the programmatic wait, so the weight stream starts
+// while the kernel before this one finishes; x is read only after the wait.
 template <typename T>
-__global__ void __launch_bounds__(256) gemv_rows_kernel(const T *x, const T *w, T *y, int m, int n, int k) {
+__global__ void __launch_bounds__(256) gemv_rows_kernel(const T *x, const T *w, T *y, int m, int n, int k,
+                                                        int fixed_w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int n0 = blockIdx.x * 8;
   const int span = k / 8;
@@ -126,6 +160,24 @@ __global__ void __launch_bounds__(256) gemv_rows_kernel(const T *x, const T *w, 
   constexpr int kUnroll = 4;
   int it = 0;
   const int iters = span / 32;  // 32-wide k blocks of this warp: one uint4 (8 of the block's 32 k) per lane
+  if (fixed_w && iters >= kUnroll) {
+    uint4 wv[kUnroll], xv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) wv[u] = __ldcs(wp + 4 * u);
+    dep_wait();
+    dep_release();
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) xv[u] = row ? xp[4 * u] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      mma16816<T>(c, xv[u].x, 0u, xv[u].y, 0u, wv[u].x, wv[u].y);
+      mma16816<T>(c, xv[u].z, 0u, xv[u].w, 0u, wv[u].z, wv[u].w);
+    }
+    it = kUnroll;
+  } else {
+    dep_wait();
+    dep_release();
+  }
   for (; it + kUnroll <= iters; it += kUnroll) {
     uint4 wv[kUnroll], xv[kUnroll];
 #pragma unroll
@@ -166,13 +218,10 @@ int add_rmsnorm_launch(int64_t rows, int dim, const void *x, const void *r, cons
   const T *xp = static_cast<const T *>(x), *rp = static_cast<const T *>(r), *wp = static_cast<const T *>(w);
   T *ro = static_cast<T *>(res_out), *yp = static_cast<T *>(y);
   const dim3 grid(static_cast<unsigned>(rows));
-  if (dim <= 4 * kNormThreads)
-    add_rmsnorm_kernel<T, 4><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
-  else if (dim <= 8 * kNormThreads)
-    add_rmsnorm_kernel<T, 8><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
-  else
-    add_rmsnorm_kernel<T, 32><<<grid, kNormThreads, 0, st>>>(xp, rp, wp, eps, dim, ro, yp);
-  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+  const dim3 block(kNormThreads);
+  if (dim <= 4 * kNormThreads) return launch_dep(add_rmsnorm_kernel<T, 4>, grid, block, st, xp, rp, wp, eps, dim, ro, yp);
+  if (dim <= 8 * kNormThreads) return launch_dep(add_rmsnorm_kernel<T, 8>, grid, block, st, xp, rp, wp, eps, dim, ro, yp);
+  return launch_dep(add_rmsnorm_kernel<T, 32>, grid, block, st, xp, rp, wp, eps, dim, ro, yp);
 }
 
 }  // namespace
@@ -203,32 +252,29 @@ int nsnkv_rope_split(int64_t rows, int hq, int h, int dtype, const void *qkv, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(hq + 2 * h), static_cast<unsigned>(rows));
   if (dtype == NSNKV_F16)
-    rope_split_kernel<__half><<<grid, 64, 0, st>>>(
-        static_cast<const __half *>(qkv), static_cast<const __half *>(cos), static_cast<const __half *>(sin), cs_stride,
-        hq, h, static_cast<__half *>(q), static_cast<__half *>(k), static_cast<__half *>(v));
-  else
-    rope_split_kernel<__nv_bfloat16><<<grid, 64, 0, st>>>(
-        static_cast<const __nv_bfloat16 *>(qkv), static_cast<const __nv_bfloat16 *>(cos),
-        static_cast<const __nv_bfloat16 *>(sin), cs_stride, hq, h, static_cast<__nv_bfloat16 *>(q),
-        static_cast<__nv_bfloat16 *>(k), static_cast<__nv_bfloat16 *>(v));
-  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+    return launch_dep(rope_split_kernel<__half>, grid, dim3(64), st, static_cast<const __half *>(qkv),
+                      static_cast<const __half *>(cos), static_cast<const __half *>(sin), cs_stride, hq, h,
+                      static_cast<__half *>(q), static_cast<__half *>(k), static_cast<__half *>(v));
+  return launch_dep(rope_split_kernel<__nv_bfloat16>, grid, dim3(64), st, static_cast<const __nv_bfloat16 *>(qkv),
+                    static_cast<const __nv_bfloat16 *>(cos), static_cast<const __nv_bfloat16 *>(sin), cs_stride, hq,
+                    h, static_cast<__nv_bfloat16 *>(q), static_cast<__nv_bfloat16 *>(k),
+                    static_cast<__nv_bfloat16 *>(v));
 }
 
-int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, void *stream) {
+int nsnkv_gemv_rows(int m, int n, int k, int dtype, const void *x, const void *w, void *y, int flags, void *stream) {
   if (m < 0 || m > 8 || n < 0 || k < 0 || n % 8 != 0 || k % 256 != 0) return NSNKV_ERR_ARG;
   if (dtype != NSNKV_F16 && dtype != NSNKV_BF16) return NSNKV_ERR_ARG;
+  if (flags & ~NSNKV_GEMV_FIXED_WEIGHTS) return NSNKV_ERR_ARG;
   if (m == 0 || n == 0) return NSNKV_OK;
   if (!x || !w || !y || !aligned16(x) || !aligned16(w) || k == 0 || n / 8 > 0x7fffffff) return NSNKV_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = static_cast<unsigned>(n / 8);
+  const dim3 grid(static_cast<unsigned>(n / 8));
+  const int fixed_w = (flags & NSNKV_GEMV_FIXED_WEIGHTS) ? 1 : 0;
   if (dtype == NSNKV_F16)
-    gemv_rows_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(x), static_cast<const __half *>(w),
-                                                   static_cast<__half *>(y), m, n, k);
-  else
-    gemv_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(x),
-                                                          static_cast<const __nv_bfloat16 *>(w),
-                                                          static_cast<__nv_bfloat16 *>(y), m, n, k);
-  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+    return launch_dep(gemv_rows_kernel<__half>, grid, dim3(256), st, static_cast<const __half *>(x),
+                      static_cast<const __half *>(w), static_cast<__half *>(y), m, n, k, fixed_w);
+  return launch_dep(gemv_rows_kernel<__nv_bfloat16>, grid, dim3(256), st, static_cast<const __nv_bfloat16 *>(x),
+                    static_cast<const __nv_bfloat16 *>(w), static_cast<__nv_bfloat16 *>(y), m, n, k, fixed_w);
 }
 
 int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *out, void *stream) {
@@ -240,12 +286,10 @@ int nsnkv_swiglu(int64_t rows, int inter, int dtype, const void *gate_up, void *
   const int64_t n = rows * inter;
   const unsigned blocks = static_cast<unsigned>(n / 256 + 1 < 148 * 8 ? n / 256 + 1 : 148 * 8);
   if (dtype == NSNKV_F16)
-    swiglu_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half *>(gate_up), rows, inter,
-                                                  static_cast<__half *>(out));
-  else
-    swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(gate_up), rows, inter,
-                                                         static_cast<__nv_bfloat16 *>(out));
-  return cudaGetLastError() == cudaSuccess ? NSNKV_OK : NSNKV_ERR_LAUNCH;
+    return launch_dep(swiglu_kernel<__half>, dim3(blocks), dim3(256), st, static_cast<const __half *>(gate_up), rows,
+                      inter, static_cast<__half *>(out));
+  return launch_dep(swiglu_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), st,
+                    static_cast<const __nv_bfloat16 *>(gate_up), rows, inter, static_cast<__nv_bfloat16 *>(out));
 }
 
 }  // extern "C"

@@ -58,9 +58,11 @@ def rope_split(qkv, cos, sin, hq, h):
     return q, k, v
 
 
-def linear_rows(x, weight):
+def linear_rows(x, weight, fixed_weight=False):
     """x [m, k] @ weight[n, k]^T for decode rows (nsnkv_gemv_rows when m <= 8, n % 8 == 0 and
-    k % 256 == 0; torch's linear otherwise)."""
+    k % 256 == 0; torch's linear otherwise).  ``fixed_weight``: no work enqueued before this
+    call writes ``weight`` (model weights while decoding), so the kernel may start streaming
+    it before the preceding kernel on the stream has finished."""
     m, k = x.shape
     n = weight.shape[0]
     if not (m <= 8 and n % 8 == 0 and k % 256 == 0 and x.is_contiguous() and weight.is_contiguous()
@@ -68,7 +70,7 @@ def linear_rows(x, weight):
         return F.linear(x, weight)
     y = torch.empty((m, n), dtype=x.dtype, device=x.device)
     rc = L.load().nsnkv_gemv_rows(m, n, k, L.DTYPE_CODE[x.dtype], x.data_ptr(), weight.data_ptr(), y.data_ptr(),
-                                  _stream(x))
+                                  L.GEMV_FIXED_WEIGHTS if fixed_weight else 0, _stream(x))
     L.check(rc, "nsnkv_gemv_rows")
     return y
 
@@ -172,14 +174,14 @@ class PagedLoopedDecoder:
                     h, x = add_rmsnorm(h, None, ln1.weight, ln1.variance_epsilon)
                 else:
                     h, x = add_rmsnorm(pending, h, ln1.weight, ln1.variance_epsilon)
-                q, k, v = rope_split(linear_rows(x, wqkv), cos, sin, self.hq, self.h)
+                q, k, v = rope_split(linear_rows(x, wqkv, True), cos, sin, self.hq, self.h)
                 o = self._attend(self.caches[slot], q, k, v)
-                h, x = add_rmsnorm(linear_rows(o.reshape(h.shape[0], -1), a.o_proj.weight), h, ln2.weight,
+                h, x = add_rmsnorm(linear_rows(o.reshape(h.shape[0], -1), a.o_proj.weight, True), h, ln2.weight,
                                    ln2.variance_epsilon)
-                pending = linear_rows(swiglu(linear_rows(x, wgu)), mlp.down_proj.weight)
+                pending = linear_rows(swiglu(linear_rows(x, wgu, True)), mlp.down_proj.weight, True)
                 slot += 1
         _, x = add_rmsnorm(pending, h, m.norm.weight, m.norm.variance_epsilon)
-        return linear_rows(x, m.lm_head.weight)
+        return linear_rows(x, m.lm_head.weight, True)
 
     # ------------------------------------------------------------ public API
     @torch.no_grad()

@@ -139,3 +139,10 @@ def test_layer_op_argument_errors():
     assert lib.nsnkv_rope_split(70000, 16, 4, _lib.F16, f, f, f, 0, f, f, f, None) == _lib.ERR_ARG
     assert lib.nsnkv_swiglu(4, 0, _lib.F16, f, f, None) == _lib.ERR_ARG
     assert lib.nsnkv_swiglu(4, 5632, _lib.BF16, None, f, None) == _lib.ERR_ARG
+    fw = _lib.GEMV_FIXED_WEIGHTS
+    assert lib.nsnkv_gemv_rows(9, 512, 256, _lib.F16, f, f, f, fw, None) == _lib.ERR_ARG  # m > 8
+    assert lib.nsnkv_gemv_rows(4, 510, 256, _lib.F16, f, f, f, fw, None) == _lib.ERR_ARG  # n % 8
+    assert lib.nsnkv_gemv_rows(4, 512, 200, _lib.F16, f, f, f, fw, None) == _lib.ERR_ARG  # k % 256
+    assert lib.nsnkv_gemv_rows(4, 512, 256, _lib.F16, f, f, f, 2, None) == _lib.ERR_ARG  # unknown flag
+    assert lib.nsnkv_gemv_rows(4, 512, 256, _lib.F16, P(8), f, f, fw, None) == _lib.ERR_ARG  # misaligned x
+    assert lib.nsnkv_gemv_rows(0, 512, 256, _lib.F16, f, f, f, fw, None) == _lib.OK  # nothing to do

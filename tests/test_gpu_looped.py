@@ -146,15 +146,54 @@ def test_fused_layer_ops_match_the_llama_modules(dtype):
         assert torch.equal(swiglu(gu), want)
 
 
+@pytest.mark.parametrize("fixed", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("m,n,k", [(4, 6144, 2048), (1, 2048, 5632), (8, 512, 256), (3, 32000, 2048)])
-def test_gemv_rows_matches_linear(dtype, m, n, k):
-    """nsnkv_gemv_rows against torch's linear (fp32 accumulation in both, different order)."""
+def test_gemv_rows_matches_linear(dtype, m, n, k, fixed):
+    """nsnkv_gemv_rows against torch's linear (fp32 accumulation in both, different order),
+    with and without NSNKV_GEMV_FIXED_WEIGHTS (weight loads before the programmatic wait)."""
     from nsn_b200.looped import linear_rows
     torch.manual_seed(m * 7 + k)
     x = torch.randn(m, k, device="cuda").to(dtype)
     w = (torch.randn(n, k, device="cuda") / np.sqrt(k)).to(dtype)
-    got = linear_rows(x, w).float()
+    got = linear_rows(x, w, fixed).float()
     want = (x.double() @ w.double().t())
     tol = (2.0 ** -10 if dtype == torch.float16 else 2.0 ** -7) * want.abs() + 1e-3
     assert ((got.double() - want).abs() <= tol).all(), (got.double() - want).abs().max().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_layer_chain_back_to_back_equals_synchronised(dtype):
+    """The layer kernels launch with programmatic dependent launch, and the GEMV with fixed
+    weights loads weight rows before its wait.  A decode layer's chain enqueued back to back
+    (each kernel reading what the one before it wrote) gives the same bits as the same chain
+    with a device synchronise after every op, over 20 repetitions."""
+    from nsn_b200.looped import add_rmsnorm, linear_rows, rope_split, swiglu
+    torch.manual_seed(21)
+    rows, dim, hq, h, inter = 4, 2048, 16, 16, 5632
+    wqkv = (torch.randn((hq + 2 * h) * 128, dim, device="cuda") / np.sqrt(dim)).to(dtype)
+    wo = (torch.randn(dim, hq * 128, device="cuda") / np.sqrt(hq * 128)).to(dtype)
+    wgu = (torch.randn(2 * inter, dim, device="cuda") / np.sqrt(dim)).to(dtype)
+    wd = (torch.randn(dim, inter, device="cuda") / np.sqrt(inter)).to(dtype)
+    ln = (torch.rand(dim, device="cuda") + 0.5).to(dtype)
+    cos = torch.cos(torch.arange(128, device="cuda") * 0.01).to(dtype)
+    sin = torch.sin(torch.arange(128, device="cuda") * 0.01).to(dtype)
+
+    def chain(h0, sync):
+        s = torch.cuda.synchronize if sync else (lambda: None)
+        res, x = add_rmsnorm(h0, None, ln, 1e-5); s()
+        qkv = linear_rows(x, wqkv, True); s()
+        q, k, v = rope_split(qkv, cos, sin, hq, h); s()
+        a = linear_rows(q.reshape(rows, -1), wo, True); s()
+        h2, x2 = add_rmsnorm(a, res, ln, 1e-5); s()
+        gu = linear_rows(x2, wgu, True); s()
+        y = linear_rows(swiglu(gu), wd, True); s()
+        return torch.cat([h2.flatten(), k.flatten(), v.flatten(), y.flatten()])
+
+    with torch.no_grad():
+        for rep in range(20):
+            h0 = torch.randn(rows, dim, device="cuda").to(dtype)
+            want = chain(h0, True)
+            got = chain(h0, False)
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), rep
