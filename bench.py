@@ -662,6 +662,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="nsn", choices=["nsn", "reference"])
     ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--as-rank", default=None, metavar="R/N",
+                    help="one GPU, one process: time rank R's share of an N-way run of the cfg2 batch (the "
+                         "sequences shard_sequences gives that rank), to study a rank of a multi-GPU run alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the cfg4 split-KV sub-record of the cfg2 line")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
@@ -701,12 +704,19 @@ def main():
     from nsn_b200 import workloads
     from nsn_b200 import _lib as L
     blocks, tails = workloads.np_cfg2_lengths(args.batch)
-    seqs = shard_sequences(blocks, tails, world, rank)
+    if args.as_rank:
+        if world > 1:
+            raise SystemExit("--as-rank runs one process")
+        r_, n_ = (int(x) for x in args.as_rank.split("/"))
+        seqs = shard_sequences(blocks, tails, n_, r_)
+    else:
+        seqs = shard_sequences(blocks, tails, world, rank)
     total_steps = args.warmup + args.steps + 16
     # (+ the end-to-end and latency steps below)
     cache = build_cache(seqs, blocks, tails, total_steps + 1 + 48, device, rounding=args.restore_rounding)
     lib = L.load()
     n_seq = len(seqs)
+    tok_step = n_seq if args.as_rank else args.batch  # tokens one timed step decodes, whole job
     q, kn, vn = step_inputs(n_seq, total_steps + 1, device)
     stream = torch.cuda.current_stream(device)
     # The timed steps rotate over R caches holding the same sequences (built from the same
@@ -848,7 +858,7 @@ def main():
         if dist:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = te.item()
-        e2e = {"value": args.batch / (e2e_ms / 1000.0), "unit": "tokens/s",
+        e2e = {"value": tok_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": int(inh[0].numel() * 2), "d2h_bytes_per_step": int(outh[0].numel() * 2),
                "ms_per_step": e2e_ms,
                "path": "PagedKVCache.step_host (nsnkv_paged_step_host, the C-ABI step with host buffers): pinned "
@@ -893,7 +903,7 @@ def main():
             cpu = cpu_bridge_rate()
         line = {
             "metric": "decode tokens/s (batched packed-KV decode, cfg2)",
-            "value": args.batch / (mean_step / 1000.0),
+            "value": tok_step / (mean_step / 1000.0),
             "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": mean_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -906,6 +916,7 @@ def main():
                              f"the rank's sequences ({rot_bytes / 1e6:.1f} MB of blocks each), so at least two L2 "
                              "sizes of other blocks stream in between two steps on one cache",
                        "rotation_caches_rank0": n_rot,
+                       "as_rank": args.as_rank,
                        "attn_bytes_per_step_rank0": bytes_attn, "attn_ms_rank0": mean_attn,
                        "attn_ms_max_over_ranks": mean_attn_max, "seqs_rank0": n_seq},
             "roofline": {"bound": "hbm",

@@ -1958,6 +1958,25 @@ static int s3_chunk_blocks(int64_t batch, int h, int32_t max_blocks, int32_t max
   if (ch > 32) ch = 32;
   const int64_t floor_ch = chunk_blocks_for(batch, h, max_blocks, max_tail);
   ch = std::max<int64_t>(ch, floor_ch);
+  if (batch > 1) {
+    // Under two waves the rounding of each sequence's last chunk decides: a sequence ends
+    // half a chunk past its blocks on average, so a grid sized for the average sequence can
+    // land just past a wave, whose last CTAs then run alone (8 cfg2 sequences, one rank of
+    // 8: 624-640 CTAs of 16 blocks for 592 slots).  Here the multiple of 4 from min(ch, 16)
+    // to 32 that minimises waves x (c + 2 blocks of start-up) wins, with the expected CTA
+    // count units x (avg / c + 1/2).  On B200: a rank of 8, 20 blocks 31.5-32.0 us against
+    // 37.0-38.8 at 16; a rank of 4, 20 blocks 51.7 us against 59.1 at 32.  From two waves
+    // up, later CTAs fill the slots as earlier ones end, and the chunk above stays.
+    const auto ctas = [&](int64_t c) { return (units * (2 * avg + c) + 2 * c - 1) / (2 * c); };
+    if (ctas(ch) < 2 * target) {
+      int64_t best = ch, best_cost = (ctas(ch) + target - 1) / target * (ch + 2);
+      for (int64_t c = std::max<int64_t>(std::min<int64_t>(ch, 16), (floor_ch + 3) / 4 * 4); c <= 32; c += 4) {
+        const int64_t cost = (ctas(c) + target - 1) / target * (c + 2);
+        if (cost < best_cost) best = c, best_cost = cost;
+      }
+      ch = best;
+    }
+  }
   if (batch == 1) {
     // One sequence: every CTA but the last of each head runs c blocks.  Candidates start at
     // about two CTAs per SM, at most 16 blocks (fewer, longer chunks cost fewer CTA starts
